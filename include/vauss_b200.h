@@ -1,0 +1,230 @@
+/*
+ * vauss_b200 — C ABI of the B200 (sm_100a) Gaussian-splat training step.
+ *
+ * Drop-in boundary for the reference trainer's GPU operators (voyager-so/vauss,
+ * Brush-derived Rust/CubeCL).  Every entry point names the reference trait
+ * method or kernel it replaces (paths relative to the reference project root).
+ *
+ * Conventions
+ *  - All tensor pointers are DEVICE pointers owned by the caller, in the
+ *    reference layouts: transforms [N,10] f32 = mean(3), quaternion (w,x,y,z)(4),
+ *    log-scale(3); sh_coeffs [N,(d+1)^2,3] f32 or f16; raw_opacities [N] f32;
+ *    images [H,W,4] f32 RGBA; ground truth [H,W] u32 packed RGBA8 (r low byte).
+ *  - A vs_ctx owns one device, one stream and a grow-only workspace.  A
+ *    vs_frame owns the per-render intermediates (projected splats, the sorted
+ *    intersection list, tile ranges) that the backward of that render reads.
+ *  - Calls enqueue work on the ctx stream and return without waiting, except
+ *    vs_render_forward, which reads the two projection counts back (the
+ *    reference's render-count readback, src/render.rs:590-597) to size the
+ *    intersection list exactly.
+ *  - Every call returns a vs_status; vs_ctx_last_error() describes the last
+ *    failure.  No call aborts the process.
+ */
+#ifndef VAUSS_B200_H
+#define VAUSS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VS_API __attribute__((visibility("default")))
+
+typedef enum vs_status {
+  VS_OK = 0,
+  VS_ERR_INVALID = 1,        /* bad argument (sizes, null pointers, degree) */
+  VS_ERR_CAPACITY = 2,       /* a size limit was exceeded (message gives the size) */
+  VS_ERR_CUDA = 3,           /* a CUDA runtime call failed */
+  VS_ERR_DEVICE_TIMEOUT = 4, /* a bounded device-side wait gave up */
+  VS_ERR_UNSUPPORTED = 5
+} vs_status;
+
+/* Pinhole view (crates/splat-train-render/src/camera.rs:12-97 + the
+ * ProjectUniforms of src/kernels/types.rs:53-82). */
+typedef struct vs_camera {
+  float viewmat[12]; /* world->camera 3x4, column-major: rotation columns, translation */
+  float fx, fy, cx, cy;
+  float cam_pos[3];  /* view-direction origin of the SH colour */
+  uint32_t img_w, img_h;
+} vs_camera;
+
+/* Render options (SplatOps::render arguments, crates/splat-train-render/src/lib.rs:53-115). */
+typedef struct vs_render_cfg {
+  int32_t mip;           /* SplatRenderMode::Mip: blur 0.1 + opacity compensation; else 0.3 */
+  int32_t sh_degree;     /* 0..3 */
+  int32_t sh_half;       /* sh_coeffs stored as IEEE binary16 */
+  int32_t has_min_scale; /* min_scale [N] is read (Mip-Splatting 3D floor) */
+  float log_scale_offset;
+  float bg[3];           /* background colour */
+} vs_render_cfg;
+
+typedef struct vs_render_counts {
+  uint32_t num_visible;
+  uint32_t num_tiles;
+  uint64_t num_intersections;
+} vs_render_counts;
+
+typedef struct vs_ctx vs_ctx;
+typedef struct vs_frame vs_frame;
+
+/* ---- context ------------------------------------------------------------ */
+VS_API vs_status vs_ctx_create(int device, vs_ctx** out);
+VS_API void vs_ctx_destroy(vs_ctx* ctx);
+/* Run subsequent work on `cuda_stream` (a cudaStream_t; NULL = legacy default). */
+VS_API vs_status vs_ctx_set_stream(vs_ctx* ctx, void* cuda_stream);
+VS_API const char* vs_ctx_last_error(const vs_ctx* ctx);
+/* Bytes of device workspace the ctx and its frames currently hold. */
+VS_API uint64_t vs_ctx_workspace_bytes(const vs_ctx* ctx);
+VS_API const char* vs_version(void);
+
+VS_API vs_status vs_frame_create(vs_ctx* ctx, vs_frame** out);
+VS_API void vs_frame_destroy(vs_frame* frame);
+
+/* Frame buffers exposed for inspection and for the backward/optimizer calls. */
+typedef enum vs_frame_field {
+  VS_FIELD_COMPACT_FROM_GLOBAL = 0, /* u32 [N]   compact id + 1, 0 = culled */
+  VS_FIELD_GLOBAL_FROM_COMPACT = 1, /* u32 [V]   */
+  VS_FIELD_DEPTHS = 2,              /* f32 [V]   view-space z, compact order */
+  VS_FIELD_TILE_COUNTS = 3,         /* u32 [V]   tiles hit, compact order */
+  VS_FIELD_PROJECTED = 4,           /* f32 [V,12] [x,y,c00,c01, c11,opac,r,g, b,gid,0,0] */
+  VS_FIELD_DEPTH_ORDER = 5,         /* u32 [V]   compact ids sorted by depth */
+  VS_FIELD_ISECT_TILE = 6,          /* u32 [I]   tile id of each sorted intersection */
+  VS_FIELD_ISECT_COMPACT = 7,       /* u32 [I]   compact id of each sorted intersection */
+  VS_FIELD_TILE_RANGES = 8,         /* u32 [T,2] [start,end) after binning */
+  VS_FIELD_TILE_USED_END = 9,       /* u32 [T]   one past the last intersection any pixel used */
+  VS_FIELD_OPACITIES = 10,          /* f32 [N]   floored sigmoid opacity (0 if culled early) */
+  VS_FIELD_MAX_RADIUS = 11          /* f32 [N]   screen radius (fraction of the image) */
+} vs_frame_field;
+VS_API vs_status vs_frame_buffer(vs_frame* frame, int32_t field, void** dev_ptr, uint64_t* count);
+VS_API vs_status vs_frame_counts(const vs_frame* frame, vs_render_counts* out);
+/* Copies up to max_bytes of a frame buffer into caller device memory (stream-ordered). */
+VS_API vs_status vs_frame_copy(vs_frame* frame, int32_t field, void* dst_device, uint64_t max_bytes);
+
+/* ---- render forward -------------------------------------------------------
+ * Replaces SplatOps::render for training passes (crates/splat-train-render/
+ * src/render.rs:315-349 -> render_cube :401-979): projection + SH colour
+ * (project_forward.rs, project_visible.rs), depth sort, intersection emission,
+ * stable tile sort and tile ranges (map_gaussians.rs, splat-train-sort,
+ * get_tile_offset.rs), front-to-back compositing (kernels/rasterize.rs with
+ * bwd_info).  Writes out_img [H,W,4] and visible [N] (1.0 where a splat
+ * contributed to a pixel, else 0.0); counts_out may be NULL. */
+VS_API vs_status vs_render_forward(vs_ctx* ctx, vs_frame* frame, const vs_camera* cam, const vs_render_cfg* cfg,
+                                   uint32_t num_splats, const float* transforms, const void* sh_coeffs,
+                                   const float* raw_opacities, const float* min_scale, float* out_img,
+                                   float* visible, vs_render_counts* counts_out);
+
+/* ---- loss ------------------------------------------------------------------
+ * Replaces LossOps::image_loss_forward_train + image_loss_backward_coeffs
+ * (crates/splat-train-loss/src/lib.rs:238-469, :821-1028) fused in one pass:
+ * per-pixel loss (l1_w*|p-g| + ssim_w*SSIM, 11x11 Gaussian window sigma 1.5,
+ * zero padding), weighted per-16x16-tile partial sums partials [3, tiles]
+ * (weight 1/(3HW)), the total into *loss_dev (device f32, may be NULL), and
+ * d(total)/d(pred) into dl_dpred [H,W,4] (alpha channel 0; may be NULL).
+ * The reference training objective is l1_w = 1-w, ssim_w = -w (lib.rs:1227-1257). */
+VS_API vs_status vs_loss(vs_ctx* ctx, uint32_t h, uint32_t w, const float* pred, const uint32_t* gt_packed,
+                         float l1_w, float ssim_w, float* partials, float* loss_dev, float* dl_dpred);
+
+/* ---- render backward -------------------------------------------------------
+ * Replaces SplatBwdOps::rasterize_bwd (src/bwd/render_bwd.rs:27-155 ->
+ * rasterize_backwards_planes.rs): per-splat gradients v_combined [V,10] =
+ * [xy(2), conic(3), rgb(3), alpha, refine] in compact order (zeroed here). */
+VS_API vs_status vs_rasterize_backward(vs_ctx* ctx, vs_frame* frame, const float* out_img, const float* v_output,
+                                       float* v_combined);
+
+/* ---- optimizer, reference mode ------------------------------------------- */
+typedef struct vs_adam_cfg {
+  float beta1, beta2, inv1, inv2, epsilon; /* inv1/inv2 = 1/(1-beta^t) */
+  float lr_opac, opac_reg;
+  uint32_t round_seed; /* stochastic-rounding stream (the step count) */
+} vs_adam_cfg;
+
+/* Replaces ProjectUpdateOps::project_update (src/bwd/project_update.rs:84-224,
+ * kernels/project_update.rs:36-178): projection VJP fused with Adam on packed
+ * 16/16 moments w_t [N,10], w_o [N] (geo_moments.rs).  lr_scale is a HOST
+ * array of 10 per-column learning rates.  Writes color_dir [N+1,6] (row 0
+ * zero), v_refine [N], grad_sq [N].  If variance != NULL the SH reduced second
+ * moment [N] is also stepped here (crates/splat-train/src/optim.rs:454-469):
+ * visible rows v = beta2*v + (1-beta2)*grad_sq, culled rows kept, or
+ * v = (1-beta2)*grad_sq on the first step. */
+VS_API vs_status vs_project_update(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
+                                   float* transforms, const void* sh_coeffs, float* raw_opacities,
+                                   const float* min_scale, const float* v_combined, uint32_t* w_t,
+                                   const float* lr_scale, uint32_t* w_o, const vs_adam_cfg* adam, float* color_dir,
+                                   float* v_refine, float* grad_sq, float* variance, int32_t first_step);
+
+/* Replaces QuantMomentOps::step_moment on the colour path
+ * (crates/splat-train/src/quant_kernels.rs:277-376, step_kernel_w4 :597-714):
+ * f16 SH coefficients [N*row_width], int8 first moment in 128-value blocks
+ * (codes [blocks*32] u32, scales [blocks] f32), reduced second moment
+ * variance [N]; lazy on culled rows (grad_rows == 0).  lr_scale is a HOST
+ * array of row_width learning-rate factors. */
+VS_API vs_status vs_sh_step(vs_ctx* ctx, uint32_t num_splats, uint32_t row_width, uint16_t* sh_f16,
+                            const float* color_dir, const uint32_t* grad_rows, uint32_t* codes, float* scales,
+                            const float* variance, const float* lr_scale, float beta, float factor, float inv1,
+                            float inv2, float epsilon, float lr, uint32_t round_seed);
+
+/* ---- optimizer, 8-bit m+v mode (the benchmark configuration) -------------- */
+typedef struct vs_q8_tensor { /* one parameter tensor's moments */
+  uint8_t* m_codes;           /* [count] +128-biased signed codes */
+  uint8_t* v_codes;           /* [count] sqrt(v) codes */
+  float* m_scales;            /* [ceil(count/256)] absmax|m|/127 */
+  float* v_scales;            /* [ceil(count/256)] absmax sqrt(v)/255 */
+} vs_q8_tensor;
+
+typedef struct vs_q8_cfg {
+  float beta1, beta2, inv1, inv2, epsilon;
+  float lr_transforms[10]; /* per-column learning rates */
+  float lr_sh_dc, lr_sh_rest; /* coefficient 0 and coefficients 1.. */
+  float lr_opac, opac_reg;
+  uint32_t seed;              /* stochastic rounding stream (the step count) */
+  /* housekeeping folded into the step (crates/splat-train/src/housekeep.rs) */
+  float noise_scale, noise_limit;
+  uint32_t noise_seed;
+} vs_q8_cfg;
+
+/* Single-view step: projection VJP from v_combined + Adam with 8-bit m and v
+ * (blocks of 256, fp32 absmax scales, stochastic rounding) on transforms,
+ * sh_coeffs (f32) and raw_opacities, plus the refine statistics
+ * (refine_norm = max, vis_count += visible, max_screen = max) and the
+ * low-opacity mean noise, in one kernel.  stats pointers may be NULL. */
+VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
+                            float* transforms, float* sh_coeffs, float* raw_opacities, const float* v_combined,
+                            vs_q8_tensor mom_t, vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8,
+                            const float* visible, float* refine_norm, float* vis_count, float* max_screen);
+
+/* Dense projection VJP (the multi-view path, src/bwd/kernels/
+ * project_backwards.rs:282-424 + the dense gather of burn_glue.rs:363-395):
+ * ACCUMULATES this frame's gradients into grads [N, 10 + 3(d+1)^2 + 1]
+ * (transforms | sh | raw opacity) and refine [N]. */
+VS_API vs_status vs_vjp_dense(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
+                              const float* transforms, const void* sh_coeffs, const float* raw_opacities,
+                              const float* min_scale, const float* v_combined, float* grads, float* refine);
+
+/* Adam (8-bit m+v) from dense gradients grads [N, width] (after the
+ * cross-GPU all-reduce).  visible may be NULL (no noise). */
+VS_API vs_status vs_adam_q8_dense(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, float* transforms,
+                                  float* sh_coeffs, float* raw_opacities, const float* grads, vs_q8_tensor mom_t,
+                                  vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8,
+                                  const float* opacities, const float* visible);
+
+/* ---- housekeeping (crates/splat-train/src/housekeep.rs:15-39) ------------- */
+VS_API vs_status vs_gather_stats(vs_ctx* ctx, uint32_t n, float* refine_norm, float* vis_count, float* max_screen,
+                                 const float* refine_weight, const float* visible, const float* radius);
+VS_API vs_status vs_noise_means(vs_ctx* ctx, uint32_t n, float* transforms, const float* opacities,
+                                const float* visible, float scale, float limit, uint32_t seed);
+
+/* ---- building blocks exposed for tests ------------------------------------ */
+/* Stable LSD radix sort of (key, value) u32 pairs on bits [0, key_bits). */
+VS_API vs_status vs_radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* values, uint32_t count,
+                                     uint32_t key_bits);
+/* Inclusive prefix sum of u32 in place; the total (u64) to *total_dev if non-NULL. */
+VS_API vs_status vs_scan_inclusive(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev);
+/* Elementwise vs_expf / vs_logf (the shared deterministic functions). */
+VS_API vs_status vs_math_probe(vs_ctx* ctx, int32_t which, const float* x, float* y, uint32_t n);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VAUSS_B200_H */

@@ -1,0 +1,648 @@
+// Optimizer kernels.
+//
+// Reference mode (drop-in parity with the reference trainer):
+//   project_update_kernel -- projection VJP fused with Adam on packed 16/16
+//     moments (crates/splat-train-render/src/bwd/kernels/project_update.rs:
+//     36-178, geo_moments.rs:26-96), plus the SH reduced-variance update
+//     (crates/splat-train/src/optim.rs:454-469);
+//   sh_step_kernel -- f16 SH Adam with an 8-bit first moment in 128-value
+//     blocks, one warp per block (crates/splat-train/src/quant_kernels.rs:
+//     597-714).
+// Q8 mode (the benchmark's optimizer: 8-bit m AND v, 256-value blocks):
+//   q8_kernel<false> -- single view: VJP + Adam on all 59 parameters +
+//     refine statistics + mean noise, one CTA per 256 splats;
+//   q8_kernel<true>  -- the same Adam from an all-reduced dense gradient;
+//   vjp_dense_kernel -- accumulates one view's dense gradient rows.
+#include "vjp.cuh"
+#include "vs_internal.cuh"
+
+namespace {
+
+using namespace vs;
+
+// ---- packed geometry moments (geo_moments.rs:26-96) ----
+constexpr float GEO_U_MAX = 8.0f, GEO_U_CODES = 32767.0f;
+constexpr float GEO_U_STEP = GEO_U_MAX / GEO_U_CODES, GEO_U_PER_UNIT = GEO_U_CODES / GEO_U_MAX;
+constexpr float GEO_L_MAX = 64.0f, GEO_L_CODES = 65535.0f;
+constexpr float GEO_L_STEP = GEO_L_MAX / GEO_L_CODES, GEO_L_PER_UNIT = GEO_L_CODES / GEO_L_MAX;
+
+__device__ __forceinline__ uint32_t pack_geo(float m, float v, float eps, float rl, float ru) {
+  const float l = vs_logf(1.0f + sqrtf(fmaxf(v, 0.0f)) / eps) * GEO_L_PER_UNIT;
+  const float l_code = floorf(clampf(l + rl, 0.0f, GEO_L_CODES));
+  const float scale = eps * vs_expf(l_code * GEO_L_STEP);
+  const float uu = fabsf(m) / scale * GEO_U_PER_UNIT;
+  const uint32_t u_code = (uint32_t)floorf(clampf(uu + ru, 0.0f, GEO_U_CODES));
+  const uint32_t sign = m < 0.0f ? 0x8000u : 0u;
+  return ((uint32_t)l_code << 16) | sign | u_code;
+}
+
+__device__ __forceinline__ void adam_packed(float* params, uint32_t* words, size_t index, float g, float lr, float b1,
+                                            float b2, float inv1, float inv2, float eps, uint32_t seed) {
+  const uint32_t word = words[index];
+  const float growth = vs_expf((float)(word >> 16) * GEO_L_STEP);
+  const float mag = (float)(word & 0x7fffu) * GEO_U_STEP;
+  const float un = (word & 0x8000u) ? -mag : mag;
+  const float root = eps * (growth - 1.0f);
+  const float m1 = un * (eps * growth) * b1 + g * (1.0f - b1);
+  const float v1 = root * root * b2 + g * g * (1.0f - b2);
+  const float step = (m1 * inv1) / (sqrtf(v1 * inv2) + eps);
+  params[index] = params[index] - step * lr;
+  const uint32_t hsh = vs_mix_hash((uint32_t)index, seed);
+  words[index] = pack_geo(m1, v1, eps, (float)(hsh >> 16) / 65536.0f, (float)(hsh & 0xffffu) / 65536.0f);
+}
+
+struct AdamArgs {
+  float b1, b2, inv1, inv2, eps, lr_opac, opac_reg;
+  uint32_t seed;
+  float lr_scale[10];
+};
+
+__global__ void __launch_bounds__(256) project_update_kernel(
+    Uniforms u, uint32_t n, float* __restrict__ transforms, const void* __restrict__ sh, float* __restrict__ raw_opac,
+    const float* __restrict__ min_scale, const uint32_t* __restrict__ compact_from_global,
+    const float* __restrict__ v_combined, uint32_t* __restrict__ w_t, uint32_t* __restrict__ w_o, AdamArgs a,
+    float* __restrict__ color_dir, float* __restrict__ v_refine, float* __restrict__ grad_sq,
+    float* __restrict__ variance, int32_t first_step) {
+  const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n) return;
+  if (g == 0) {
+#pragma unroll
+    for (int k = 0; k < 6; ++k) color_dir[k] = 0.0f;
+  }
+  float gr[10];
+#pragma unroll
+  for (int k = 0; k < 10; ++k) gr[k] = 0.0f;
+  float g_opac = 0.0f, refine = 0.0f, gsq = 0.0f;
+  const uint32_t row = compact_from_global[g];
+  float* t = transforms + (size_t)g * 10;
+  if (row > 0) {
+    const float* rg = v_combined + (size_t)(row - 1) * 10;
+    float rr[10];
+    bool any = false;
+#pragma unroll
+    for (int k = 0; k < 10; ++k) {
+      rr[k] = rg[k];
+      any = any || rr[k] != 0.0f;
+    }
+    float* cd = color_dir + (size_t)row * 6;
+    if (any) {
+      float tt[10];
+#pragma unroll
+      for (int k = 0; k < 10; ++k) tt[k] = t[k];
+      const VjpOut o = splat_vjp(tt, raw_opac[g], sh, min_scale, g, rr, u);
+      cd[0] = rr[5]; cd[1] = rr[6]; cd[2] = rr[7];
+      cd[3] = o.dir.x; cd[4] = o.dir.y; cd[5] = o.dir.z;
+      gr[0] = o.v_mean.x; gr[1] = o.v_mean.y; gr[2] = o.v_mean.z;
+      gr[3] = o.v_q.w; gr[4] = o.v_q.x; gr[5] = o.v_q.y; gr[6] = o.v_q.z;
+      gr[7] = o.v_scale.x; gr[8] = o.v_scale.y; gr[9] = o.v_scale.z;
+      g_opac = o.v_raw;
+      refine = clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
+      const float c0 = SH_C0 * rr[5], c1 = SH_C0 * rr[6], c2 = SH_C0 * rr[7];
+      gsq = (c0 * c0 + c1 * c1 + c2 * c2) / 3.0f;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 6; ++k) cd[k] = 0.0f;
+    }
+  }
+  v_refine[g] = refine;
+  grad_sq[g] = gsq;
+  if (variance) {
+    if (first_step) variance[g] = gsq * (1.0f - a.b2);
+    else if (row > 0) variance[g] = variance[g] * a.b2 + gsq * (1.0f - a.b2);
+  }
+  const float o = 1.0f / (1.0f + vs_expf(-raw_opac[g]));
+  g_opac += a.opac_reg * o * (1.0f - o);
+  const uint32_t seed_t = a.seed ^ (10u << 24), seed_o = a.seed ^ (1u << 24);
+#pragma unroll
+  for (int k = 0; k < 10; ++k)
+    adam_packed(transforms, w_t, (size_t)g * 10 + k, gr[k], a.lr_scale[k], a.b1, a.b2, a.inv1, a.inv2, a.eps, seed_t);
+  adam_packed(raw_opac, w_o, g, g_opac, a.lr_opac, a.b1, a.b2, a.inv1, a.inv2, a.eps, seed_o);
+}
+
+__device__ __forceinline__ float sh_basis_one(uint32_t k, float x, float y, float z) {
+  float b[16];
+  sh_basis_all(x, y, z, b);
+  float r = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r = (k == (uint32_t)i) ? b[i] : r;
+  return r;
+}
+
+// Stochastic rounding to f16 storage (quant_kernels.rs:860-890).
+__device__ __forceinline__ float stochastic_half(float value, uint32_t index, uint32_t step) {
+  const float mag = fabsf(value);
+  float result = value;
+  if (mag <= 65504.0f) {
+    float lower, upper;
+    if (mag < 0.00006103515625f) {
+      lower = floorf(mag * 16777216.0f) / 16777216.0f;
+      upper = lower + 0.000000059604644775390625f;
+    } else {
+      const uint32_t bits = __float_as_uint(mag) & 0xffffe000u;
+      lower = __uint_as_float(bits);
+      upper = __uint_as_float(bits + 8192u);
+    }
+    const uint32_t hsh = vs_mix_hash(index, step);
+    const float uni = (float)(hsh >> 8) / 16777216.0f;
+    const float prob = (mag - lower) / (upper - lower);
+    result = uni < prob ? upper : lower;
+    if (value < 0.0f) result = -result;
+  }
+  return result;
+}
+
+struct ShStepArgs {
+  float beta, factor, inv1, inv2, eps, lr;
+  uint32_t seed;
+};
+
+// One warp per 128-value block, one 4-value code word per lane.
+__global__ void __launch_bounds__(128) sh_step_kernel(uint32_t count, uint32_t row_width, uint16_t* __restrict__ params,
+                                                      const float* __restrict__ color_dir,
+                                                      const uint32_t* __restrict__ grad_rows,
+                                                      uint32_t* __restrict__ codes, float* __restrict__ scales,
+                                                      const float* __restrict__ variance,
+                                                      const float* __restrict__ lr_scale, uint32_t nblocks,
+                                                      ShStepArgs a) {
+  const uint32_t lane = threadIdx.x & 31u;
+  const uint32_t block = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (block >= nblocks) return;
+  const uint32_t word = block * 32 + lane;
+  bool any = false;
+#pragma unroll
+  for (uint32_t j = 0; j < 4; ++j) {
+    const uint32_t i = word * 4 + j;
+    if (i < count) any = any || grad_rows[i / row_width] != 0u;
+  }
+  if (!__any_sync(0xffffffffu, any)) return;
+  const uint32_t old = codes[word];
+  const float old_scale = scales[block];
+  float m[4];
+#pragma unroll
+  for (uint32_t j = 0; j < 4; ++j) {
+    const uint32_t code = (old >> (j * 8)) & 255u;
+    m[j] = (word * 4 + j < count) ? ((float)code - 128.0f) * old_scale : 0.0f;
+  }
+#pragma unroll
+  for (uint32_t j = 0; j < 4; ++j) {
+    const uint32_t i = word * 4 + j;
+    if (i >= count) continue;
+    const uint32_t row = i / row_width, col = i % row_width;
+    const uint32_t gr = grad_rows[row];
+    if (gr == 0u) continue;
+    const float* cd = color_dir + (size_t)gr * 6;
+    const float basis = sh_basis_one(col / 3, cd[3], cd[4], cd[5]);
+    const float gg = basis * cd[col % 3];
+    const float moment = m[j] * a.beta + gg * a.factor;
+    const float denom = sqrtf(variance[row] * a.inv2) + a.eps;
+    const float delta = (moment * a.inv1 / denom) * (lr_scale[col] * a.lr);
+    float updated = vs_f16_to_f32(params[i]) - delta;
+    updated = stochastic_half(updated, i, a.seed);
+    params[i] = vs_f32_to_f16(updated);
+    m[j] = moment;
+  }
+  float local = fmaxf(fmaxf(fabsf(m[0]), fabsf(m[1])), fmaxf(fabsf(m[2]), fabsf(m[3])));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) local = fmaxf(local, __shfl_xor_sync(0xffffffffu, local, off));
+  const float scale = local / 127.0f;
+  if (lane == 0) scales[block] = scale;
+  uint32_t packed = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < 4; ++j) {
+    uint32_t code = 128u;
+    if (scale > 0.0f) code = (uint32_t)(rintf(clampf(m[j] / scale, -127.0f, 127.0f)) + 128.0f);
+    packed |= code << (j * 8);
+  }
+  codes[word] = packed;
+}
+
+// ---- dense VJP ----
+__global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t n, const float* __restrict__ transforms,
+                                                        const void* __restrict__ sh, const float* __restrict__ raw_opac,
+                                                        const float* __restrict__ min_scale,
+                                                        const uint32_t* __restrict__ compact_from_global,
+                                                        const float* __restrict__ v_combined,
+                                                        float* __restrict__ grads, float* __restrict__ refine) {
+  const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n) return;
+  const uint32_t row = compact_from_global[g];
+  if (row == 0) return;
+  const float* rg = v_combined + (size_t)(row - 1) * 10;
+  float rr[10];
+  bool any = false;
+#pragma unroll
+  for (int k = 0; k < 10; ++k) {
+    rr[k] = rg[k];
+    any = any || rr[k] != 0.0f;
+  }
+  if (!any) return;
+  const int nc = (u.sh_degree + 1) * (u.sh_degree + 1);
+  const int width = 10 + 3 * nc + 1;
+  float tt[10];
+#pragma unroll
+  for (int k = 0; k < 10; ++k) tt[k] = transforms[(size_t)g * 10 + k];
+  const VjpOut o = splat_vjp(tt, raw_opac[g], sh, min_scale, g, rr, u);
+  float* d = grads + (size_t)g * width;
+  const float gv[10] = {o.v_mean.x, o.v_mean.y, o.v_mean.z, o.v_q.w, o.v_q.x, o.v_q.y, o.v_q.z,
+                        o.v_scale.x, o.v_scale.y, o.v_scale.z};
+#pragma unroll
+  for (int k = 0; k < 10; ++k) d[k] += gv[k];
+  float b[16];
+  sh_basis_all(o.dir.x, o.dir.y, o.dir.z, b);
+  for (int k = 0; k < nc; ++k) {
+#pragma unroll
+    for (int c = 0; c < 3; ++c) d[10 + k * 3 + c] += rr[5 + c] * b[k];
+  }
+  d[width - 1] += o.v_raw;
+  refine[g] += clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
+}
+
+// ---- Q8 Adam ----
+struct Q8T {
+  uint8_t* mc;
+  uint8_t* vc;
+  float* ms;
+  float* vs;
+};
+
+struct Q8Args {
+  float b1, b2, inv1, inv2, eps;
+  float lr_t[10];
+  float lr_dc, lr_rest, lr_opac, opac_reg;
+  uint32_t seed;
+  float noise_scale, noise_limit;
+  uint32_t noise_seed;
+};
+
+constexpr uint32_t Q8_SPLATS = 256;
+constexpr uint32_t Q8_WARPS = 8;
+// Stochastic-rounding stream salts per tensor (the reference separates its
+// transforms and opacity streams the same way, project_update.rs:163-166).
+constexpr uint32_t SALT_T = 10u << 24, SALT_SH = 48u << 24, SALT_O = 1u << 24;
+
+__device__ __forceinline__ float hash_uniform(uint32_t key, uint32_t seed) {
+  const uint32_t h = vs_mix_hash(key, seed);
+  return (float)((h >> 8) + 1u) / 16777216.0f;
+}
+
+// Noise on the mean (crates/splat-train/src/housekeep.rs:134-160).
+__device__ __forceinline__ void mean_noise(uint32_t i, float opac, float vis, float scale, float limit, uint32_t seed,
+                                           float* nx, float* ny, float* nz) {
+  *nx = *ny = *nz = 0.0f;
+  const float om = 1.0f - opac;
+  const float pw = om > 0.0f ? vs_expf(150.0f * vs_logf(om)) : 0.0f;
+  const float gate = clampf(pw, 0.0f, 1.0f) * vis;
+  if (gate > 0.0f) {
+    const float w = gate * scale;
+    const uint32_t base = i * 4u;
+    const float r1 = sqrtf(-2.0f * vs_logf(hash_uniform(base, seed)));
+    const float a1 = 6.2831855f * hash_uniform(base + 1u, seed);
+    const float r2 = sqrtf(-2.0f * vs_logf(hash_uniform(base + 2u, seed)));
+    const float a2 = 6.2831855f * hash_uniform(base + 3u, seed);
+    float s1, c1, s2, c2;
+    vs_sincosf(a1, &s1, &c1);
+    vs_sincosf(a2, &s2, &c2);
+    *nx = clampf(r1 * c1 * w, -limit, limit);
+    *ny = clampf(r1 * s1 * w, -limit, limit);
+    *nz = clampf(r2 * c2 * w, -limit, limit);
+  }
+}
+
+template <bool kDense>
+__global__ void __launch_bounds__(Q8_SPLATS) q8_kernel(
+    Uniforms u, uint32_t n, float* __restrict__ transforms, float* __restrict__ sh, float* __restrict__ raw_opac,
+    const float* __restrict__ min_scale, const uint32_t* __restrict__ compact_from_global,
+    const float* __restrict__ v_combined, const float* __restrict__ grads, Q8T mt, Q8T msh, Q8T mo, Q8Args a,
+    const float* __restrict__ opacities, const float* __restrict__ visible, const float* __restrict__ max_radius,
+    float* __restrict__ refine_norm, float* __restrict__ vis_count, float* __restrict__ max_screen) {
+  __shared__ float s_gt[Q8_SPLATS * 10];
+  __shared__ float s_go[Q8_SPLATS];
+  __shared__ float s_vc[Q8_SPLATS * 3];
+  __shared__ float s_bas[Q8_SPLATS * 16];
+  __shared__ float s_noise[Q8_SPLATS * 3];
+
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const uint32_t base = blockIdx.x * Q8_SPLATS;
+  const int nc = (u.sh_degree + 1) * (u.sh_degree + 1);
+  const uint32_t wsh = 3u * (uint32_t)nc;
+  const uint32_t width = 10u + wsh + 1u;
+
+  // ---- phase 1: one splat per thread ----
+  {
+    const uint32_t g = base + tid;
+    float gr[10];
+#pragma unroll
+    for (int k = 0; k < 10; ++k) gr[k] = 0.0f;
+    float go = 0.0f, vc0 = 0.0f, vc1 = 0.0f, vc2 = 0.0f, dx = 0.0f, dy = 0.0f, dz = 1.0f;
+    float nx = 0.0f, ny = 0.0f, nz = 0.0f;
+    if (g < n) {
+      if (kDense) {
+        const float* d = grads + (size_t)g * width;
+#pragma unroll
+        for (int k = 0; k < 10; ++k) gr[k] = d[k];
+        go = d[width - 1];
+      } else {
+        const uint32_t row = compact_from_global[g];
+        float refine = 0.0f;
+        if (row > 0) {
+          const float* rg = v_combined + (size_t)(row - 1) * 10;
+          float rr[10];
+          bool any = false;
+#pragma unroll
+          for (int k = 0; k < 10; ++k) {
+            rr[k] = rg[k];
+            any = any || rr[k] != 0.0f;
+          }
+          if (any) {
+            float tt[10];
+#pragma unroll
+            for (int k = 0; k < 10; ++k) tt[k] = transforms[(size_t)g * 10 + k];
+            const VjpOut o = splat_vjp(tt, raw_opac[g], sh, min_scale, g, rr, u);
+            gr[0] = o.v_mean.x; gr[1] = o.v_mean.y; gr[2] = o.v_mean.z;
+            gr[3] = o.v_q.w; gr[4] = o.v_q.x; gr[5] = o.v_q.y; gr[6] = o.v_q.z;
+            gr[7] = o.v_scale.x; gr[8] = o.v_scale.y; gr[9] = o.v_scale.z;
+            go = o.v_raw;
+            vc0 = rr[5]; vc1 = rr[6]; vc2 = rr[7];
+            dx = o.dir.x; dy = o.dir.y; dz = o.dir.z;
+            refine = clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
+          }
+        }
+        if (refine_norm) refine_norm[g] = fmaxf(refine_norm[g], refine);
+        if (vis_count) vis_count[g] += visible[g];
+        if (max_screen) max_screen[g] = fmaxf(max_screen[g], max_radius[g]);
+      }
+      if (a.opac_reg != 0.0f) {
+        const float o = 1.0f / (1.0f + vs_expf(-raw_opac[g]));
+        go = go + a.opac_reg * o * (1.0f - o);
+      }
+      if (opacities && visible && a.noise_scale != 0.0f)
+        mean_noise(g, opacities[g], visible[g], a.noise_scale, a.noise_limit, a.noise_seed, &nx, &ny, &nz);
+    }
+#pragma unroll
+    for (int k = 0; k < 10; ++k) s_gt[tid * 10 + k] = gr[k];
+    s_go[tid] = go;
+    s_vc[tid * 3 + 0] = vc0;
+    s_vc[tid * 3 + 1] = vc1;
+    s_vc[tid * 3 + 2] = vc2;
+    if (!kDense) {
+      float b[16];
+      sh_basis_all(dx, dy, dz, b);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) s_bas[tid * 16 + k] = b[k];
+    }
+    s_noise[tid * 3 + 0] = nx;
+    s_noise[tid * 3 + 1] = ny;
+    s_noise[tid * 3 + 2] = nz;
+  }
+  __syncthreads();
+
+  // ---- phase 2: one warp per 256-value quantization block ----
+  const uint32_t splats_here = min(Q8_SPLATS, n - base);
+  const uint32_t nb_t = div_up(splats_here * 10u, 256u);
+  const uint32_t nb_sh = div_up(splats_here * wsh, 256u);
+  const uint32_t nb_o = 1u;
+  const uint32_t total_blocks = nb_t + nb_sh + nb_o;
+  for (uint32_t job = warp; job < total_blocks; job += Q8_WARPS) {
+    uint32_t tensor, jb, w;
+    if (job < nb_t) { tensor = 0; jb = job; w = 10u; }
+    else if (job < nb_t + nb_sh) { tensor = 1; jb = job - nb_t; w = wsh; }
+    else { tensor = 2; jb = 0; w = 1u; }
+    float* params = tensor == 0 ? transforms : (tensor == 1 ? sh : raw_opac);
+    const Q8T q = tensor == 0 ? mt : (tensor == 1 ? msh : mo);
+    const uint32_t salt = tensor == 0 ? SALT_T : (tensor == 1 ? SALT_SH : SALT_O);
+    const size_t t_base = (size_t)base * w;        // first value of this CTA in the tensor
+    const size_t count = (size_t)n * w;            // tensor size
+    const size_t v0 = t_base + (size_t)jb * 256u;  // first value of this block
+    const size_t blk = v0 / 256u;
+    const float ms = q.ms[blk], vsc = q.vs[blk];
+    float m1[8], r1[8];
+    float am = 0.0f, ar = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const size_t i = v0 + (size_t)j * 32 + lane;
+      m1[j] = 0.0f;
+      r1[j] = 0.0f;
+      if (i >= count) continue;
+      const uint32_t s = (uint32_t)(i / w) - base;
+      const uint32_t col = (uint32_t)(i % w);
+      float g, lr;
+      if (tensor == 0) {
+        g = s_gt[s * 10 + col];
+        lr = a.lr_t[col];
+      } else if (tensor == 1) {
+        g = kDense ? grads[(size_t)(base + s) * width + 10 + col] : s_vc[s * 3 + col % 3] * s_bas[s * 16 + col / 3];
+        lr = (col / 3 == 0) ? a.lr_dc : a.lr_rest;
+      } else {
+        g = s_go[s];
+        lr = a.lr_opac;
+      }
+      const float m0 = ((float)q.mc[i] - 128.0f) * ms;
+      const float r0 = (float)q.vc[i] * vsc;
+      const float m = m0 * a.b1 + g * (1.0f - a.b1);
+      const float v = r0 * r0 * a.b2 + g * g * (1.0f - a.b2);
+      const float mh = m * a.inv1;
+      const float denom = fmaxf(sqrtf(v * a.inv2) + a.eps, fabsf(mh) * 0.125f);
+      float p = params[i] - (mh / denom) * lr;
+      if (tensor == 0 && col < 3) p = p + s_noise[s * 3 + col];
+      params[i] = p;
+      m1[j] = m;
+      r1[j] = sqrtf(v);
+      am = fmaxf(am, fabsf(m));
+      ar = fmaxf(ar, r1[j]);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+      ar = fmaxf(ar, __shfl_xor_sync(0xffffffffu, ar, off));
+    }
+    const float nms = am / 127.0f, nvs = ar / 255.0f;
+    if (lane == 0) {
+      q.ms[blk] = nms;
+      q.vs[blk] = nvs;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const size_t i = v0 + (size_t)j * 32 + lane;
+      if (i >= count) continue;
+      const uint32_t hsh = vs_mix_hash((uint32_t)i, a.seed ^ salt);
+      const float u1 = (float)(hsh >> 16) / 65536.0f, u2 = (float)(hsh & 0xffffu) / 65536.0f;
+      float qm = 0.0f, qr = 0.0f;
+      if (nms > 0.0f) qm = clampf(floorf(m1[j] / nms + u1), -127.0f, 127.0f);
+      if (nvs > 0.0f) qr = clampf(floorf(r1[j] / nvs + u2), 0.0f, 255.0f);
+      q.mc[i] = (uint8_t)((int32_t)qm + 128);
+      q.vc[i] = (uint8_t)qr;
+    }
+  }
+}
+
+__global__ void stats_kernel(uint32_t n, float* norm, float* vis, float* screen, const float* weight,
+                             const float* visible, const float* radius) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    norm[i] = fmaxf(norm[i], weight[i]);
+    vis[i] += visible[i];
+    screen[i] = fmaxf(screen[i], radius[i]);
+  }
+}
+
+__global__ void noise_kernel(uint32_t n, float* transforms, const float* opacities, const float* visible, float scale,
+                             float limit, uint32_t seed) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float nx, ny, nz;
+  mean_noise(i, opacities[i], visible[i], scale, limit, seed, &nx, &ny, &nz);
+  if (nx != 0.0f || ny != 0.0f || nz != 0.0f) {
+    float* t = transforms + (size_t)i * 10;
+    t[0] += nx;
+    t[1] += ny;
+    t[2] += nz;
+  }
+}
+
+Q8T to_q8(const vs_q8_tensor& t) { return {t.m_codes, t.v_codes, t.m_scales, t.v_scales}; }
+
+Q8Args to_args(const vs_q8_cfg& c) {
+  Q8Args a;
+  a.b1 = c.beta1; a.b2 = c.beta2; a.inv1 = c.inv1; a.inv2 = c.inv2; a.eps = c.epsilon;
+  for (int k = 0; k < 10; ++k) a.lr_t[k] = c.lr_transforms[k];
+  a.lr_dc = c.lr_sh_dc; a.lr_rest = c.lr_sh_rest; a.lr_opac = c.lr_opac; a.opac_reg = c.opac_reg;
+  a.seed = c.seed;
+  a.noise_scale = c.noise_scale; a.noise_limit = c.noise_limit; a.noise_seed = c.noise_seed;
+  return a;
+}
+
+bool q8_valid(const vs_q8_tensor& t) { return t.m_codes && t.v_codes && t.m_scales && t.v_scales; }
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+extern "C" {
+
+VS_API vs_status vs_project_update(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
+                                   float* transforms, const void* sh_coeffs, float* raw_opacities,
+                                   const float* min_scale, const float* v_combined, uint32_t* w_t,
+                                   const float* lr_scale, uint32_t* w_o, const vs_adam_cfg* adam, float* color_dir,
+                                   float* v_refine, float* grad_sq, float* variance, int32_t first_step) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!frame || !frame->rendered || !cfg || !adam || !lr_scale)
+    return vs_fail(ctx, VS_ERR_INVALID, "project_update: missing frame/config");
+  if (num_splats != frame->n) return vs_fail(ctx, VS_ERR_INVALID, "project_update: %u splats, frame has %u", num_splats, frame->n);
+  if (!transforms || !sh_coeffs || !raw_opacities || !w_t || !w_o || !color_dir || !v_refine || !grad_sq ||
+      (frame->v && !v_combined))
+    return vs_fail(ctx, VS_ERR_INVALID, "project_update: null buffer");
+  if (num_splats == 0) return VS_OK;
+  AdamArgs a;
+  a.b1 = adam->beta1; a.b2 = adam->beta2; a.inv1 = adam->inv1; a.inv2 = adam->inv2; a.eps = adam->epsilon;
+  a.lr_opac = adam->lr_opac; a.opac_reg = adam->opac_reg; a.seed = adam->round_seed;
+  for (int k = 0; k < 10; ++k) a.lr_scale[k] = lr_scale[k];
+  vs::Uniforms u = frame->u;
+  u.sh_half = cfg->sh_half;
+  project_update_kernel<<<vs::div_up(num_splats, 256), 256, 0, ctx->stream>>>(
+      u, num_splats, transforms, sh_coeffs, raw_opacities, min_scale,
+      (const uint32_t*)frame->compact_from_global.ptr, v_combined, w_t, w_o, a, color_dir, v_refine, grad_sq, variance,
+      first_step);
+  return vs_cuda(ctx, cudaGetLastError(), "project_update launch");
+}
+
+VS_API vs_status vs_sh_step(vs_ctx* ctx, uint32_t num_splats, uint32_t row_width, uint16_t* sh_f16,
+                            const float* color_dir, const uint32_t* grad_rows, uint32_t* codes, float* scales,
+                            const float* variance, const float* lr_scale, float beta, float factor, float inv1,
+                            float inv2, float epsilon, float lr, uint32_t round_seed) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!sh_f16 || !color_dir || !grad_rows || !codes || !scales || !variance || !lr_scale || row_width == 0 ||
+      row_width > 48 || row_width % 3 != 0)
+    return vs_fail(ctx, VS_ERR_INVALID, "sh_step: bad arguments");
+  const uint64_t count = (uint64_t)num_splats * row_width;
+  if (count >= 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "sh_step: %llu values exceed u32 indexing", (unsigned long long)count);
+  if (count == 0) return VS_OK;
+  const uint32_t nblocks = (uint32_t)((count + 127) / 128);
+  VS_TRY(vs_ensure(ctx, ctx->misc, 48 * 4));
+  VS_CUDA(ctx, cudaMemcpyAsync(ctx->misc.ptr, lr_scale, row_width * 4, cudaMemcpyHostToDevice, ctx->stream));
+  ShStepArgs a{beta, factor, inv1, inv2, epsilon, lr, round_seed};
+  sh_step_kernel<<<vs::div_up(nblocks, 4), 128, 0, ctx->stream>>>((uint32_t)count, row_width, sh_f16, color_dir,
+                                                                  grad_rows, codes, scales, variance,
+                                                                  (const float*)ctx->misc.ptr, nblocks, a);
+  return vs_cuda(ctx, cudaGetLastError(), "sh_step launch");
+}
+
+VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
+                            float* transforms, float* sh_coeffs, float* raw_opacities, const float* v_combined,
+                            vs_q8_tensor mom_t, vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8,
+                            const float* visible, float* refine_norm, float* vis_count, float* max_screen) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!frame || !frame->rendered || !cfg || !q8) return vs_fail(ctx, VS_ERR_INVALID, "step_q8: missing frame/config");
+  if (num_splats != frame->n) return vs_fail(ctx, VS_ERR_INVALID, "step_q8: %u splats, frame has %u", num_splats, frame->n);
+  if (cfg->sh_half) return vs_fail(ctx, VS_ERR_UNSUPPORTED, "step_q8: SH coefficients must be f32");
+  if (!transforms || !sh_coeffs || !raw_opacities || (frame->v && !v_combined) || !q8_valid(mom_t) ||
+      !q8_valid(mom_sh) || !q8_valid(mom_o))
+    return vs_fail(ctx, VS_ERR_INVALID, "step_q8: null buffer");
+  if ((refine_norm || vis_count || max_screen || q8->noise_scale != 0.0f) && !visible)
+    return vs_fail(ctx, VS_ERR_INVALID, "step_q8: statistics and noise need `visible`");
+  const uint64_t count_sh = (uint64_t)num_splats * 3 * (cfg->sh_degree + 1) * (cfg->sh_degree + 1);
+  if (count_sh >= 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "step_q8: %llu SH values exceed u32 indexing", (unsigned long long)count_sh);
+  if (num_splats == 0) return VS_OK;
+  const Q8Args a = to_args(*q8);
+  q8_kernel<false><<<vs::div_up(num_splats, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
+      frame->u, num_splats, transforms, sh_coeffs, raw_opacities, nullptr,
+      (const uint32_t*)frame->compact_from_global.ptr, v_combined, nullptr, to_q8(mom_t), to_q8(mom_sh), to_q8(mom_o),
+      a, (const float*)frame->opacities.ptr, visible, (const float*)frame->max_radius.ptr, refine_norm, vis_count,
+      max_screen);
+  return vs_cuda(ctx, cudaGetLastError(), "step_q8 launch");
+}
+
+VS_API vs_status vs_vjp_dense(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
+                              const float* transforms, const void* sh_coeffs, const float* raw_opacities,
+                              const float* min_scale, const float* v_combined, float* grads, float* refine) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!frame || !frame->rendered || !cfg) return vs_fail(ctx, VS_ERR_INVALID, "vjp_dense: missing frame/config");
+  if (num_splats != frame->n) return vs_fail(ctx, VS_ERR_INVALID, "vjp_dense: %u splats, frame has %u", num_splats, frame->n);
+  if (!transforms || !sh_coeffs || !raw_opacities || !grads || !refine || (frame->v && !v_combined))
+    return vs_fail(ctx, VS_ERR_INVALID, "vjp_dense: null buffer");
+  if (num_splats == 0) return VS_OK;
+  vs::Uniforms u = frame->u;
+  u.sh_half = cfg->sh_half;
+  vjp_dense_kernel<<<vs::div_up(num_splats, 256), 256, 0, ctx->stream>>>(
+      u, num_splats, transforms, sh_coeffs, raw_opacities, min_scale, (const uint32_t*)frame->compact_from_global.ptr,
+      v_combined, grads, refine);
+  return vs_cuda(ctx, cudaGetLastError(), "vjp_dense launch");
+}
+
+VS_API vs_status vs_adam_q8_dense(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, float* transforms,
+                                  float* sh_coeffs, float* raw_opacities, const float* grads, vs_q8_tensor mom_t,
+                                  vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8,
+                                  const float* opacities, const float* visible) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!q8 || !transforms || !sh_coeffs || !raw_opacities || !grads || !q8_valid(mom_t) || !q8_valid(mom_sh) ||
+      !q8_valid(mom_o) || sh_degree < 0 || sh_degree > 3)
+    return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_dense: bad arguments");
+  if (num_splats == 0) return VS_OK;
+  vs::Uniforms u{};
+  u.sh_degree = sh_degree;
+  const Q8Args a = to_args(*q8);
+  q8_kernel<true><<<vs::div_up(num_splats, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
+      u, num_splats, transforms, sh_coeffs, raw_opacities, nullptr, nullptr, nullptr, grads, to_q8(mom_t),
+      to_q8(mom_sh), to_q8(mom_o), a, opacities, visible, nullptr, nullptr, nullptr, nullptr);
+  return vs_cuda(ctx, cudaGetLastError(), "adam_q8_dense launch");
+}
+
+VS_API vs_status vs_gather_stats(vs_ctx* ctx, uint32_t n, float* refine_norm, float* vis_count, float* max_screen,
+                                 const float* refine_weight, const float* visible, const float* radius) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!refine_norm || !vis_count || !max_screen || !refine_weight || !visible || !radius)
+    return vs_fail(ctx, VS_ERR_INVALID, "gather_stats: null buffer");
+  if (n == 0) return VS_OK;
+  stats_kernel<<<vs::div_up(n, 256), 256, 0, ctx->stream>>>(n, refine_norm, vis_count, max_screen, refine_weight,
+                                                            visible, radius);
+  return vs_cuda(ctx, cudaGetLastError(), "gather_stats launch");
+}
+
+VS_API vs_status vs_noise_means(vs_ctx* ctx, uint32_t n, float* transforms, const float* opacities,
+                                const float* visible, float scale, float limit, uint32_t seed) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!transforms || !opacities || !visible) return vs_fail(ctx, VS_ERR_INVALID, "noise_means: null buffer");
+  if (n == 0) return VS_OK;
+  noise_kernel<<<vs::div_up(n, 256), 256, 0, ctx->stream>>>(n, transforms, opacities, visible, scale, limit, seed);
+  return vs_cuda(ctx, cudaGetLastError(), "noise_means launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,181 @@
+// Binning: depth sort of the visible splats, intersection emission in depth
+// order, stable tile sort and per-tile ranges.
+//
+// Replaces src/render.rs:689-810 of the reference: DepthSort
+// (radix_argsort_with_count on the f32 depth bits), scan_sorted_counts_kernel +
+// scan_in_place (kernels/map_gaussians.rs:195-269), map_gaussians_to_intersect
+// (:21-174), the tile sort and get_tile_offsets (src/get_tile_offset.rs:11-52).
+// The resulting order is (tile, depth, compact id) -- a stable sort on the
+// 64-bit key tile << 32 | f32_bits(depth) -- done as a 32-bit depth sort over
+// the V visible splats followed by a stable sort over the tile bits only.
+#include "vs_internal.cuh"
+
+namespace {
+
+using namespace vs;
+
+constexpr uint32_t BIN_BLOCK = 256;
+constexpr uint32_t BIG_BOX = 16;
+
+__global__ void depth_keys_kernel(const float* __restrict__ depths, uint32_t v, uint32_t* __restrict__ keys,
+                                  uint32_t* __restrict__ ids) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < v) {
+    keys[i] = __float_as_uint(depths[i]);  // depth >= 0.01, so the bits are monotone
+    ids[i] = i;
+  }
+}
+
+__global__ void gather_counts_kernel(const uint32_t* __restrict__ order, const uint32_t* __restrict__ counts,
+                                     uint32_t v, uint32_t* __restrict__ out) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < v) out[i] = counts[order[i]];
+}
+
+// One thread per depth-sorted splat; large boxes are walked by the whole warp
+// (map_gaussians.rs:117-173).  Emission stops at the splat's counted budget
+// and pads any shortfall with the sentinel tile id T (map_gaussians.rs:76-113).
+__global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v, const uint32_t* __restrict__ order,
+                                                         const uint32_t* __restrict__ cum,
+                                                         const float4* __restrict__ projected,
+                                                         uint32_t* __restrict__ tile_keys,
+                                                         uint32_t* __restrict__ compact_vals) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t lane = threadIdx.x & 31u;
+  const bool active = i < v;
+  const uint32_t T = u.tbw * u.tbh;
+  uint32_t c = 0, start = 0, budget = 0, nb = 0, bw = 0;
+  float px = 0.f, py = 0.f, pt = 0.f;
+  S2 conic = {0.f, 0.f, 0.f};
+  TileBox b = {0, 0, 0, 0};
+  if (active) {
+    c = order[i];
+    start = i ? cum[i - 1] : 0u;
+    budget = cum[i] - start;
+    const float4 r0 = projected[(size_t)c * PROJ_F4];
+    const float4 r1 = projected[(size_t)c * PROJ_F4 + 1];
+    px = r0.x; py = r0.y;
+    conic = {r0.z, r0.w, r1.x};
+    pt = vs_logf(r1.y * 255.0f);
+    float ex, ey;
+    bbox_extent(conic, pt, &ex, &ey);
+    b = tile_bbox(px, py, ex, ey, u.tbw, u.tbh);
+    bw = b.x1 - b.x0;
+    nb = (b.y1 - b.y0) * bw;
+  }
+  if (active && nb <= BIG_BOX) {
+    uint32_t slot = 0;
+    for (uint32_t k = 0; k < nb && slot < budget; ++k) {
+      const uint32_t tx = k % bw + b.x0, ty = k / bw + b.y0;
+      if (tile_hit(tx, ty, px, py, conic, pt)) {
+        tile_keys[start + slot] = tx + ty * u.tbw;
+        compact_vals[start + slot] = c;
+        ++slot;
+      }
+    }
+    for (; slot < budget; ++slot) {
+      tile_keys[start + slot] = T;
+      compact_vals[start + slot] = c;
+    }
+  }
+  uint32_t pending = __ballot_sync(0xffffffffu, active && nb > BIG_BOX);
+  while (pending) {
+    const int leader = __ffs(pending) - 1;
+    const float lx = __shfl_sync(0xffffffffu, px, leader);
+    const float ly = __shfl_sync(0xffffffffu, py, leader);
+    const S2 lc = {__shfl_sync(0xffffffffu, conic.c00, leader), __shfl_sync(0xffffffffu, conic.c01, leader),
+                   __shfl_sync(0xffffffffu, conic.c11, leader)};
+    const float lpt = __shfl_sync(0xffffffffu, pt, leader);
+    const uint32_t lx0 = __shfl_sync(0xffffffffu, b.x0, leader);
+    const uint32_t ly0 = __shfl_sync(0xffffffffu, b.y0, leader);
+    const uint32_t lw = __shfl_sync(0xffffffffu, bw, leader);
+    const uint32_t ln = __shfl_sync(0xffffffffu, nb, leader);
+    const uint32_t lstart = __shfl_sync(0xffffffffu, start, leader);
+    const uint32_t lbudget = __shfl_sync(0xffffffffu, budget, leader);
+    const uint32_t lc_id = __shfl_sync(0xffffffffu, c, leader);
+    uint32_t emitted = 0;
+    for (uint32_t t0 = 0; t0 < ln; t0 += 32) {
+      const uint32_t t = t0 + lane;
+      const uint32_t tx = t % lw + lx0, ty = t / lw + ly0;
+      const bool hit = t < ln && tile_hit(tx, ty, lx, ly, lc, lpt);
+      const uint32_t mask = __ballot_sync(0xffffffffu, hit);
+      const uint32_t slot = emitted + __popc(mask & ((1u << lane) - 1u));
+      if (hit && slot < lbudget) {
+        tile_keys[lstart + slot] = tx + ty * u.tbw;
+        compact_vals[lstart + slot] = lc_id;
+      }
+      emitted += __popc(mask);
+    }
+    for (uint32_t p = min(emitted, lbudget) + lane; p < lbudget; p += 32) {
+      tile_keys[lstart + p] = T;
+      compact_vals[lstart + p] = lc_id;
+    }
+    pending &= pending - 1u;
+  }
+}
+
+// [start, end) of every tile present in the sorted list; absent tiles stay
+// [0, 0) from the preceding memset.  Sentinel ids (>= T) are skipped.
+__global__ void tile_ranges_kernel(const uint32_t* __restrict__ tiles_sorted, uint32_t count, uint32_t T,
+                                   uint2* __restrict__ ranges) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= count) return;
+  const uint32_t t = tiles_sorted[i];
+  if (t >= T) return;
+  if (i == 0 || tiles_sorted[i - 1] != t) ranges[t].x = i;
+  if (i + 1 == count || tiles_sorted[i + 1] != t) ranges[t].y = i + 1;
+}
+
+}  // namespace
+
+vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
+  const uint32_t v = f->v, T = f->T;
+  VS_TRY(vs_ensure(ctx, f->tile_ranges, (size_t)T * 8));
+  VS_TRY(vs_ensure(ctx, f->tile_used_end, (size_t)T * 4));
+  VS_CUDA(ctx, cudaMemsetAsync(f->tile_ranges.ptr, 0, (size_t)T * 8, ctx->stream));
+  VS_TRY(vs_ensure(ctx, f->depth_order, (size_t)(v + 1) * 4));
+  if (v == 0) {
+    f->I = 0;
+    return VS_OK;
+  }
+  // depth sort: keys = depth bits, values = compact ids
+  const uint64_t I = f->I;
+  const size_t scratch = (size_t)std::max<uint64_t>(v, I) * 4;
+  VS_TRY(vs_ensure(ctx, ctx->sort_keys, scratch * 2));
+  VS_TRY(vs_ensure(ctx, ctx->sort_vals, scratch * 2));
+  uint32_t* k0 = (uint32_t*)ctx->sort_keys.ptr;
+  uint32_t* k1 = k0 + scratch / 4;
+  uint32_t* v0 = (uint32_t*)ctx->sort_vals.ptr;
+  uint32_t* v1 = v0 + scratch / 4;
+  const uint32_t blocks_v = div_up(v, BIN_BLOCK);
+  depth_keys_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const float*)f->depths.ptr, v, k0, v0);
+  bool alt = false;
+  VS_TRY(radix_sort_pairs(ctx, k0, v0, k1, v1, v, 32, &alt));
+  uint32_t* order = alt ? v1 : v0;
+  VS_CUDA(ctx, cudaMemcpyAsync(f->depth_order.ptr, order, (size_t)v * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  // tile counts in depth order, inclusive scan -> emission offsets
+  uint32_t* cum = alt ? k0 : k1;  // free half of the key scratch
+  gather_counts_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const uint32_t*)f->depth_order.ptr,
+                                                                 (const uint32_t*)f->tile_counts.ptr, v, cum);
+  VS_TRY(scan_inclusive_u32(ctx, cum, v, nullptr));
+  VS_TRY(vs_ensure(ctx, f->isect_tile, (size_t)(I + 1) * 4));
+  VS_TRY(vs_ensure(ctx, f->isect_compact, (size_t)(I + 1) * 4));
+  if (I == 0) return VS_OK;
+  // emit straight into the frame's buffers, sort with the scratch as ping-pong
+  uint32_t* tkeys = (uint32_t*)f->isect_tile.ptr;
+  uint32_t* tvals = (uint32_t*)f->isect_compact.ptr;
+  emit_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>(f->u, v, (const uint32_t*)f->depth_order.ptr, cum,
+                                                        (const float4*)f->projected.ptr, tkeys, tvals);
+  VS_CUDA(ctx, cudaGetLastError());
+  const uint32_t tile_bits = 32u - (uint32_t)__builtin_clz(T | 1u);
+  uint32_t* sk = (uint32_t*)ctx->sort_keys.ptr;
+  uint32_t* sv = (uint32_t*)ctx->sort_vals.ptr;
+  VS_TRY(radix_sort_pairs(ctx, tkeys, tvals, sk, sv, (uint32_t)I, tile_bits, &alt));
+  if (alt) {
+    VS_CUDA(ctx, cudaMemcpyAsync(tkeys, sk, (size_t)I * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    VS_CUDA(ctx, cudaMemcpyAsync(tvals, sv, (size_t)I * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  }
+  tile_ranges_kernel<<<div_up((uint32_t)I, 256), 256, 0, ctx->stream>>>(tkeys, (uint32_t)I, T,
+                                                                        (uint2*)f->tile_ranges.ptr);
+  return vs_cuda(ctx, cudaGetLastError(), "bin launch");
+}

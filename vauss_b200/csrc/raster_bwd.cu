@@ -1,0 +1,201 @@
+// Rasterizer backward: per-pixel front-to-back replay with register-resident
+// pixel state.
+//
+// Replaces rasterize_backwards_planes_kernel (crates/splat-train-render/src/
+// bwd/kernels/rasterize_backwards_planes.rs:112-682, gaussian branch):
+// one 128-thread CTA per tile, two pixels per thread (rows y and y + 8),
+// splats staged 32 at a time in shared memory.  Per splat, each thread sums its
+// pixels' gradients, a 32-lane butterfly reduce-scatter leaves one component
+// per lane pair, the four warps' partials are added in shared memory, and one
+// atomic add per non-zero (tile, splat, component) lands in v_combined [V,10]
+// = [xy(2), conic(3), rgb(3), alpha, refine].
+//
+// The replay evaluates exactly the forward's exponent, alpha and transmittance
+// sequence (raster_sigma, vs_expf, the same comparisons), so every
+// accept/terminate decision matches the forward pass bit for bit.
+#include "vs_internal.cuh"
+
+namespace {
+
+using namespace vs;
+
+constexpr uint32_t RB_THREADS = 128;
+constexpr uint32_t RB_WARPS = RB_THREADS / 32;
+constexpr uint32_t RB_BATCH = 32;
+constexpr uint32_t NG = 10;
+
+// Butterfly reduce-scatter of 16 values over 32 lanes: afterwards v[0] of lane
+// l holds the warp sum of component (l >> 1) & 15.
+__device__ __forceinline__ float reduce_scatter16(float v[16], uint32_t lane) {
+  {
+    const bool hi = lane & 16u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float keep = hi ? v[i + 8] : v[i];
+      const float send = hi ? v[i] : v[i + 8];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+  }
+  {
+    const bool hi = lane & 8u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float keep = hi ? v[i + 4] : v[i];
+      const float send = hi ? v[i] : v[i + 4];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+  }
+  {
+    const bool hi = lane & 4u;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float keep = hi ? v[i + 2] : v[i];
+      const float send = hi ? v[i] : v[i + 2];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+  }
+  {
+    const bool hi = lane & 2u;
+    const float keep = hi ? v[1] : v[0];
+    const float send = hi ? v[0] : v[1];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+__global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
+    uint32_t w, uint32_t h, uint32_t tbw, float bg_r, float bg_g, float bg_b, const uint2* __restrict__ ranges,
+    const uint32_t* __restrict__ used_end, const uint32_t* __restrict__ isect_compact,
+    const float4* __restrict__ projected, const float4* __restrict__ out_img, const float4* __restrict__ v_out,
+    float* __restrict__ v_combined) {
+  __shared__ float4 s_a[RB_BATCH];  // x, y, c00, c01
+  __shared__ float4 s_b[RB_BATCH];  // c11, opac, r, g
+  __shared__ float2 s_c[RB_BATCH];  // b, sigma cut
+  __shared__ uint32_t s_cid[RB_BATCH];
+  __shared__ float s_part[RB_WARPS][RB_BATCH][NG];
+
+  const uint32_t tile = blockIdx.x;
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const uint32_t px = (tile % tbw) * TILE + tid % TILE;
+  const uint32_t py0 = (tile / tbw) * TILE + tid / TILE;
+  const float fx = (float)px + 0.5f;
+  const float img_w = (float)w, img_h = (float)h;
+
+  float sr[2], sg[2], sb[2], st[2], vr[2], vg[2], vb[2], vt[2], rs[2], fy[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const uint32_t py = py0 + 8u * k;
+    fy[k] = (float)py + 0.5f;
+    sr[k] = sg[k] = sb[k] = st[k] = vr[k] = vg[k] = vb[k] = vt[k] = rs[k] = 0.0f;
+    if (px < w && py < h) {
+      const size_t p = (size_t)py * w + px;
+      const float4 o = out_img[p];
+      const float4 vo = v_out[p];
+      const float t_final = 1.0f - o.w;
+      sr[k] = o.x - t_final * bg_r;
+      sg[k] = o.y - t_final * bg_g;
+      sb[k] = o.z - t_final * bg_b;
+      st[k] = 1.0f;
+      vr[k] = vo.x;
+      vg[k] = vo.y;
+      vb[k] = vo.z;
+      vt[k] = (vo.w - (bg_r * vo.x + bg_g * vo.y + bg_b * vo.z)) * t_final;
+      rs[k] = 1.0f / fmaxf(o.w, 1.0e-5f);
+    }
+  }
+
+  const uint32_t lo = ranges[tile].x, hi = used_end[tile];
+  for (uint32_t batch = lo; batch < hi; batch += RB_BATCH) {
+    const uint32_t cnt = min(RB_BATCH, hi - batch);
+    if (tid < cnt) {
+      const uint32_t c = isect_compact[batch + tid];
+      const float4 a = projected[(size_t)c * PROJ_F4];
+      const float4 bb = projected[(size_t)c * PROJ_F4 + 1];
+      const float4 cc = projected[(size_t)c * PROJ_F4 + 2];
+      s_a[tid] = a;
+      s_b[tid] = bb;
+      s_c[tid] = make_float2(cc.x, vs_logf(bb.y / ALPHA_EDGE) + 1.0e-3f);
+      s_cid[tid] = c;
+    }
+    __syncthreads();
+    for (uint32_t t = 0; t < cnt; ++t) {
+      const float4 a = s_a[t];
+      const float4 bb = s_b[t];
+      const float2 cc = s_c[t];
+      const float c00 = a.z, c01 = a.w, c11 = bb.x, opac = bb.y;
+      const float cr = fmaxf(bb.z, 0.0f), cg = fmaxf(bb.w, 0.0f), cb = fmaxf(cc.x, 0.0f);
+      const float dx = a.x - fx;
+      float g[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) g[i] = 0.0f;
+      bool contributes = false;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const float dy = a.y - fy[k];
+        const float sigma = raster_sigma(0.5f * c00, c01, 0.5f * c11, dx, dy);
+        if (!(st[k] > 1.0e-4f && sigma <= cc.y)) continue;
+        const float gauss = vs_expf(-sigma);
+        const float alpha = fminf(0.999f, opac * gauss);
+        if (!(sigma >= 0.0f && alpha >= ALPHA_MIN)) continue;
+        const float next_t = st[k] * (1.0f - alpha);
+        if (next_t <= 1.0e-4f) {
+          st[k] = 0.0f;
+          continue;
+        }
+        contributes = true;
+        const float vis = alpha * st[k];
+        if (bb.z >= 0.0f) g[5] += vis * vr[k];
+        if (bb.w >= 0.0f) g[6] += vis * vg[k];
+        if (cc.x >= 0.0f) g[7] += vis * vb[k];
+        const float ra = 1.0f / (1.0f - alpha);
+        const float dot =
+            ((st[k] * cr - sr[k]) * vr[k] + (st[k] * cg - sg[k]) * vg[k] + (st[k] * cb - sb[k]) * vb[k]) * ra;
+        const float v_alpha = dot + vt[k] * ra;
+        const float v_sigma = -alpha * v_alpha;
+        const float vxx = v_sigma * (c00 * dx + c01 * dy);
+        const float vxy = v_sigma * (c01 * dx + c11 * dy);
+        if (opac * gauss <= 0.999f) {
+          g[2] += 0.5f * v_sigma * dx * dx;
+          g[3] += v_sigma * dx * dy;
+          g[4] += 0.5f * v_sigma * dy * dy;
+          g[0] += vxx;
+          g[1] += vxy;
+          g[8] += v_alpha * gauss;
+          g[9] += sqrtf(vxx * img_w * vxx * img_w + vxy * img_h * vxy * img_h) * rs[k];
+        }
+        sr[k] = sr[k] - vis * cr;
+        sg[k] = sg[k] - vis * cg;
+        sb[k] = sb[k] - vis * cb;
+        st[k] = next_t;
+      }
+      if (__any_sync(0xffffffffu, contributes)) {
+        const float sum = reduce_scatter16(g, lane);
+        const uint32_t comp = (lane >> 1) & 15u;
+        if ((lane & 1u) == 0 && comp < NG) s_part[warp][t][comp] = sum;
+      } else if (lane < NG) {
+        s_part[warp][t][lane] = 0.0f;
+      }
+    }
+    __syncthreads();
+    for (uint32_t idx = tid; idx < cnt * NG; idx += RB_THREADS) {
+      const uint32_t s = idx / NG, comp = idx % NG;
+      float sum = 0.0f;
+#pragma unroll
+      for (uint32_t ww = 0; ww < RB_WARPS; ++ww) sum += s_part[ww][s][comp];
+      if (sum != 0.0f) atomicAdd(&v_combined[(size_t)s_cid[s] * NG + comp], sum);
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+vs_status launch_raster_bwd(vs_ctx* ctx, vs_frame* f, const float* out_img, const float* v_out, float* v_combined) {
+  VS_CUDA(ctx, cudaMemsetAsync(v_combined, 0, (size_t)f->v * NG * 4, ctx->stream));
+  if (f->T == 0 || f->I == 0) return VS_OK;
+  raster_bwd_kernel<<<f->T, RB_THREADS, 0, ctx->stream>>>(
+      f->u.w, f->u.h, f->u.tbw, f->u.bg[0], f->u.bg[1], f->u.bg[2], (const uint2*)f->tile_ranges.ptr,
+      (const uint32_t*)f->tile_used_end.ptr, (const uint32_t*)f->isect_compact.ptr, (const float4*)f->projected.ptr,
+      (const float4*)out_img, (const float4*)v_out, v_combined);
+  return vs_cuda(ctx, cudaGetLastError(), "raster_bwd launch");
+}

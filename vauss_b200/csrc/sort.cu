@@ -1,0 +1,267 @@
+// Stable LSD radix sort of (u32 key, u32 value) pairs and a device-wide
+// inclusive scan.
+//
+// Replaces the reference's radix_argsort_with_count
+// (crates/splat-train-sort/src/lib.rs:40-189, kernels.rs:13-341: 8-bit digits,
+// count / reduce / scan / scan_add / scatter per pass) and prefix sums
+// (crates/splat-train-scan/src/kernels.rs:30-212).
+//
+// Per 8-bit pass: (1) each block histograms its 2048-key tile into a
+// digit-major table hist[digit][tile]; (2) an exclusive scan of that table
+// gives every (digit, tile) its global output offset; (3) each block ranks its
+// keys stably (every warp ranks a contiguous 256-key slice with match_any,
+// warps are combined through per-digit counts), scatters them into shared
+// memory in digit order and writes contiguous per-digit runs to global memory.
+#include "vs_internal.cuh"
+
+namespace {
+
+using namespace vs;
+
+constexpr uint32_t SORT_THREADS = 256;
+constexpr uint32_t SORT_WARPS = SORT_THREADS / 32;
+constexpr uint32_t ITEMS = 8;  // per thread
+constexpr uint32_t SORT_TILE = SORT_THREADS * ITEMS;  // 2048
+constexpr uint32_t RADIX = 256;
+
+__global__ void __launch_bounds__(SORT_THREADS) hist_kernel(const uint32_t* __restrict__ keys, uint32_t count,
+                                                            uint32_t shift, uint32_t mask, uint32_t tiles,
+                                                            uint32_t* __restrict__ hist) {
+  __shared__ uint32_t s_hist[RADIX];
+  const uint32_t tid = threadIdx.x;
+  s_hist[tid] = 0;
+  __syncthreads();
+  const uint32_t base = blockIdx.x * SORT_TILE;
+  const uint32_t lane = tid & 31u;
+#pragma unroll
+  for (uint32_t r = 0; r < ITEMS; ++r) {
+    const uint32_t i = base + r * SORT_THREADS + tid;
+    const bool valid = i < count;
+    const uint32_t d = valid ? ((keys[i] >> shift) & mask) : RADIX;
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    if (valid && (uint32_t)(__ffs(peers) - 1) == lane) atomicAdd(&s_hist[d], (uint32_t)__popc(peers));
+  }
+  __syncthreads();
+  hist[tid * tiles + blockIdx.x] = s_hist[tid];
+}
+
+__global__ void __launch_bounds__(SORT_THREADS) scatter_kernel(
+    const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in, uint32_t* __restrict__ keys_out,
+    uint32_t* __restrict__ vals_out, uint32_t count, uint32_t shift, uint32_t mask, uint32_t tiles,
+    const uint32_t* __restrict__ offsets /* exclusive-scanned hist, digit-major */) {
+  __shared__ uint32_t s_wcnt[SORT_WARPS][RADIX];  // per-warp digit counts, then per-warp offsets
+  __shared__ uint32_t s_dstart[RADIX];            // block-local start of each digit
+  __shared__ uint32_t s_goff[RADIX];              // global start of each digit for this tile
+  __shared__ uint32_t s_keys[SORT_TILE];
+  __shared__ uint32_t s_vals[SORT_TILE];
+  __shared__ uint32_t s_scan[SORT_WARPS];
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  for (uint32_t i = tid; i < SORT_WARPS * RADIX; i += SORT_THREADS) (&s_wcnt[0][0])[i] = 0;
+  s_goff[tid] = offsets[tid * tiles + blockIdx.x];
+  __syncthreads();
+
+  // Warp `warp` owns keys [base + warp*256, base + warp*256 + 256), 32 per round.
+  const uint32_t base = blockIdx.x * SORT_TILE + warp * (ITEMS * 32);
+  uint32_t k[ITEMS], v[ITEMS], d[ITEMS], rank[ITEMS];
+#pragma unroll
+  for (uint32_t r = 0; r < ITEMS; ++r) {
+    const uint32_t i = base + r * 32 + lane;
+    const bool valid = i < count;
+    k[r] = valid ? keys_in[i] : 0u;
+    v[r] = valid ? vals_in[i] : 0u;
+    d[r] = valid ? ((k[r] >> shift) & mask) : RADIX;
+  }
+#pragma unroll
+  for (uint32_t r = 0; r < ITEMS; ++r) {
+    const uint32_t peers = __match_any_sync(0xffffffffu, d[r]);
+    const uint32_t leader = __ffs(peers) - 1;
+    uint32_t before = 0;
+    if (lane == leader && d[r] < RADIX) {
+      before = s_wcnt[warp][d[r]];
+      s_wcnt[warp][d[r]] = before + __popc(peers);
+    }
+    before = __shfl_sync(0xffffffffu, before, leader);
+    rank[r] = before + __popc(peers & ((1u << lane) - 1u));
+    __syncwarp();
+  }
+  __syncthreads();
+  // thread `tid` owns digit `tid`: exclusive prefix over warps, block total
+  uint32_t run = 0;
+#pragma unroll
+  for (uint32_t w = 0; w < SORT_WARPS; ++w) {
+    const uint32_t c = s_wcnt[w][tid];
+    s_wcnt[w][tid] = run;
+    run += c;
+  }
+  // exclusive scan of the digit totals across the block (digit-ordered)
+  uint32_t incl = run;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= (uint32_t)off) incl += y;
+  }
+  if (lane == 31) s_scan[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t s = lane < SORT_WARPS ? s_scan[lane] : 0u;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, s, off);
+      if (lane >= (uint32_t)off) s += y;
+    }
+    if (lane < SORT_WARPS) s_scan[lane] = s;
+  }
+  __syncthreads();
+  s_dstart[tid] = incl - run + (warp ? s_scan[warp - 1] : 0u);
+  __syncthreads();
+#pragma unroll
+  for (uint32_t r = 0; r < ITEMS; ++r) {
+    if (d[r] < RADIX) {
+      const uint32_t pos = s_dstart[d[r]] + s_wcnt[warp][d[r]] + rank[r];
+      s_keys[pos] = k[r];
+      s_vals[pos] = v[r];
+    }
+  }
+  __syncthreads();
+  const uint32_t tile_base = blockIdx.x * SORT_TILE;
+  const uint32_t n_here = min(SORT_TILE, count - tile_base);
+  for (uint32_t p = tid; p < n_here; p += SORT_THREADS) {
+    const uint32_t key = s_keys[p];
+    const uint32_t dd = (key >> shift) & mask;
+    const uint32_t out = s_goff[dd] + (p - s_dstart[dd]);
+    keys_out[out] = key;
+    vals_out[out] = s_vals[p];
+  }
+}
+
+// ---- device-wide inclusive scan of u32 (three phases) ----
+constexpr uint32_t SCAN_THREADS = 256;
+constexpr uint32_t SCAN_ITEMS = 16;
+constexpr uint32_t SCAN_CHUNK = SCAN_THREADS * SCAN_ITEMS;  // 4096
+
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t x, uint32_t* s_warp, uint32_t* total) {
+  const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+  uint32_t incl = x;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= (uint32_t)off) incl += y;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t s = lane < (blockDim.x >> 5) ? s_warp[lane] : 0u;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, s, off);
+      if (lane >= (uint32_t)off) s += y;
+    }
+    s_warp[lane] = s;
+  }
+  __syncthreads();
+  const uint32_t res = incl - x + (warp ? s_warp[warp - 1] : 0u);
+  *total = s_warp[(blockDim.x >> 5) - 1];
+  __syncthreads();
+  return res;
+}
+
+__global__ void __launch_bounds__(SCAN_THREADS) scan_reduce_kernel(const uint32_t* __restrict__ data, uint32_t count,
+                                                                   uint32_t* __restrict__ sums) {
+  __shared__ uint32_t s_warp[32];
+  const uint32_t base = blockIdx.x * SCAN_CHUNK + threadIdx.x * SCAN_ITEMS;
+  uint32_t s = 0;
+#pragma unroll
+  for (uint32_t i = 0; i < SCAN_ITEMS; ++i) s += (base + i < count) ? data[base + i] : 0u;
+  uint32_t total;
+  block_exclusive_scan(s, s_warp, &total);
+  if (threadIdx.x == 0) sums[blockIdx.x] = total;
+}
+
+// One block: exclusive scan of the chunk sums in place; total to *total_dev.
+__global__ void __launch_bounds__(1024) scan_sums_kernel(uint32_t* sums, uint32_t nsums,
+                                                         unsigned long long* total_dev) {
+  __shared__ uint32_t s_warp[32];
+  const uint32_t per = (nsums + blockDim.x - 1) / blockDim.x;
+  const uint32_t b0 = threadIdx.x * per;
+  uint32_t local = 0;
+  for (uint32_t i = 0; i < per; ++i) local += (b0 + i < nsums) ? sums[b0 + i] : 0u;
+  uint32_t total;
+  uint32_t run = block_exclusive_scan(local, s_warp, &total);
+  for (uint32_t i = 0; i < per; ++i) {
+    if (b0 + i < nsums) {
+      const uint32_t x = sums[b0 + i];
+      sums[b0 + i] = run;
+      run += x;
+    }
+  }
+  if (threadIdx.x == 0 && total_dev) *total_dev = total;
+}
+
+template <bool kInclusive>
+__global__ void __launch_bounds__(SCAN_THREADS) scan_apply_kernel(uint32_t* __restrict__ data, uint32_t count,
+                                                                  const uint32_t* __restrict__ sums) {
+  __shared__ uint32_t s_warp[32];
+  const uint32_t base = blockIdx.x * SCAN_CHUNK + threadIdx.x * SCAN_ITEMS;
+  uint32_t x[SCAN_ITEMS];
+  uint32_t s = 0;
+#pragma unroll
+  for (uint32_t i = 0; i < SCAN_ITEMS; ++i) {
+    x[i] = (base + i < count) ? data[base + i] : 0u;
+    s += x[i];
+  }
+  uint32_t total;
+  uint32_t run = block_exclusive_scan(s, s_warp, &total) + sums[blockIdx.x];
+#pragma unroll
+  for (uint32_t i = 0; i < SCAN_ITEMS; ++i) {
+    if (kInclusive) run += x[i];
+    if (base + i < count) data[base + i] = run;
+    if (!kInclusive) run += x[i];
+  }
+}
+
+vs_status scan_impl(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev, bool inclusive) {
+  if (count == 0) {
+    if (total_dev) VS_CUDA(ctx, cudaMemsetAsync(total_dev, 0, 8, ctx->stream));
+    return VS_OK;
+  }
+  const uint32_t chunks = div_up(count, SCAN_CHUNK);
+  VS_TRY(vs_ensure(ctx, ctx->scan_sums, (size_t)chunks * sizeof(uint32_t)));
+  uint32_t* sums = (uint32_t*)ctx->scan_sums.ptr;
+  scan_reduce_kernel<<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums);
+  scan_sums_kernel<<<1, 1024, 0, ctx->stream>>>(sums, chunks, (unsigned long long*)total_dev);
+  if (inclusive)
+    scan_apply_kernel<true><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums);
+  else
+    scan_apply_kernel<false><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums);
+  return vs_cuda(ctx, cudaGetLastError(), "scan launch");
+}
+
+}  // namespace
+
+vs_status scan_inclusive_u32(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev) {
+  return scan_impl(ctx, data, count, total_dev, true);
+}
+
+vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
+                           uint32_t count, uint32_t key_bits, bool* result_in_alt) {
+  *result_in_alt = false;
+  if (count <= 1 || key_bits == 0) return VS_OK;
+  const uint32_t tiles = div_up(count, SORT_TILE);
+  const size_t hist_n = (size_t)RADIX * tiles;
+  if (hist_n > 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "radix sort: %u keys exceed the histogram", count);
+  VS_TRY(vs_ensure(ctx, ctx->sort_hist, hist_n * sizeof(uint32_t)));
+  uint32_t* hist = (uint32_t*)ctx->sort_hist.ptr;
+  uint32_t *kin = keys, *vin = vals, *kout = keys_alt, *vout = vals_alt;
+  for (uint32_t shift = 0; shift < key_bits; shift += 8) {
+    const uint32_t bits = min(8u, key_bits - shift);
+    const uint32_t mask = (1u << bits) - 1u;
+    hist_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist);
+    VS_TRY(scan_impl(ctx, hist, (uint32_t)hist_n, nullptr, false));
+    scatter_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist);
+    VS_CUDA(ctx, cudaGetLastError());
+    uint32_t* t = kin; kin = kout; kout = t;
+    t = vin; vin = vout; vout = t;
+    *result_in_alt = !*result_in_alt;
+  }
+  return VS_OK;
+}

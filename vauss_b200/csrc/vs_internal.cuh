@@ -1,0 +1,69 @@
+// Host-side internals: context, frames, workspace, launch declarations.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string>
+
+#include "../../include/vauss_b200.h"
+#include "vs_common.cuh"
+
+// A grow-only device allocation.
+struct DevBuf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
+struct vs_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  uint32_t* d_err = nullptr;       // device error word (VS_DERR_*)
+  uint32_t* h_pinned = nullptr;    // pinned host mirror for small readbacks (16 words)
+  uint64_t workspace = 0;          // bytes held by the ctx and its frames
+  // scratch shared by calls on this ctx (stream-ordered reuse)
+  DevBuf sort_keys, sort_vals, sort_hist, scan_sums, misc;
+};
+
+struct vs_frame {
+  vs_ctx* ctx = nullptr;
+  vs::Uniforms u{};
+  vs_render_cfg cfg{};
+  uint32_t n = 0, v = 0, T = 0;
+  uint64_t I = 0;
+  bool rendered = false;
+  DevBuf compact_from_global, global_from_compact, depths, tile_counts, projected, depth_order;
+  DevBuf isect_tile, isect_compact, tile_ranges, tile_used_end, opacities, max_radius;
+  DevBuf lookback, counters;  // projection compaction state
+};
+
+// Records a message on the ctx and returns `st`.
+vs_status vs_fail(vs_ctx* ctx, vs_status st, const char* fmt, ...);
+// Checks a CUDA call result.
+vs_status vs_cuda(vs_ctx* ctx, cudaError_t e, const char* what);
+// Grows `b` to at least `bytes` (contents are not preserved).
+vs_status vs_ensure(vs_ctx* ctx, DevBuf& b, size_t bytes);
+void vs_release(vs_ctx* ctx, DevBuf& b);
+// Reads the device error word, clears it, and maps it to a status.
+vs_status vs_check_device_error(vs_ctx* ctx, const char* stage);
+
+#define VS_TRY(expr)                  \
+  do {                                \
+    vs_status _st = (expr);           \
+    if (_st != VS_OK) return _st;     \
+  } while (0)
+#define VS_CUDA(ctx, expr) VS_TRY(vs_cuda((ctx), (expr), #expr))
+
+vs::Uniforms vs_make_uniforms(const vs_camera& c, const vs_render_cfg& cfg);
+
+// ---- launchers (defined next to their kernels) ----
+vs_status launch_project(vs_ctx* ctx, vs_frame* f, const float* transforms, const void* sh, const float* raw_opac,
+                         const float* min_scale);
+vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
+                           uint32_t count, uint32_t key_bits, bool* result_in_alt);
+vs_status scan_inclusive_u32(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev);
+vs_status launch_bin(vs_ctx* ctx, vs_frame* f);
+vs_status launch_raster_fwd(vs_ctx* ctx, vs_frame* f, float* out_img, float* visible);
+vs_status launch_raster_bwd(vs_ctx* ctx, vs_frame* f, const float* out_img, const float* v_out, float* v_combined);
+vs_status launch_loss(vs_ctx* ctx, uint32_t h, uint32_t w, const float* pred, const uint32_t* gt, float l1_w,
+                      float ssim_w, float* partials, float* loss_dev, float* dl_dpred);
