@@ -77,6 +77,8 @@ VS_API vs_status vs_ctx_set_stream(vs_ctx* ctx, void* cuda_stream);
 VS_API const char* vs_ctx_last_error(const vs_ctx* ctx);
 /* Bytes of device workspace the ctx and its frames currently hold. */
 VS_API uint64_t vs_ctx_workspace_bytes(const vs_ctx* ctx);
+/* Number of kernels this ctx has launched (all entry points together). */
+VS_API uint64_t vs_ctx_launch_count(const vs_ctx* ctx);
 VS_API const char* vs_version(void);
 
 VS_API vs_status vs_frame_create(vs_ctx* ctx, vs_frame** out);
@@ -114,6 +116,14 @@ VS_API vs_status vs_render_forward(vs_ctx* ctx, vs_frame* frame, const vs_camera
                                    uint32_t num_splats, const float* transforms, const void* sh_coeffs,
                                    const float* raw_opacities, const float* min_scale, float* out_img,
                                    float* visible, vs_render_counts* counts_out);
+/* vs_render_forward in three stages (it calls exactly these):
+ * project = project_forward_kernel + project_visible_kernel + the count readback,
+ * bin = depth sort + emission + tile sort + tile ranges, rasterize = compositing. */
+VS_API vs_status vs_render_project(vs_ctx* ctx, vs_frame* frame, const vs_camera* cam, const vs_render_cfg* cfg,
+                                   uint32_t num_splats, const float* transforms, const void* sh_coeffs,
+                                   const float* raw_opacities, const float* min_scale, vs_render_counts* counts_out);
+VS_API vs_status vs_render_bin(vs_ctx* ctx, vs_frame* frame);
+VS_API vs_status vs_render_rasterize(vs_ctx* ctx, vs_frame* frame, float* out_img, float* visible);
 
 /* ---- loss ------------------------------------------------------------------
  * Replaces LossOps::image_loss_forward_train + image_loss_backward_coeffs
@@ -197,13 +207,16 @@ VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* c
 /* Dense projection VJP (the multi-view path, src/bwd/kernels/
  * project_backwards.rs:282-424 + the dense gather of burn_glue.rs:363-395):
  * ACCUMULATES this frame's gradients into grads [N, 10 + 3(d+1)^2 + 1]
- * (transforms | sh | raw opacity) and refine [N]. */
+ * (transforms | sh | raw opacity) and refine [N]; with vis_accum != NULL also
+ * vis_accum += visible (the per-step count of views that saw each splat). */
 VS_API vs_status vs_vjp_dense(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
                               const float* transforms, const void* sh_coeffs, const float* raw_opacities,
-                              const float* min_scale, const float* v_combined, float* grads, float* refine);
+                              const float* min_scale, const float* v_combined, float* grads, float* refine,
+                              const float* visible, float* vis_accum);
 
 /* Adam (8-bit m+v) from dense gradients grads [N, width] (after the
- * cross-GPU all-reduce).  visible may be NULL (no noise). */
+ * cross-GPU all-reduce).  visible may be NULL (no noise); with opacities NULL
+ * the noise gate uses sigmoid(raw_opacities). */
 VS_API vs_status vs_adam_q8_dense(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, float* transforms,
                                   float* sh_coeffs, float* raw_opacities, const float* grads, vs_q8_tensor mom_t,
                                   vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8,

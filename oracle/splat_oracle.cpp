@@ -1366,7 +1366,7 @@ OR_API int or_noise_means(uint32_t n, float* transforms, const float* opacities,
   for (uint32_t i = 0; i < n; ++i) {
     const float om = 1.0f - opacities[i];
     const float pw = om > 0.0f ? vs_expf(150.0f * vs_logf(om)) : 0.0f;
-    const float gate = clampf(pw, 0.0f, 1.0f) * visible[i];
+    const float gate = clampf(pw, 0.0f, 1.0f) * fminf(visible[i], 1.0f);
     if (gate > 0.0f) {
       const float w = gate * scale;
       const uint32_t base = i * 4u;

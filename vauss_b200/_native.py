@@ -67,6 +67,7 @@ _SIGS = {
     "vs_ctx_set_stream": ([c_vp, c_vp], ctypes.c_int),
     "vs_ctx_last_error": ([c_vp], ctypes.c_char_p),
     "vs_ctx_workspace_bytes": ([c_vp], ctypes.c_uint64),
+    "vs_ctx_launch_count": ([c_vp], ctypes.c_uint64),
     "vs_frame_create": ([c_vp, ctypes.POINTER(c_vp)], ctypes.c_int),
     "vs_frame_destroy": ([c_vp], None),
     "vs_frame_buffer": ([c_vp, ctypes.c_int32, ctypes.POINTER(c_vp), ctypes.POINTER(ctypes.c_uint64)], ctypes.c_int),
@@ -74,6 +75,10 @@ _SIGS = {
     "vs_frame_copy": ([c_vp, ctypes.c_int32, c_vp, ctypes.c_uint64], ctypes.c_int),
     "vs_render_forward": ([c_vp, c_vp, ctypes.POINTER(VsCamera), ctypes.POINTER(RenderCfg), ctypes.c_uint32, c_vp,
                            c_vp, c_vp, c_vp, c_vp, c_vp, ctypes.POINTER(RenderCounts)], ctypes.c_int),
+    "vs_render_project": ([c_vp, c_vp, ctypes.POINTER(VsCamera), ctypes.POINTER(RenderCfg), ctypes.c_uint32, c_vp,
+                           c_vp, c_vp, c_vp, ctypes.POINTER(RenderCounts)], ctypes.c_int),
+    "vs_render_bin": ([c_vp, c_vp], ctypes.c_int),
+    "vs_render_rasterize": ([c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_loss": ([c_vp, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, ctypes.c_float, ctypes.c_float, c_vp, c_vp,
                  c_vp], ctypes.c_int),
     "vs_rasterize_backward": ([c_vp, c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
@@ -86,7 +91,7 @@ _SIGS = {
     "vs_step_q8": ([c_vp, c_vp, ctypes.POINTER(RenderCfg), ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, Q8Tensor,
                     Q8Tensor, Q8Tensor, ctypes.POINTER(Q8Cfg), c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_vjp_dense": ([c_vp, c_vp, ctypes.POINTER(RenderCfg), ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
-                      c_vp], ctypes.c_int),
+                      c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_adam_q8_dense": ([c_vp, ctypes.c_uint32, ctypes.c_int32, c_vp, c_vp, c_vp, c_vp, Q8Tensor, Q8Tensor,
                           Q8Tensor, ctypes.POINTER(Q8Cfg), c_vp, c_vp], ctypes.c_int),
     "vs_gather_stats": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], ctypes.c_int),

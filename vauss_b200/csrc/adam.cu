@@ -222,9 +222,12 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t n, 
                                                         const float* __restrict__ min_scale,
                                                         const uint32_t* __restrict__ compact_from_global,
                                                         const float* __restrict__ v_combined,
-                                                        float* __restrict__ grads, float* __restrict__ refine) {
+                                                        float* __restrict__ grads, float* __restrict__ refine,
+                                                        const float* __restrict__ visible,
+                                                        float* __restrict__ vis_accum) {
   const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
   if (g >= n) return;
+  if (vis_accum) vis_accum[g] += visible[g];
   const uint32_t row = compact_from_global[g];
   if (row == 0) return;
   const float* rg = v_combined + (size_t)(row - 1) * 10;
@@ -291,7 +294,8 @@ __device__ __forceinline__ void mean_noise(uint32_t i, float opac, float vis, fl
   *nx = *ny = *nz = 0.0f;
   const float om = 1.0f - opac;
   const float pw = om > 0.0f ? vs_expf(150.0f * vs_logf(om)) : 0.0f;
-  const float gate = clampf(pw, 0.0f, 1.0f) * vis;
+  // `vis` is a 0/1 mark, or a per-step count of views that saw the splat
+  const float gate = clampf(pw, 0.0f, 1.0f) * fminf(vis, 1.0f);
   if (gate > 0.0f) {
     const float w = gate * scale;
     const uint32_t base = i * 4u;
@@ -375,8 +379,13 @@ __global__ void __launch_bounds__(Q8_SPLATS) q8_kernel(
         const float o = 1.0f / (1.0f + vs_expf(-raw_opac[g]));
         go = go + a.opac_reg * o * (1.0f - o);
       }
-      if (opacities && visible && a.noise_scale != 0.0f)
-        mean_noise(g, opacities[g], visible[g], a.noise_scale, a.noise_limit, a.noise_seed, &nx, &ny, &nz);
+      if (visible && a.noise_scale != 0.0f) {
+        // without per-view opacities (the multi-view path) the gate uses the
+        // unfloored sigmoid opacity, which projection also reports when no
+        // min_scale floor is set
+        const float op = opacities ? opacities[g] : 1.0f / (1.0f + vs_expf(-raw_opac[g]));
+        mean_noise(g, op, visible[g], a.noise_scale, a.noise_limit, a.noise_seed, &nx, &ny, &nz);
+      }
     }
 #pragma unroll
     for (int k = 0; k < 10; ++k) s_gt[tid * 10 + k] = gr[k];
@@ -540,7 +549,7 @@ VS_API vs_status vs_project_update(vs_ctx* ctx, vs_frame* frame, const vs_render
   project_update_kernel<<<vs::div_up(num_splats, 256), 256, 0, ctx->stream>>>(
       u, num_splats, transforms, sh_coeffs, raw_opacities, min_scale,
       (const uint32_t*)frame->compact_from_global.ptr, v_combined, w_t, w_o, a, color_dir, v_refine, grad_sq, variance,
-      first_step);
+      first_step); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "project_update launch");
 }
 
@@ -561,7 +570,7 @@ VS_API vs_status vs_sh_step(vs_ctx* ctx, uint32_t num_splats, uint32_t row_width
   ShStepArgs a{beta, factor, inv1, inv2, epsilon, lr, round_seed};
   sh_step_kernel<<<vs::div_up(nblocks, 4), 128, 0, ctx->stream>>>((uint32_t)count, row_width, sh_f16, color_dir,
                                                                   grad_rows, codes, scales, variance,
-                                                                  (const float*)ctx->misc.ptr, nblocks, a);
+                                                                  (const float*)ctx->misc.ptr, nblocks, a); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "sh_step launch");
 }
 
@@ -586,24 +595,26 @@ VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* c
       frame->u, num_splats, transforms, sh_coeffs, raw_opacities, nullptr,
       (const uint32_t*)frame->compact_from_global.ptr, v_combined, nullptr, to_q8(mom_t), to_q8(mom_sh), to_q8(mom_o),
       a, (const float*)frame->opacities.ptr, visible, (const float*)frame->max_radius.ptr, refine_norm, vis_count,
-      max_screen);
+      max_screen); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "step_q8 launch");
 }
 
 VS_API vs_status vs_vjp_dense(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
                               const float* transforms, const void* sh_coeffs, const float* raw_opacities,
-                              const float* min_scale, const float* v_combined, float* grads, float* refine) {
+                              const float* min_scale, const float* v_combined, float* grads, float* refine,
+                              const float* visible, float* vis_accum) {
   if (!ctx) return VS_ERR_INVALID;
   if (!frame || !frame->rendered || !cfg) return vs_fail(ctx, VS_ERR_INVALID, "vjp_dense: missing frame/config");
   if (num_splats != frame->n) return vs_fail(ctx, VS_ERR_INVALID, "vjp_dense: %u splats, frame has %u", num_splats, frame->n);
-  if (!transforms || !sh_coeffs || !raw_opacities || !grads || !refine || (frame->v && !v_combined))
+  if (!transforms || !sh_coeffs || !raw_opacities || !grads || !refine || (frame->v && !v_combined) ||
+      (vis_accum && !visible))
     return vs_fail(ctx, VS_ERR_INVALID, "vjp_dense: null buffer");
   if (num_splats == 0) return VS_OK;
   vs::Uniforms u = frame->u;
   u.sh_half = cfg->sh_half;
   vjp_dense_kernel<<<vs::div_up(num_splats, 256), 256, 0, ctx->stream>>>(
       u, num_splats, transforms, sh_coeffs, raw_opacities, min_scale, (const uint32_t*)frame->compact_from_global.ptr,
-      v_combined, grads, refine);
+      v_combined, grads, refine, visible, vis_accum); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "vjp_dense launch");
 }
 
@@ -621,7 +632,7 @@ VS_API vs_status vs_adam_q8_dense(vs_ctx* ctx, uint32_t num_splats, int32_t sh_d
   const Q8Args a = to_args(*q8);
   q8_kernel<true><<<vs::div_up(num_splats, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
       u, num_splats, transforms, sh_coeffs, raw_opacities, nullptr, nullptr, nullptr, grads, to_q8(mom_t),
-      to_q8(mom_sh), to_q8(mom_o), a, opacities, visible, nullptr, nullptr, nullptr, nullptr);
+      to_q8(mom_sh), to_q8(mom_o), a, opacities, visible, nullptr, nullptr, nullptr, nullptr); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "adam_q8_dense launch");
 }
 
@@ -632,7 +643,7 @@ VS_API vs_status vs_gather_stats(vs_ctx* ctx, uint32_t n, float* refine_norm, fl
     return vs_fail(ctx, VS_ERR_INVALID, "gather_stats: null buffer");
   if (n == 0) return VS_OK;
   stats_kernel<<<vs::div_up(n, 256), 256, 0, ctx->stream>>>(n, refine_norm, vis_count, max_screen, refine_weight,
-                                                            visible, radius);
+                                                            visible, radius); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "gather_stats launch");
 }
 
@@ -641,7 +652,7 @@ VS_API vs_status vs_noise_means(vs_ctx* ctx, uint32_t n, float* transforms, cons
   if (!ctx) return VS_ERR_INVALID;
   if (!transforms || !opacities || !visible) return vs_fail(ctx, VS_ERR_INVALID, "noise_means: null buffer");
   if (n == 0) return VS_OK;
-  noise_kernel<<<vs::div_up(n, 256), 256, 0, ctx->stream>>>(n, transforms, opacities, visible, scale, limit, seed);
+  noise_kernel<<<vs::div_up(n, 256), 256, 0, ctx->stream>>>(n, transforms, opacities, visible, scale, limit, seed); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "noise_means launch");
 }
 

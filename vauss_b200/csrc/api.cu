@@ -135,6 +135,8 @@ VS_API const char* vs_ctx_last_error(const vs_ctx* ctx) { return ctx ? ctx->err.
 
 VS_API uint64_t vs_ctx_workspace_bytes(const vs_ctx* ctx) { return ctx ? ctx->workspace : 0; }
 
+VS_API uint64_t vs_ctx_launch_count(const vs_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
 VS_API vs_status vs_frame_create(vs_ctx* ctx, vs_frame** out) {
   if (!ctx || !out) return VS_ERR_INVALID;
   vs_frame* f = new vs_frame();
@@ -194,20 +196,20 @@ VS_API vs_status vs_frame_copy(vs_frame* f, int32_t field, void* dst_device, uin
                  "frame_copy");
 }
 
-VS_API vs_status vs_render_forward(vs_ctx* ctx, vs_frame* f, const vs_camera* cam, const vs_render_cfg* cfg,
+VS_API vs_status vs_render_project(vs_ctx* ctx, vs_frame* f, const vs_camera* cam, const vs_render_cfg* cfg,
                                    uint32_t num_splats, const float* transforms, const void* sh_coeffs,
-                                   const float* raw_opacities, const float* min_scale, float* out_img,
-                                   float* visible, vs_render_counts* counts_out) {
+                                   const float* raw_opacities, const float* min_scale, vs_render_counts* counts_out) {
   if (!ctx) return VS_ERR_INVALID;
   if (!f || f->ctx != ctx || !cam || !cfg) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: missing frame/camera/config");
   if (cam->img_w == 0 || cam->img_h == 0) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: zero image size");
   if (cfg->sh_degree < 0 || cfg->sh_degree > 3) return vs_fail(ctx, VS_ERR_UNSUPPORTED, "render_forward: SH degree %d (0..3 supported)", cfg->sh_degree);
   if (num_splats > 0 && (!transforms || !sh_coeffs || !raw_opacities)) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: null splat buffer");
   if (cfg->has_min_scale && !min_scale) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: has_min_scale without min_scale");
-  if (!out_img || !visible) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: null output");
   if (num_splats > 0xfffffff0u / 10u) return vs_fail(ctx, VS_ERR_CAPACITY, "render_forward: %u splats exceed 32-bit indexing", num_splats);
   VS_TRY(set_device(ctx));
   f->rendered = false;
+  f->binned = false;
+  f->projected_ok = false;
   f->cfg = *cfg;
   f->u = vs_make_uniforms(*cam, *cfg);
   f->n = num_splats;
@@ -232,15 +234,44 @@ VS_API vs_status vs_render_forward(vs_ctx* ctx, vs_frame* f, const vs_camera* ca
   if (f->I >= 0xffffffffull)
     return vs_fail(ctx, VS_ERR_CAPACITY, "render_forward: %llu intersections exceed 32-bit indexing",
                    (unsigned long long)f->I);
-  VS_TRY(launch_bin(ctx, f));
-  VS_TRY(launch_raster_fwd(ctx, f, out_img, visible));
-  f->rendered = true;
+  f->projected_ok = true;
   if (counts_out) {
     counts_out->num_visible = f->v;
     counts_out->num_tiles = f->T;
     counts_out->num_intersections = f->I;
   }
   return VS_OK;
+}
+
+VS_API vs_status vs_render_bin(vs_ctx* ctx, vs_frame* f) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!f || !f->projected_ok) return vs_fail(ctx, VS_ERR_INVALID, "render_bin: frame has not been projected");
+  VS_TRY(set_device(ctx));
+  VS_TRY(launch_bin(ctx, f));
+  f->binned = true;
+  return VS_OK;
+}
+
+VS_API vs_status vs_render_rasterize(vs_ctx* ctx, vs_frame* f, float* out_img, float* visible) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!f || !f->binned) return vs_fail(ctx, VS_ERR_INVALID, "render_rasterize: frame has not been binned");
+  if (!out_img || !visible) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: null output");
+  VS_TRY(set_device(ctx));
+  VS_TRY(launch_raster_fwd(ctx, f, out_img, visible));
+  f->rendered = true;
+  return VS_OK;
+}
+
+VS_API vs_status vs_render_forward(vs_ctx* ctx, vs_frame* f, const vs_camera* cam, const vs_render_cfg* cfg,
+                                   uint32_t num_splats, const float* transforms, const void* sh_coeffs,
+                                   const float* raw_opacities, const float* min_scale, float* out_img,
+                                   float* visible, vs_render_counts* counts_out) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!out_img || !visible) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: null output");
+  VS_TRY(vs_render_project(ctx, f, cam, cfg, num_splats, transforms, sh_coeffs, raw_opacities, min_scale,
+                           counts_out));
+  VS_TRY(vs_render_bin(ctx, f));
+  return vs_render_rasterize(ctx, f, out_img, visible);
 }
 
 VS_API vs_status vs_loss(vs_ctx* ctx, uint32_t h, uint32_t w, const float* pred, const uint32_t* gt_packed,
@@ -299,6 +330,6 @@ extern "C" VS_API vs_status vs_math_probe(vs_ctx* ctx, int32_t which, const floa
   if (!ctx) return VS_ERR_INVALID;
   if (!x || !y || which < 0 || which > 1) return vs_fail(ctx, VS_ERR_INVALID, "math_probe: bad arguments");
   if (n == 0) return VS_OK;
-  math_probe_kernel<<<vs::div_up(n, 256), 256, 0, ctx->stream>>>(which, x, y, n);
+  math_probe_kernel<<<vs::div_up(n, 256), 256, 0, ctx->stream>>>(which, x, y, n); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "math_probe launch");
 }

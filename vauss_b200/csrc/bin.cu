@@ -148,7 +148,7 @@ vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
   uint32_t* v0 = (uint32_t*)ctx->sort_vals.ptr;
   uint32_t* v1 = v0 + scratch / 4;
   const uint32_t blocks_v = div_up(v, BIN_BLOCK);
-  depth_keys_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const float*)f->depths.ptr, v, k0, v0);
+  depth_keys_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const float*)f->depths.ptr, v, k0, v0); ++ctx->launches;
   bool alt = false;
   VS_TRY(radix_sort_pairs(ctx, k0, v0, k1, v1, v, 32, &alt));
   uint32_t* order = alt ? v1 : v0;
@@ -156,7 +156,7 @@ vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
   // tile counts in depth order, inclusive scan -> emission offsets
   uint32_t* cum = alt ? k0 : k1;  // free half of the key scratch
   gather_counts_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const uint32_t*)f->depth_order.ptr,
-                                                                 (const uint32_t*)f->tile_counts.ptr, v, cum);
+                                                                 (const uint32_t*)f->tile_counts.ptr, v, cum); ++ctx->launches;
   VS_TRY(scan_inclusive_u32(ctx, cum, v, nullptr));
   VS_TRY(vs_ensure(ctx, f->isect_tile, (size_t)(I + 1) * 4));
   VS_TRY(vs_ensure(ctx, f->isect_compact, (size_t)(I + 1) * 4));
@@ -165,7 +165,7 @@ vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
   uint32_t* tkeys = (uint32_t*)f->isect_tile.ptr;
   uint32_t* tvals = (uint32_t*)f->isect_compact.ptr;
   emit_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>(f->u, v, (const uint32_t*)f->depth_order.ptr, cum,
-                                                        (const float4*)f->projected.ptr, tkeys, tvals);
+                                                        (const float4*)f->projected.ptr, tkeys, tvals); ++ctx->launches;
   VS_CUDA(ctx, cudaGetLastError());
   const uint32_t tile_bits = 32u - (uint32_t)__builtin_clz(T | 1u);
   uint32_t* sk = (uint32_t*)ctx->sort_keys.ptr;
@@ -176,6 +176,6 @@ vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
     VS_CUDA(ctx, cudaMemcpyAsync(tvals, sv, (size_t)I * 4, cudaMemcpyDeviceToDevice, ctx->stream));
   }
   tile_ranges_kernel<<<div_up((uint32_t)I, 256), 256, 0, ctx->stream>>>(tkeys, (uint32_t)I, T,
-                                                                        (uint2*)f->tile_ranges.ptr);
+                                                                        (uint2*)f->tile_ranges.ptr); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "bin launch");
 }

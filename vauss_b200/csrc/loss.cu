@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(LT) loss_kernel(uint32_t h, uint32_t w, const 
       if (ry >= HALO && ry < HALO + LB && rx >= HALO && rx < HALO + LB) {
         const float raw = (ct * dt) / (a * b);
         const float val = clampf(raw, -1.0f, 1.0f);
-        const float p1 = s_x[ry + 2 * HALO][rx + 2 * HALO], p2 = s_y[ry + 2 * HALO][rx + 2 * HALO];
+        const float p1 = s_x[ry + HALO][rx + HALO], p2 = s_y[ry + HALO][rx + HALO];
         my_loss = l1_w * fabsf(p1 - p2) + ssim_w * val;
         s_red[(ry - HALO) * LB + (rx - HALO)] = my_loss;
       }
@@ -218,13 +218,11 @@ __global__ void __launch_bounds__(256) loss_total_kernel(const float* __restrict
   if (threadIdx.x == 0) *out = s[0];
 }
 
-bool g_taps_ready = false;
-
 }  // namespace
 
 vs_status launch_loss(vs_ctx* ctx, uint32_t h, uint32_t w, const float* pred, const uint32_t* gt, float l1_w,
                       float ssim_w, float* partials, float* loss_dev, float* dl_dpred) {
-  if (!g_taps_ready) {
+  if (!ctx->taps_ready) {
     // 11-tap Gaussian window, sigma 1.5, normalised (lib.rs:50-63), computed in
     // double and rounded once.
     float taps[11];
@@ -236,7 +234,7 @@ vs_status launch_loss(vs_ctx* ctx, uint32_t h, uint32_t w, const float* pred, co
     }
     for (int i = 0; i < 11; ++i) taps[i] = (float)(t[i] / s);
     VS_CUDA(ctx, cudaMemcpyToSymbol(c_taps, taps, sizeof(taps)));
-    g_taps_ready = true;
+    ctx->taps_ready = true;  // __constant__ memory is per device; one ctx per device
   }
   if (h == 0 || w == 0) return vs_fail(ctx, VS_ERR_INVALID, "loss: empty image");
   const uint32_t tx = div_up(w, 16), ty = div_up(h, 16);
@@ -247,8 +245,11 @@ vs_status launch_loss(vs_ctx* ctx, uint32_t h, uint32_t w, const float* pred, co
   }
   const float rgb_weight = 1.0f / (3.0f * (float)(h * w));
   dim3 grid(tx, ty, 3);
-  loss_kernel<<<grid, LT, 0, ctx->stream>>>(h, w, pred, gt, l1_w, ssim_w, rgb_weight, parts, dl_dpred);
+  loss_kernel<<<grid, LT, 0, ctx->stream>>>(h, w, pred, gt, l1_w, ssim_w, rgb_weight, parts, dl_dpred); ++ctx->launches;
   VS_CUDA(ctx, cudaGetLastError());
-  if (loss_dev) loss_total_kernel<<<1, 256, 0, ctx->stream>>>(parts, 3 * tx * ty, loss_dev);
+  if (loss_dev) {
+    loss_total_kernel<<<1, 256, 0, ctx->stream>>>(parts, 3 * tx * ty, loss_dev);
+    ++ctx->launches;
+  }
   return vs_cuda(ctx, cudaGetLastError(), "loss launch");
 }

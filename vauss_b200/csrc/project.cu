@@ -281,6 +281,6 @@ vs_status launch_project(vs_ctx* ctx, vs_frame* f, const float* transforms, cons
       f->u, n, transforms, sh, raw_opac, min_scale, (uint32_t*)f->compact_from_global.ptr, (float*)f->opacities.ptr,
       (float*)f->max_radius.ptr, (uint32_t*)f->global_from_compact.ptr, (float*)f->depths.ptr,
       (uint32_t*)f->tile_counts.ptr, (float4*)f->projected.ptr, (unsigned long long*)f->lookback.ptr, counters,
-      isect_total, ctx->d_err);
+      isect_total, ctx->d_err); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "project_kernel launch");
 }

@@ -196,6 +196,6 @@ vs_status launch_raster_bwd(vs_ctx* ctx, vs_frame* f, const float* out_img, cons
   raster_bwd_kernel<<<f->T, RB_THREADS, 0, ctx->stream>>>(
       f->u.w, f->u.h, f->u.tbw, f->u.bg[0], f->u.bg[1], f->u.bg[2], (const uint2*)f->tile_ranges.ptr,
       (const uint32_t*)f->tile_used_end.ptr, (const uint32_t*)f->isect_compact.ptr, (const float4*)f->projected.ptr,
-      (const float4*)out_img, (const float4*)v_out, v_combined);
+      (const float4*)out_img, (const float4*)v_out, v_combined); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "raster_bwd launch");
 }

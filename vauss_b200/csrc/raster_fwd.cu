@@ -121,6 +121,6 @@ vs_status launch_raster_fwd(vs_ctx* ctx, vs_frame* f, float* out_img, float* vis
   raster_fwd_kernel<<<f->T, RF_THREADS, 0, ctx->stream>>>(
       f->u.w, f->u.h, f->u.tbw, f->u.bg[0], f->u.bg[1], f->u.bg[2], (const uint2*)f->tile_ranges.ptr,
       (const uint32_t*)f->isect_compact.ptr, (const float4*)f->projected.ptr, (float4*)out_img, visible,
-      (uint32_t*)f->tile_used_end.ptr);
+      (uint32_t*)f->tile_used_end.ptr); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "raster_fwd launch");
 }

@@ -227,12 +227,13 @@ vs_status scan_impl(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total
   const uint32_t chunks = div_up(count, SCAN_CHUNK);
   VS_TRY(vs_ensure(ctx, ctx->scan_sums, (size_t)chunks * sizeof(uint32_t)));
   uint32_t* sums = (uint32_t*)ctx->scan_sums.ptr;
-  scan_reduce_kernel<<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums);
-  scan_sums_kernel<<<1, 1024, 0, ctx->stream>>>(sums, chunks, (unsigned long long*)total_dev);
+  scan_reduce_kernel<<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums); ++ctx->launches;
+  scan_sums_kernel<<<1, 1024, 0, ctx->stream>>>(sums, chunks, (unsigned long long*)total_dev); ++ctx->launches;
   if (inclusive)
     scan_apply_kernel<true><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums);
   else
     scan_apply_kernel<false><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums);
+  ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "scan launch");
 }
 
@@ -255,9 +256,9 @@ vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t
   for (uint32_t shift = 0; shift < key_bits; shift += 8) {
     const uint32_t bits = min(8u, key_bits - shift);
     const uint32_t mask = (1u << bits) - 1u;
-    hist_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist);
+    hist_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
     VS_TRY(scan_impl(ctx, hist, (uint32_t)hist_n, nullptr, false));
-    scatter_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist);
+    scatter_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist); ++ctx->launches;
     VS_CUDA(ctx, cudaGetLastError());
     uint32_t* t = kin; kin = kout; kout = t;
     t = vin; vin = vout; vout = t;

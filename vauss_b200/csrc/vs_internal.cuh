@@ -21,6 +21,8 @@ struct vs_ctx {
   uint32_t* d_err = nullptr;       // device error word (VS_DERR_*)
   uint32_t* h_pinned = nullptr;    // pinned host mirror for small readbacks (16 words)
   uint64_t workspace = 0;          // bytes held by the ctx and its frames
+  uint64_t launches = 0;           // kernels launched through this ctx
+  bool taps_ready = false;         // SSIM window uploaded to this device's constant memory
   // scratch shared by calls on this ctx (stream-ordered reuse)
   DevBuf sort_keys, sort_vals, sort_hist, scan_sums, misc;
 };
@@ -31,7 +33,7 @@ struct vs_frame {
   vs_render_cfg cfg{};
   uint32_t n = 0, v = 0, T = 0;
   uint64_t I = 0;
-  bool rendered = false;
+  bool projected_ok = false, binned = false, rendered = false;
   DevBuf compact_from_global, global_from_compact, depths, tile_counts, projected, depth_order;
   DevBuf isect_tile, isect_compact, tile_ranges, tile_used_end, opacities, max_radius;
   DevBuf lookback, counters;  // projection compaction state

@@ -49,6 +49,10 @@ class Context:
     def workspace_bytes(self) -> int:
         return int(self.lib.vs_ctx_workspace_bytes(self.h))
 
+    @property
+    def launch_count(self) -> int:
+        return int(self.lib.vs_ctx_launch_count(self.h))
+
     def __del__(self):
         try:
             if getattr(self, "h", None):
@@ -152,6 +156,26 @@ def render(camera: Camera, cfg: N.RenderCfg, transforms: torch.Tensor, sh_coeffs
     ctx.check(ctx.lib.vs_render_forward(ctx.h, frame.h, ctypes.byref(cam), ctypes.byref(cfg), n, _ptr(transforms),
                                         _ptr(sh_coeffs), _ptr(raw_opacities), _ptr(min_scale), _ptr(out_img),
                                         _ptr(visible), ctypes.byref(frame.counts)))
+    return RenderOutput(out_img, visible, frame)
+
+
+def render_stages(camera: Camera, cfg: N.RenderCfg, transforms, sh_coeffs, raw_opacities, frame: Frame, out_img,
+                  visible, min_scale=None, hook=None) -> RenderOutput:
+    """``render`` as its three stages (project, bin, rasterize); ``hook(name)``
+    runs after each (the benchmark records CUDA events there)."""
+    ctx = frame.ctx.bind()
+    cam = camera.to_c()
+    ctx.check(ctx.lib.vs_render_project(ctx.h, frame.h, ctypes.byref(cam), ctypes.byref(cfg), transforms.shape[0],
+                                        _ptr(transforms), _ptr(sh_coeffs), _ptr(raw_opacities), _ptr(min_scale),
+                                        ctypes.byref(frame.counts)))
+    if hook:
+        hook("project")
+    ctx.check(ctx.lib.vs_render_bin(ctx.h, frame.h))
+    if hook:
+        hook("bin")
+    ctx.check(ctx.lib.vs_render_rasterize(ctx.h, frame.h, _ptr(out_img), _ptr(visible)))
+    if hook:
+        hook("raster_fwd")
     return RenderOutput(out_img, visible, frame)
 
 
@@ -278,12 +302,12 @@ def step_q8(frame: Frame, cfg: N.RenderCfg, transforms, sh_coeffs, raw_opacities
 
 
 def vjp_dense(frame: Frame, cfg: N.RenderCfg, transforms, sh_coeffs, raw_opacities, v_combined, grads, refine,
-              min_scale=None):
+              min_scale=None, visible=None, vis_accum=None):
     """Accumulates one view's dense gradient rows [N, 10 + 3(d+1)^2 + 1] (multi-view path)."""
     ctx = frame.ctx.bind()
     ctx.check(ctx.lib.vs_vjp_dense(ctx.h, frame.h, ctypes.byref(cfg), transforms.shape[0], _ptr(transforms),
                                    _ptr(sh_coeffs), _ptr(raw_opacities), _ptr(min_scale), _ptr(v_combined),
-                                   _ptr(grads), _ptr(refine)))
+                                   _ptr(grads), _ptr(refine), _ptr(visible), _ptr(vis_accum)))
 
 
 def adam_q8_dense(sh_degree: int, transforms, sh_coeffs, raw_opacities, grads, mom_t: Q8Moments,
