@@ -190,8 +190,10 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    counts = {}
     for k in range(args.warmup):
-        step(k)
+        _, st0 = step(k)
+        counts = {"visible": int(st0.num_visible), "intersections": int(st0.num_intersections)}
     barrier()
     ctx = ops.context(dev)
     launches0 = ctx.launch_count
@@ -266,7 +268,7 @@ def run_ours(args):
                                   "8-bit m+v Adam (block 256)", "splats": splats.num_splats, "width": 1600,
                       "height": 1060, "views_per_step": world, "optimizer": "q8",
                       "parallelism": f"view-parallel x{world}" if world > 1 else "single GPU",
-                      "l2": "inputs larger than L2 (params + moments ~0.9 GB)"},
+                      "l2": "inputs larger than L2 (params + moments ~0.9 GB)", **counts},
            "gpu_launches": int(launches), "clocks": clk.summary()}
     if roofline:
         out["roofline"] = roofline

@@ -292,6 +292,12 @@ def noise_means(transforms, opacities, visible, scale, limit, seed):
     return t
 
 
+def splitmix_shuffle(n: int, seed: int) -> np.ndarray:
+    keys = np.empty(n, np.uint32)
+    lib().or_splitmix_shuffle(_p(keys, U32P), ctypes.c_uint64(n), ctypes.c_uint64(seed))
+    return keys
+
+
 def expf(x):
     x = _f32(x)
     y = np.empty_like(x)

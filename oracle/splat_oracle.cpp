@@ -1284,7 +1284,8 @@ OR_API int or_vjp_dense(const Camera* cam, const RenderCfg* cfg, uint32_t n, con
 //  * v: sqrt(v) as unsigned codes, scale = absmax sqrt(v) / 255;
 //  * both re-encoded with stochastic rounding from vs_mix_hash(index,
 //    step ^ salt): m code = floor(m/scale + u1), r code = floor(r/scale + u2);
-//  * step = (m1 inv1) / max(sqrt(v1 inv2) + eps, |m1 inv1| / 8): the
+//  * scales enter as reciprocals: code = floor(m * (1/scale) + u);
+//  * step = (m1 inv1) / max(sqrt(v1) sqrt(inv2) + eps, |m1 inv1| / 8): the
 //    normalized update is bounded by 8, the bound the reference's packed
 //    geometry codec imposes (src/bwd/kernels/geo_moments.rs:186,192).
 // grads [count] (dense); lr per column: lr_col[index % row_width] * lr.
@@ -1295,6 +1296,7 @@ OR_API int or_adam_q8(size_t count, uint32_t row_width, float* params, const flo
                       const float* lr_col, float lr, float b1, float b2, float inv1, float inv2, float eps,
                       uint32_t seed) {
   const size_t blocks = (count + 255) / 256;
+  const float sqrt_inv2 = sqrtf(inv2);
 #pragma omp parallel for schedule(static)
   for (int64_t bi = 0; bi < (int64_t)blocks; ++bi) {
     const size_t b0 = (size_t)bi * 256;
@@ -1309,11 +1311,12 @@ OR_API int or_adam_q8(size_t count, uint32_t row_width, float* params, const flo
       const float r0 = (float)v_codes[i] * vsc;
       const float m = m0 * b1 + g * (1.0f - b1);
       const float v = r0 * r0 * b2 + g * g * (1.0f - b2);
+      const float r = sqrtf(v);
       const float mh = m * inv1;
-      const float denom = fmaxf(sqrtf(v * inv2) + eps, fabsf(mh) * 0.125f);
+      const float denom = fmaxf(r * sqrt_inv2 + eps, fabsf(mh) * 0.125f);
       params[i] = params[i] - (mh / denom) * (lr_col[col] * lr);
       m1[j] = m;
-      r1[j] = sqrtf(v);
+      r1[j] = r;
     }
     float am = 0.0f, ar = 0.0f;
     for (size_t j = 0; j < nb; ++j) {
@@ -1321,15 +1324,16 @@ OR_API int or_adam_q8(size_t count, uint32_t row_width, float* params, const flo
       ar = fmaxf(ar, r1[j]);
     }
     const float nms = am / 127.0f, nvs = ar / 255.0f;
+    const float inv_ms = nms > 0.0f ? 1.0f / nms : 0.0f, inv_vs = nvs > 0.0f ? 1.0f / nvs : 0.0f;
     m_scales[bi] = nms;
     v_scales[bi] = nvs;
     for (size_t j = 0; j < nb; ++j) {
       const size_t i = b0 + j;
       const uint32_t hsh = vs_mix_hash((uint32_t)i, seed);
-      const float u1 = (float)(hsh >> 16) / 65536.0f, u2 = (float)(hsh & 0xffffu) / 65536.0f;
+      const float u1 = (float)(hsh >> 16) * (1.0f / 65536.0f), u2 = (float)(hsh & 0xffffu) * (1.0f / 65536.0f);
       float qm = 0.0f, qr = 0.0f;
-      if (nms > 0.0f) qm = clampf(floorf(m1[j] / nms + u1), -127.0f, 127.0f);
-      if (nvs > 0.0f) qr = clampf(floorf(r1[j] / nvs + u2), 0.0f, 255.0f);
+      if (nms > 0.0f) qm = clampf(floorf(m1[j] * inv_ms + u1), -127.0f, 127.0f);
+      if (nvs > 0.0f) qr = clampf(floorf(r1[j] * inv_vs + u2), 0.0f, 255.0f);
       m_codes[i] = (uint8_t)((int32_t)qm + 128);
       v_codes[i] = (uint8_t)qr;
     }
@@ -1384,6 +1388,25 @@ OR_API int or_noise_means(uint32_t n, float* transforms, const float* opacities,
     }
   }
   return 0;
+}
+
+// Seeded Fisher-Yates shuffle of 0..n-1 driven by splitmix64, the generator of
+// the reference's >67M-key sort regression test
+// (crates/splat-train-sort/src/lib.rs:358-404).
+OR_API void or_splitmix_shuffle(uint32_t* keys, uint64_t n, uint64_t seed) {
+  for (uint64_t i = 0; i < n; ++i) keys[i] = (uint32_t)i;
+  uint64_t state = seed;
+  for (uint64_t i = n - 1; i >= 1; --i) {
+    state += 0x9E3779B97F4A7C15ull;
+    uint64_t z = state;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    const uint64_t j = z % (i + 1);
+    const uint32_t t = keys[i];
+    keys[i] = keys[j];
+    keys[j] = t;
+  }
 }
 
 // Elementary-function probes for the tests.

@@ -270,6 +270,7 @@ struct Q8T {
 
 struct Q8Args {
   float b1, b2, inv1, inv2, eps;
+  float sqrt_inv2;  // sqrtf(inv2), so sqrt(v inv2) is evaluated as sqrt(v) * sqrt(inv2)
   float lr_t[10];
   float lr_dc, lr_rest, lr_opac, opac_reg;
   uint32_t seed;
@@ -312,8 +313,104 @@ __device__ __forceinline__ void mean_noise(uint32_t i, float opac, float vis, fl
   }
 }
 
+// Per-CTA shared state of the Q8 step: per-splat transforms/opacity gradients,
+// colour gradient and SH bases (the SH gradient is Y_k(dir) * colour, rebuilt
+// per value), mean noise, and the 10 transforms learning rates.
+struct Q8Shared {
+  const float* gt;     // [256][10]
+  const float* go;     // [256]
+  const float* vc;     // [256][3]
+  const float* bas;    // [256][16]
+  const float* noise;  // [256][3]
+  const float* lr_t;   // [10]
+};
+
+// One 256-value block of one parameter tensor, by one warp.  `W` is the
+// tensor's row width (values per splat), `KIND` 0 = transforms, 1 = SH,
+// 2 = opacity.  Lane l owns values jb*256 + 32 j + l (j < 8): each load and
+// store instruction of the warp covers 32 consecutive values.  All loads are
+// issued before any store, so a warp keeps 8 loads of each stream in flight.
+template <bool kDense, uint32_t W, int KIND>
+__device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t vals_here, float* __restrict__ tensor,
+                                         const Q8T& q, size_t t_base, uint32_t salt, const Q8Args& a,
+                                         const Q8Shared& sm, const float* __restrict__ grow, uint32_t width) {
+  float* p = tensor + t_base;
+  uint8_t* mcp = q.mc + t_base;
+  uint8_t* vcp = q.vc + t_base;
+  const size_t blk = t_base / 256u + jb;
+  const float ms = q.ms[blk], vsc = q.vs[blk];
+  const uint32_t v0 = jb * 256u;
+  float pv[8], g[8], m1[8], r1[8];
+  uint32_t mcode[8], vcode[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t li = v0 + (uint32_t)j * 32u + lane;
+    const bool ok = li < vals_here;
+    pv[j] = ok ? p[li] : 0.0f;
+    mcode[j] = ok ? mcp[li] : 128u;
+    vcode[j] = ok ? vcp[li] : 0u;
+    const uint32_t s = li / W, col = li - s * W;
+    if (KIND == 0) {
+      g[j] = ok ? sm.gt[s * 10u + col] : 0.0f;
+    } else if (KIND == 1) {
+      if (kDense) g[j] = ok ? grow[(size_t)s * width + 10u + col] : 0.0f;
+      else g[j] = ok ? sm.vc[s * 3u + col % 3u] * sm.bas[s * 16u + col / 3u] : 0.0f;
+    } else {
+      g[j] = ok ? sm.go[s] : 0.0f;
+    }
+  }
+  float am = 0.0f, ar = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t li = v0 + (uint32_t)j * 32u + lane;
+    const uint32_t s = li / W, col = li - s * W;
+    const float lr = KIND == 0 ? sm.lr_t[col] : (KIND == 1 ? (col / 3u == 0u ? a.lr_dc : a.lr_rest) : a.lr_opac);
+    const float m0 = ((float)mcode[j] - 128.0f) * ms;
+    const float r0 = (float)vcode[j] * vsc;
+    const float gg = g[j];
+    const float m = m0 * a.b1 + gg * (1.0f - a.b1);
+    const float v = r0 * r0 * a.b2 + gg * gg * (1.0f - a.b2);
+    const float r = sqrtf(v);
+    const float mh = m * a.inv1;
+    const float denom = fmaxf(r * a.sqrt_inv2 + a.eps, fabsf(mh) * 0.125f);
+    float pn = pv[j] - (mh / denom) * lr;
+    if (KIND == 0 && col < 3u) pn = pn + sm.noise[s * 3u + col];
+    pv[j] = pn;
+    m1[j] = m;
+    r1[j] = r;
+    if (li < vals_here) {
+      am = fmaxf(am, fabsf(m));
+      ar = fmaxf(ar, r);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    ar = fmaxf(ar, __shfl_xor_sync(0xffffffffu, ar, off));
+  }
+  const float nms = am / 127.0f, nvs = ar / 255.0f;
+  const float inv_ms = nms > 0.0f ? 1.0f / nms : 0.0f, inv_vs = nvs > 0.0f ? 1.0f / nvs : 0.0f;
+  if (lane == 0) {
+    q.ms[blk] = nms;
+    q.vs[blk] = nvs;
+  }
+  const uint32_t hbase = (uint32_t)t_base;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t li = v0 + (uint32_t)j * 32u + lane;
+    if (li >= vals_here) continue;
+    const uint32_t hsh = vs_mix_hash(hbase + li, a.seed ^ salt);
+    const float u1 = (float)(hsh >> 16) * (1.0f / 65536.0f), u2 = (float)(hsh & 0xffffu) * (1.0f / 65536.0f);
+    const float qm = nms > 0.0f ? clampf(floorf(m1[j] * inv_ms + u1), -127.0f, 127.0f) : 0.0f;
+    const float qr = nvs > 0.0f ? clampf(floorf(r1[j] * inv_vs + u2), 0.0f, 255.0f) : 0.0f;
+    p[li] = pv[j];
+    mcp[li] = (uint8_t)((int32_t)qm + 128);
+    vcp[li] = (uint8_t)qr;
+  }
+}
+
 template <bool kDense>
-__global__ void __launch_bounds__(Q8_SPLATS) q8_kernel(
+__global__ void __launch_bounds__(Q8_SPLATS, 3) q8_kernel(
     Uniforms u, uint32_t n, float* __restrict__ transforms, float* __restrict__ sh, float* __restrict__ raw_opac,
     const float* __restrict__ min_scale, const uint32_t* __restrict__ compact_from_global,
     const float* __restrict__ v_combined, const float* __restrict__ grads, Q8T mt, Q8T msh, Q8T mo, Q8Args a,
@@ -324,9 +421,14 @@ __global__ void __launch_bounds__(Q8_SPLATS) q8_kernel(
   __shared__ float s_vc[Q8_SPLATS * 3];
   __shared__ float s_bas[Q8_SPLATS * 16];
   __shared__ float s_noise[Q8_SPLATS * 3];
+  __shared__ float s_lr[10];
 
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   const uint32_t base = blockIdx.x * Q8_SPLATS;
+  if (tid == 0) {
+#pragma unroll
+    for (int k = 0; k < 10; ++k) s_lr[k] = a.lr_t[k];
+  }
   const int nc = (u.sh_degree + 1) * (u.sh_degree + 1);
   const uint32_t wsh = 3u * (uint32_t)nc;
   const uint32_t width = 10u + wsh + 1u;
@@ -409,77 +511,24 @@ __global__ void __launch_bounds__(Q8_SPLATS) q8_kernel(
   const uint32_t splats_here = min(Q8_SPLATS, n - base);
   const uint32_t nb_t = div_up(splats_here * 10u, 256u);
   const uint32_t nb_sh = div_up(splats_here * wsh, 256u);
-  const uint32_t nb_o = 1u;
-  const uint32_t total_blocks = nb_t + nb_sh + nb_o;
+  const uint32_t total_blocks = nb_t + nb_sh + 1u;
+  const Q8Shared sm{s_gt, s_go, s_vc, s_bas, s_noise, s_lr};
+  const float* grow = kDense ? grads + (size_t)base * width : nullptr;
   for (uint32_t job = warp; job < total_blocks; job += Q8_WARPS) {
-    uint32_t tensor, jb, w;
-    if (job < nb_t) { tensor = 0; jb = job; w = 10u; }
-    else if (job < nb_t + nb_sh) { tensor = 1; jb = job - nb_t; w = wsh; }
-    else { tensor = 2; jb = 0; w = 1u; }
-    float* params = tensor == 0 ? transforms : (tensor == 1 ? sh : raw_opac);
-    const Q8T q = tensor == 0 ? mt : (tensor == 1 ? msh : mo);
-    const uint32_t salt = tensor == 0 ? SALT_T : (tensor == 1 ? SALT_SH : SALT_O);
-    const size_t t_base = (size_t)base * w;        // first value of this CTA in the tensor
-    const size_t count = (size_t)n * w;            // tensor size
-    const size_t v0 = t_base + (size_t)jb * 256u;  // first value of this block
-    const size_t blk = v0 / 256u;
-    const float ms = q.ms[blk], vsc = q.vs[blk];
-    float m1[8], r1[8];
-    float am = 0.0f, ar = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const size_t i = v0 + (size_t)j * 32 + lane;
-      m1[j] = 0.0f;
-      r1[j] = 0.0f;
-      if (i >= count) continue;
-      const uint32_t s = (uint32_t)(i / w) - base;
-      const uint32_t col = (uint32_t)(i % w);
-      float g, lr;
-      if (tensor == 0) {
-        g = s_gt[s * 10 + col];
-        lr = a.lr_t[col];
-      } else if (tensor == 1) {
-        g = kDense ? grads[(size_t)(base + s) * width + 10 + col] : s_vc[s * 3 + col % 3] * s_bas[s * 16 + col / 3];
-        lr = (col / 3 == 0) ? a.lr_dc : a.lr_rest;
-      } else {
-        g = s_go[s];
-        lr = a.lr_opac;
+    if (job < nb_t) {
+      q8_block<kDense, 10, 0>(lane, job, splats_here * 10u, transforms, mt, (size_t)base * 10u, SALT_T, a, sm,
+                              grow, width);
+    } else if (job < nb_t + nb_sh) {
+      const uint32_t jb = job - nb_t;
+      const size_t tb = (size_t)base * wsh;
+      switch (u.sh_degree) {
+        case 3: q8_block<kDense, 48, 1>(lane, jb, splats_here * 48u, sh, msh, tb, SALT_SH, a, sm, grow, width); break;
+        case 2: q8_block<kDense, 27, 1>(lane, jb, splats_here * 27u, sh, msh, tb, SALT_SH, a, sm, grow, width); break;
+        case 1: q8_block<kDense, 12, 1>(lane, jb, splats_here * 12u, sh, msh, tb, SALT_SH, a, sm, grow, width); break;
+        default: q8_block<kDense, 3, 1>(lane, jb, splats_here * 3u, sh, msh, tb, SALT_SH, a, sm, grow, width); break;
       }
-      const float m0 = ((float)q.mc[i] - 128.0f) * ms;
-      const float r0 = (float)q.vc[i] * vsc;
-      const float m = m0 * a.b1 + g * (1.0f - a.b1);
-      const float v = r0 * r0 * a.b2 + g * g * (1.0f - a.b2);
-      const float mh = m * a.inv1;
-      const float denom = fmaxf(sqrtf(v * a.inv2) + a.eps, fabsf(mh) * 0.125f);
-      float p = params[i] - (mh / denom) * lr;
-      if (tensor == 0 && col < 3) p = p + s_noise[s * 3 + col];
-      params[i] = p;
-      m1[j] = m;
-      r1[j] = sqrtf(v);
-      am = fmaxf(am, fabsf(m));
-      ar = fmaxf(ar, r1[j]);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
-      ar = fmaxf(ar, __shfl_xor_sync(0xffffffffu, ar, off));
-    }
-    const float nms = am / 127.0f, nvs = ar / 255.0f;
-    if (lane == 0) {
-      q.ms[blk] = nms;
-      q.vs[blk] = nvs;
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const size_t i = v0 + (size_t)j * 32 + lane;
-      if (i >= count) continue;
-      const uint32_t hsh = vs_mix_hash((uint32_t)i, a.seed ^ salt);
-      const float u1 = (float)(hsh >> 16) / 65536.0f, u2 = (float)(hsh & 0xffffu) / 65536.0f;
-      float qm = 0.0f, qr = 0.0f;
-      if (nms > 0.0f) qm = clampf(floorf(m1[j] / nms + u1), -127.0f, 127.0f);
-      if (nvs > 0.0f) qr = clampf(floorf(r1[j] / nvs + u2), 0.0f, 255.0f);
-      q.mc[i] = (uint8_t)((int32_t)qm + 128);
-      q.vc[i] = (uint8_t)qr;
+    } else {
+      q8_block<kDense, 1, 2>(lane, 0, splats_here, raw_opac, mo, (size_t)base, SALT_O, a, sm, grow, width);
     }
   }
 }
@@ -517,6 +566,7 @@ Q8Args to_args(const vs_q8_cfg& c) {
   a.lr_dc = c.lr_sh_dc; a.lr_rest = c.lr_sh_rest; a.lr_opac = c.lr_opac; a.opac_reg = c.opac_reg;
   a.seed = c.seed;
   a.noise_scale = c.noise_scale; a.noise_limit = c.noise_limit; a.noise_seed = c.noise_seed;
+  a.sqrt_inv2 = sqrtf(c.inv2);
   return a;
 }
 

@@ -148,7 +148,7 @@ __device__ __forceinline__ void lb_store(unsigned long long* p, unsigned long lo
   r.store(v, cuda::memory_order_release);
 }
 
-__global__ void __launch_bounds__(PROJ_BLOCK) project_kernel(
+__global__ void __launch_bounds__(PROJ_BLOCK, 3) project_kernel(
     Uniforms u, uint32_t n, const float* __restrict__ transforms, const void* __restrict__ sh,
     const float* __restrict__ raw_opac, const float* __restrict__ min_scale, uint32_t* __restrict__ compact_from_global,
     float* __restrict__ opacities, float* __restrict__ max_radius, uint32_t* __restrict__ global_from_compact,
@@ -209,41 +209,54 @@ __global__ void __launch_bounds__(PROJ_BLOCK) project_kernel(
   for (int off = 16; off > 0; off >>= 1) hsum += __shfl_xor_sync(0xffffffffu, hsum, off);
   if (lane == 0 && hsum) atomicAdd(&s_isect, hsum);
   __syncthreads();
-  if (tid == 0) {
+  if (warp == 0) {
     uint32_t total = 0;
-    for (uint32_t w = 0; w < PROJ_BLOCK / 32; ++w) {
-      const uint32_t c = s_warp_cnt[w];
-      s_warp_cnt[w] = total;
-      total += c;
+    if (lane == 0) {
+      for (uint32_t w = 0; w < PROJ_BLOCK / 32; ++w) {
+        const uint32_t c = s_warp_cnt[w];
+        s_warp_cnt[w] = total;
+        total += c;
+      }
+      if (s_isect) atomicAdd(isect_total, s_isect);
+      lb_store(&lookback[bid], ((bid == 0 ? 2ull : 1ull) << 32) | total);
     }
-    if (s_isect) atomicAdd(isect_total, s_isect);
-    // decoupled look-back over the preceding blocks
+    total = __shfl_sync(0xffffffffu, total, 0);
+    // Decoupled look-back, a warp at a time: lane l reads the status of block
+    // hi - l; the nearest published inclusive prefix ends the walk.  Positions
+    // before block 0 read as an inclusive prefix of 0.
     uint32_t exclusive = 0;
-    if (bid == 0) {
-      lb_store(&lookback[0], (2ull << 32) | total);
-    } else {
-      lb_store(&lookback[bid], (1ull << 32) | total);
-      int64_t p = (int64_t)bid - 1;
+    if (bid > 0) {
+      int64_t hi = (int64_t)bid - 1;
       uint32_t spins = 0;
-      while (p >= 0) {
-        const unsigned long long s = lb_load(&lookback[p]);
+      while (true) {
+        const int64_t p = hi - (int64_t)lane;
+        const unsigned long long s = p >= 0 ? lb_load(&lookback[p]) : (2ull << 32);
         const uint32_t flag = (uint32_t)(s >> 32);
-        if (flag == 0u) {
+        const uint32_t incl = __ballot_sync(0xffffffffu, flag == 2u);
+        const uint32_t pending = __ballot_sync(0xffffffffu, flag == 0u);
+        const uint32_t first = incl ? (uint32_t)(__ffs(incl) - 1) : 32u;
+        const uint32_t needed = first >= 31u ? 0xffffffffu : ((2u << first) - 1u);
+        if (pending & needed) {
           if (++spins > SPIN_LIMIT) {
-            atomicOr(err, VS_DERR_WAIT);
+            if (lane == 0) atomicOr(err, VS_DERR_WAIT);
             break;
           }
-          if (spins > 64) __nanosleep(64);
+          if (spins > 32) __nanosleep(64);
           continue;
         }
-        exclusive += (uint32_t)s;
-        if (flag == 2u) break;
-        --p;
+        uint32_t part = lane <= first ? (uint32_t)s : 0u;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+        exclusive += part;
+        if (first < 32u) break;
+        hi -= 32;
       }
-      lb_store(&lookback[bid], (2ull << 32) | (exclusive + total));
+      if (lane == 0) lb_store(&lookback[bid], (2ull << 32) | (exclusive + total));
     }
-    s_block_off = exclusive;
-    if (bid == gridDim.x - 1) counters[1] = exclusive + total;
+    if (lane == 0) {
+      s_block_off = exclusive;
+      if (bid == gridDim.x - 1) counters[1] = exclusive + total;
+    }
   }
   __syncthreads();
   if (g >= n) return;
