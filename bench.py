@@ -43,7 +43,7 @@ N_TARGETS = 8
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--splats", type=int, default=N_SPLATS)
@@ -75,17 +75,23 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            t0 = time.monotonic()  # the sampler needs a moment to come up
+            while not self.lines and time.monotonic() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
 
+    def mark(self, which):
+        setattr(self, which, time.monotonic())
+
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.monotonic(), line.strip()))
 
     def __exit__(self, *a):
         if self.proc:
@@ -97,21 +103,23 @@ class ClockSampler:
 
     def summary(self):
         rows = []
-        for l in self.lines:
+        t0, t1 = getattr(self, "start", None), getattr(self, "stop", None)
+        for ts, l in self.lines:
             parts = [x.strip() for x in l.split(",")]
             if len(parts) < 7:
                 continue
             try:
-                rows.append((float(parts[0]), float(parts[1]), float(parts[2]), parts[3:7]))
+                rows.append((float(parts[0]), float(parts[1]), float(parts[2]), parts[3:7], ts))
             except ValueError:
                 continue
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        loaded = [r for r in rows if r[2] > 200.0] or rows
+        inside = [r for r in rows if t0 is not None and t1 is not None and t0 <= r[4] <= t1]
+        loaded = inside or [r for r in rows if r[2] > 200.0] or rows
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in loaded for i in range(4) if r[3][i].lower() == "active"})
         return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(loaded)}
+                "reasons": reasons, "samples": len(loaded), "in_timed_region": bool(inside)}
 
 
 # ------------------------------------------------------------ workloads ----
@@ -203,11 +211,13 @@ def run_ours(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(gpu_id) as clk:
         barrier()
+        clk.mark("start")
         e0.record(stream)
         for k in range(args.steps):
             step(args.warmup + k)
         e1.record(stream)
         barrier()
+        clk.mark("stop")
     ms = e0.elapsed_time(e1)
     launches = (ctx.launch_count - launches0) // max(args.steps, 1)
     t = torch.tensor([ms], dtype=torch.float64, device=dev)

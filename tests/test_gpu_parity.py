@@ -275,6 +275,29 @@ def test_q8_fused_step_bit_exact(rendered):
     assert_bits_equal(_np(ms_), ref["proj"]["max_radius"], "max screen radius")
 
 
+@pytest.mark.parametrize("deg", [1, 2])
+def test_q8_fused_step_other_sh_degrees(cuda, deg):
+    sp, cams = medium_scene(seed=40 + deg, n=9_000, sh_degree=deg)
+    cam = cams[0]
+    ref, out, cfg, cfg_o = _render_both(sp, cam, cuda)
+    rng = np.random.default_rng(deg)
+    n, v = sp.n, ref["proj"]["num_visible"]
+    vc = (1e-3 * rng.standard_normal((v, 10))).astype(np.float32)
+    mom = dict(t=_q8_host(n * 10, rng), sh=_q8_host(sp.sh.size, rng), o=_q8_host(n, rng))
+    lr_t = np.float32([1e-3] * 3 + [2e-3] * 4 + [5e-3] * 3)
+    want = _oracle_q8_step(sp, cam, cfg_o, ref["proj"], vc, ref["visible"], mom, 2, lr_t, 2.5e-3, 2.5e-4, 5e-2, 0.0,
+                           None)
+    t, sh, o = _t(sp.transforms, cuda), _t(sp.sh, cuda), _t(sp.raw_opac, cuda)
+    mt, msh, mo = _q8_dev(mom["t"], cuda), _q8_dev(mom["sh"], cuda), _q8_dev(mom["o"], cuda)
+    ops.step_q8(out.frame, cfg, t, sh, o, _t(vc, cuda), mt, msh, mo, ops.q8_cfg(2, lr_t, 2.5e-3, 2.5e-4, 5e-2))
+    torch.cuda.synchronize()
+    assert_bits_equal(_np(t), want["transforms"], "transforms")
+    assert_bits_equal(_np(sh).reshape(n, -1), want["sh"][0], "sh")
+    assert_bits_equal(_np(msh.m_codes), want["sh"][1], "sh m codes")
+    assert_bits_equal(_np(msh.v_scales), want["sh"][4], "sh v scales")
+    assert_bits_equal(_np(o), want["o"][0], "raw_opac")
+
+
 def test_dense_vjp_and_q8_dense_bit_exact(rendered):
     sp, ref, out, dev, cam = rendered["sp"], rendered["ref"], rendered["out"], rendered["dev"], rendered["cam"]
     rng = np.random.default_rng(4)

@@ -255,7 +255,7 @@ VS_API vs_status vs_render_bin(vs_ctx* ctx, vs_frame* f) {
 VS_API vs_status vs_render_rasterize(vs_ctx* ctx, vs_frame* f, float* out_img, float* visible) {
   if (!ctx) return VS_ERR_INVALID;
   if (!f || !f->binned) return vs_fail(ctx, VS_ERR_INVALID, "render_rasterize: frame has not been binned");
-  if (!out_img || !visible) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: null output");
+  if (!out_img || (!visible && f->n > 0)) return vs_fail(ctx, VS_ERR_INVALID, "render_rasterize: null output");
   VS_TRY(set_device(ctx));
   VS_TRY(launch_raster_fwd(ctx, f, out_img, visible));
   f->rendered = true;
@@ -267,7 +267,7 @@ VS_API vs_status vs_render_forward(vs_ctx* ctx, vs_frame* f, const vs_camera* ca
                                    const float* raw_opacities, const float* min_scale, float* out_img,
                                    float* visible, vs_render_counts* counts_out) {
   if (!ctx) return VS_ERR_INVALID;
-  if (!out_img || !visible) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: null output");
+  if (!out_img || (!visible && num_splats > 0)) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: null output");
   VS_TRY(vs_render_project(ctx, f, cam, cfg, num_splats, transforms, sh_coeffs, raw_opacities, min_scale,
                            counts_out));
   VS_TRY(vs_render_bin(ctx, f));

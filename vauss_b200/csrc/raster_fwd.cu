@@ -116,7 +116,7 @@ __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
 }  // namespace
 
 vs_status launch_raster_fwd(vs_ctx* ctx, vs_frame* f, float* out_img, float* visible) {
-  VS_CUDA(ctx, cudaMemsetAsync(visible, 0, (size_t)f->n * 4, ctx->stream));
+  if (f->n > 0) VS_CUDA(ctx, cudaMemsetAsync(visible, 0, (size_t)f->n * 4, ctx->stream));
   if (f->T == 0) return VS_OK;
   raster_fwd_kernel<<<f->T, RF_THREADS, 0, ctx->stream>>>(
       f->u.w, f->u.h, f->u.tbw, f->u.bg[0], f->u.bg[1], f->u.bg[2], (const uint2*)f->tile_ranges.ptr,
