@@ -233,6 +233,22 @@ VS_API vs_status vs_noise_means(vs_ctx* ctx, uint32_t n, float* transforms, cons
 /* Stable LSD radix sort of (key, value) u32 pairs on bits [0, key_bits). */
 VS_API vs_status vs_radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* values, uint32_t count,
                                      uint32_t key_bits);
+/* The same sort with no device allocation inside the call.  It has no
+ * counterpart in the reference, whose sort always obtains its temporaries
+ * from its backend.  It is for hosts that cannot allocate at the point of the
+ * call: ones that keep device memory inside a fixed budget they manage
+ * themselves, or that must not let an allocation synchronise or fail
+ * mid-stream.  All temporaries live in one statically sized array of the
+ * library's device image (about 8.5 MB, held on every device that loads the
+ * library until exit); count is limited to VS_SORT_STATIC_MAX_KEYS and larger
+ * counts return VS_ERR_CAPACITY.  The first call on a device looks the array
+ * up (cudaGetSymbolAddress, which can load the module): make that call before
+ * any stream capture on that device.  Nothing in the array has to start at
+ * zero.  The array is shared by all calls on a device, so calls that overlap
+ * on the GPU (other streams or threads) race; the caller serialises them. */
+#define VS_SORT_STATIC_MAX_KEYS (1u << 20)
+VS_API vs_status vs_radix_sort_pairs_static(vs_ctx* ctx, uint32_t* keys, uint32_t* values, uint32_t count,
+                                            uint32_t key_bits);
 /* Inclusive prefix sum of u32 in place; the total (u64) to *total_dev if non-NULL. */
 VS_API vs_status vs_scan_inclusive(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev);
 /* Elementwise vs_expf / vs_logf (the shared deterministic functions). */

@@ -98,6 +98,7 @@ _SIGS = {
     "vs_noise_means": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, ctypes.c_float, ctypes.c_float, ctypes.c_uint32],
                        ctypes.c_int),
     "vs_radix_sort_pairs": ([c_vp, c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32], ctypes.c_int),
+    "vs_radix_sort_pairs_static": ([c_vp, c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32], ctypes.c_int),
     "vs_scan_inclusive": ([c_vp, c_vp, ctypes.c_uint32, c_vp], ctypes.c_int),
     "vs_math_probe": ([c_vp, ctypes.c_int32, c_vp, c_vp, ctypes.c_uint32], ctypes.c_int),
 }

@@ -12,6 +12,8 @@
 // keys stably (every warp ranks a contiguous 256-key slice with match_any,
 // warps are combined through per-digit counts), scatters them into shared
 // memory in digit order and writes contiguous per-digit runs to global memory.
+#include <mutex>
+
 #include "vs_internal.cuh"
 
 namespace {
@@ -263,6 +265,105 @@ vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t
     uint32_t* t = kin; kin = kout; kout = t;
     t = vin; vin = vout; vout = t;
     *result_in_alt = !*result_in_alt;
+  }
+  return VS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Sort with file-scope scratch: vs_radix_sort_pairs_static.
+//
+// For callers that may not allocate device memory during the call: a host
+// that runs the sort inside a fixed device-memory budget it manages itself, or
+// at a point where an allocation would synchronise the device or be refused.
+// Every temporary lives in one statically sized __device__ array that is part
+// of the library's device image, so a call launches kernels and issues at most
+// two device-to-device copies, nothing else.  Limits and rules:
+//   - at most VS_SORT_STATIC_MAX_KEYS (2^20) pairs; larger counts are rejected
+//     with VS_ERR_CAPACITY before anything is launched;
+//   - the first call on each device looks the array up with
+//     cudaGetSymbolAddress (which can load the module); make that first call
+//     before any stream capture on that device;
+//   - nothing in the array needs to start at zero: every pass writes its whole
+//     histogram and all chunk sums before reading them;
+//   - the array is shared by every call on a device, so two calls that may run
+//     at the same time on the GPU (other streams, other threads) race.
+namespace {
+
+constexpr uint32_t STATIC_MAX_KEYS = 1u << 20;
+constexpr uint32_t STATIC_TILES = STATIC_MAX_KEYS / SORT_TILE;                 // 512
+constexpr uint32_t STATIC_HIST = RADIX * STATIC_TILES;                         // 131072
+constexpr uint32_t STATIC_SUMS = (STATIC_HIST + SCAN_CHUNK - 1) / SCAN_CHUNK;  // 32
+constexpr size_t STATIC_WORDS = 2ull * STATIC_MAX_KEYS + STATIC_HIST + 64;
+static_assert(STATIC_SUMS <= 64, "chunk-sum slots");
+
+static __device__ __align__(256) uint32_t g_sort_scratch[STATIC_WORDS];
+
+std::mutex g_scratch_mu;
+uint32_t* g_scratch_ptr[256] = {};
+
+// Device address of g_sort_scratch on ctx's device (looked up once per device,
+// with that device current).
+vs_status static_scratch(vs_ctx* ctx, uint32_t** out) {
+  if (ctx->device < 0 || ctx->device >= 256)
+    return vs_fail(ctx, VS_ERR_INVALID, "radix_sort_static: device %d", ctx->device);
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_ptr[ctx->device]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_sort_scratch);
+    if (e != cudaSuccess || !p)
+      return vs_fail(ctx, VS_ERR_CUDA, "radix_sort_static: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_scratch_ptr[ctx->device] = (uint32_t*)p;
+  }
+  *out = g_scratch_ptr[ctx->device];
+  return VS_OK;
+}
+
+// Exclusive scan of `count` words in place with caller-provided chunk sums.
+void scan_exclusive_into(vs_ctx* ctx, uint32_t* data, uint32_t count, uint32_t* sums) {
+  const uint32_t chunks = div_up(count, SCAN_CHUNK);
+  scan_reduce_kernel<<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums); ++ctx->launches;
+  scan_sums_kernel<<<1, 1024, 0, ctx->stream>>>(sums, chunks, nullptr); ++ctx->launches;
+  scan_apply_kernel<false><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums); ++ctx->launches;
+}
+
+}  // namespace
+
+extern "C" VS_API vs_status vs_radix_sort_pairs_static(vs_ctx* ctx, uint32_t* keys, uint32_t* values,
+                                                       uint32_t count, uint32_t key_bits) {
+  if (!ctx) return VS_ERR_INVALID;
+  if ((!keys || !values) && count) return vs_fail(ctx, VS_ERR_INVALID, "radix_sort_static: null buffer");
+  if (key_bits > 32) return vs_fail(ctx, VS_ERR_INVALID, "radix_sort_static: key_bits %u > 32", key_bits);
+  if (count > STATIC_MAX_KEYS)
+    return vs_fail(ctx, VS_ERR_CAPACITY, "radix_sort_static: %u pairs exceed the static scratch limit of %u", count,
+                   STATIC_MAX_KEYS);
+  VS_TRY(vs_cuda(ctx, cudaSetDevice(ctx->device), "cudaSetDevice"));
+  uint32_t* scratch = nullptr;
+  VS_TRY(static_scratch(ctx, &scratch));
+  if (count <= 1 || key_bits == 0) return VS_OK;
+  const uint32_t tiles = div_up(count, SORT_TILE);
+  const uint32_t hist_n = RADIX * tiles;
+  uint32_t* keys_alt = scratch;
+  uint32_t* vals_alt = scratch + STATIC_MAX_KEYS;
+  uint32_t* hist = scratch + 2 * STATIC_MAX_KEYS;
+  uint32_t* sums = hist + STATIC_HIST;
+  uint32_t *kin = keys, *vin = values, *kout = keys_alt, *vout = vals_alt;
+  bool in_alt = false;
+  for (uint32_t shift = 0; shift < key_bits; shift += 8) {
+    const uint32_t bits = min(8u, key_bits - shift);
+    const uint32_t mask = (1u << bits) - 1u;
+    hist_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
+    scan_exclusive_into(ctx, hist, hist_n, sums);
+    scatter_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist); ++ctx->launches;
+    VS_TRY(vs_cuda(ctx, cudaGetLastError(), "radix_sort_static launch"));
+    uint32_t* t = kin; kin = kout; kout = t;
+    t = vin; vin = vout; vout = t;
+    in_alt = !in_alt;
+  }
+  if (in_alt) {
+    VS_TRY(vs_cuda(ctx, cudaMemcpyAsync(keys, keys_alt, (size_t)count * 4, cudaMemcpyDeviceToDevice, ctx->stream),
+                   "radix_sort_static copy"));
+    VS_TRY(vs_cuda(ctx, cudaMemcpyAsync(values, vals_alt, (size_t)count * 4, cudaMemcpyDeviceToDevice, ctx->stream),
+                   "radix_sort_static copy"));
   }
   return VS_OK;
 }
