@@ -327,9 +327,11 @@ struct Q8Shared {
 
 // One 256-value block of one parameter tensor, by one warp.  `W` is the
 // tensor's row width (values per splat), `KIND` 0 = transforms, 1 = SH,
-// 2 = opacity.  Lane l owns values jb*256 + 32 j + l (j < 8): each load and
-// store instruction of the warp covers 32 consecutive values.  All loads are
-// issued before any store, so a warp keeps 8 loads of each stream in flight.
+// 2 = opacity.  Lane l owns the four consecutive values jb*256 + 128 h + 4 l
+// + e (h < 2, e < 4), so a full block moves with two 16-byte parameter loads
+// and two 4-byte loads per code stream per lane; all loads are issued before
+// any arithmetic.  A block that runs past the tensor's end (only in the last
+// CTA) takes guarded scalar accesses instead.
 template <bool kDense, uint32_t W, int KIND>
 __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t vals_here, float* __restrict__ tensor,
                                          const Q8T& q, size_t t_base, uint32_t salt, const Q8Args& a,
@@ -340,45 +342,84 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
   const size_t blk = t_base / 256u + jb;
   const float ms = q.ms[blk], vsc = q.vs[blk];
   const uint32_t v0 = jb * 256u;
-  float pv[8], g[8], m1[8], r1[8];
-  uint32_t mcode[8], vcode[8];
+  const bool full = v0 + 256u <= vals_here;
+  float pv[8], g[8], lr[8], nz[8];
+  uint32_t mw[2], vw[2];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t li = v0 + (uint32_t)j * 32u + lane;
-    const bool ok = li < vals_here;
-    pv[j] = ok ? p[li] : 0.0f;
-    mcode[j] = ok ? mcp[li] : 128u;
-    vcode[j] = ok ? vcp[li] : 0u;
-    const uint32_t s = li / W, col = li - s * W;
-    if (KIND == 0) {
-      g[j] = ok ? sm.gt[s * 10u + col] : 0.0f;
-    } else if (KIND == 1) {
-      if (kDense) g[j] = ok ? grow[(size_t)s * width + 10u + col] : 0.0f;
-      else g[j] = ok ? sm.vc[s * 3u + col % 3u] * sm.bas[s * 16u + col / 3u] : 0.0f;
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t li0 = v0 + 128u * h + 4u * lane;
+    if (full) {
+      const float4 x = *reinterpret_cast<const float4*>(p + li0);
+      pv[4 * h] = x.x; pv[4 * h + 1] = x.y; pv[4 * h + 2] = x.z; pv[4 * h + 3] = x.w;
+      mw[h] = *reinterpret_cast<const uint32_t*>(mcp + li0);
+      vw[h] = *reinterpret_cast<const uint32_t*>(vcp + li0);
     } else {
-      g[j] = ok ? sm.go[s] : 0.0f;
+      mw[h] = 0x80808080u;
+      vw[h] = 0u;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t li = li0 + (uint32_t)e;
+        const bool ok = li < vals_here;
+        pv[4 * h + e] = ok ? p[li] : 0.0f;
+        if (ok) {
+          mw[h] = (mw[h] & ~(0xffu << (8 * e))) | ((uint32_t)mcp[li] << (8 * e));
+          vw[h] |= (uint32_t)vcp[li] << (8 * e);
+        }
+      }
+    }
+    // gradient, learning rate and mean noise of the four values
+    uint32_t s = li0 / W, col = li0 - s * W;
+    uint32_t c3 = col / 3u, r3 = col - 3u * c3;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint32_t li = li0 + (uint32_t)e;
+      const bool ok = full || li < vals_here;
+      const int k = 4 * h + e;
+      nz[k] = 0.0f;
+      if (KIND == 0) {
+        g[k] = ok ? sm.gt[li] : 0.0f;
+        lr[k] = sm.lr_t[col];
+        if (col < 3u) nz[k] = ok ? sm.noise[s * 3u + col] : 0.0f;
+      } else if (KIND == 1) {
+        if (kDense) g[k] = ok ? grow[(size_t)s * width + 10u + col] : 0.0f;
+        else g[k] = ok ? sm.vc[s * 3u + r3] * sm.bas[s * 16u + c3] : 0.0f;
+        lr[k] = c3 == 0u ? a.lr_dc : a.lr_rest;
+      } else {
+        g[k] = ok ? sm.go[li] : 0.0f;
+        lr[k] = a.lr_opac;
+      }
+      if (++col == W) {
+        col = 0u;
+        ++s;
+        c3 = 0u;
+        r3 = 0u;
+      } else if (++r3 == 3u) {
+        r3 = 0u;
+        ++c3;
+      }
     }
   }
+  float m1[8], r1[8];
   float am = 0.0f, ar = 0.0f;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t li = v0 + (uint32_t)j * 32u + lane;
-    const uint32_t s = li / W, col = li - s * W;
-    const float lr = KIND == 0 ? sm.lr_t[col] : (KIND == 1 ? (col / 3u == 0u ? a.lr_dc : a.lr_rest) : a.lr_opac);
-    const float m0 = ((float)mcode[j] - 128.0f) * ms;
-    const float r0 = (float)vcode[j] * vsc;
-    const float gg = g[j];
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t li = v0 + 128u * (uint32_t)(k >> 2) + 4u * lane + (uint32_t)(k & 3);
+    // byte b as a float: 2^23 + b has b in its low mantissa bits (exact)
+    const uint32_t mb = (mw[k >> 2] >> (8 * (k & 3))) & 0xffu, vb = (vw[k >> 2] >> (8 * (k & 3))) & 0xffu;
+    const float m0 = (__uint_as_float(0x4B000000u | mb) - 8388736.0f) * ms;  // (b - 128) * scale
+    const float r0 = (__uint_as_float(0x4B000000u | vb) - 8388608.0f) * vsc;
+    const float gg = g[k];
     const float m = m0 * a.b1 + gg * (1.0f - a.b1);
     const float v = r0 * r0 * a.b2 + gg * gg * (1.0f - a.b2);
-    const float r = sqrtf(v);
+    const float r = sqrt_rn(v);
     const float mh = m * a.inv1;
     const float denom = fmaxf(r * a.sqrt_inv2 + a.eps, fabsf(mh) * 0.125f);
-    float pn = pv[j] - (mh / denom) * lr;
-    if (KIND == 0 && col < 3u) pn = pn + sm.noise[s * 3u + col];
-    pv[j] = pn;
-    m1[j] = m;
-    r1[j] = r;
-    if (li < vals_here) {
+    float pn = pv[k] - div_rn(mh, denom) * lr[k];
+    if (KIND == 0) pn = pn + nz[k];
+    pv[k] = pn;
+    m1[k] = m;
+    r1[k] = r;
+    if (full || li < vals_here) {
       am = fmaxf(am, fabsf(m));
       ar = fmaxf(ar, r);
     }
@@ -396,16 +437,43 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
   }
   const uint32_t hbase = (uint32_t)t_base;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const uint32_t li = v0 + (uint32_t)j * 32u + lane;
-    if (li >= vals_here) continue;
-    const uint32_t hsh = vs_mix_hash(hbase + li, a.seed ^ salt);
-    const float u1 = (float)(hsh >> 16) * (1.0f / 65536.0f), u2 = (float)(hsh & 0xffffu) * (1.0f / 65536.0f);
-    const float qm = nms > 0.0f ? clampf(floorf(m1[j] * inv_ms + u1), -127.0f, 127.0f) : 0.0f;
-    const float qr = nvs > 0.0f ? clampf(floorf(r1[j] * inv_vs + u2), 0.0f, 255.0f) : 0.0f;
-    p[li] = pv[j];
-    mcp[li] = (uint8_t)((int32_t)qm + 128);
-    vcp[li] = (uint8_t)qr;
+  for (int h = 0; h < 2; ++h) {
+    const uint32_t li0 = v0 + 128u * h + 4u * lane;
+    uint32_t mo = 0u, vo = 0u;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int k = 4 * h + e;
+      const uint32_t hsh = vs_mix_hash(hbase + li0 + (uint32_t)e, a.seed ^ salt);
+      // h / 65536 for a 16-bit h, exactly: (1 + h 2^-16) - 1
+      const float u1 = __uint_as_float(0x3F800000u | ((hsh >> 16) << 7)) - 1.0f;
+      const float u2 = __uint_as_float(0x3F800000u | ((hsh & 0xffffu) << 7)) - 1.0f;
+      // clamp(floor(x), lo, hi) = floor(clamp(x, lo, hi)) for integer bounds
+      // (NaN clamps to lo either way); floor of |y| < 2^22 is the low
+      // mantissa of y + 1.5 2^23 rounded toward -inf.
+      const uint32_t qm = nms > 0.0f
+          ? __float_as_uint(__fadd_rd(clampf(m1[k] * inv_ms + u1, -127.0f, 127.0f), 12582912.0f)) - 0x4B400000u + 128u
+          : 128u;
+      const uint32_t qr = nvs > 0.0f
+          ? __float_as_uint(__fadd_rd(clampf(r1[k] * inv_vs + u2, 0.0f, 255.0f), 12582912.0f)) - 0x4B400000u
+          : 0u;
+      mo |= qm << (8 * e);
+      vo |= qr << (8 * e);
+    }
+    if (full) {
+      *reinterpret_cast<float4*>(p + li0) = make_float4(pv[4 * h], pv[4 * h + 1], pv[4 * h + 2], pv[4 * h + 3]);
+      *reinterpret_cast<uint32_t*>(mcp + li0) = mo;
+      *reinterpret_cast<uint32_t*>(vcp + li0) = vo;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t li = li0 + (uint32_t)e;
+        if (li < vals_here) {
+          p[li] = pv[4 * h + e];
+          mcp[li] = (uint8_t)(mo >> (8 * e));
+          vcp[li] = (uint8_t)(vo >> (8 * e));
+        }
+      }
+    }
   }
 }
 

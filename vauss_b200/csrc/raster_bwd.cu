@@ -3,12 +3,14 @@
 //
 // Replaces rasterize_backwards_planes_kernel (crates/splat-train-render/src/
 // bwd/kernels/rasterize_backwards_planes.rs:112-682, gaussian branch):
-// one 128-thread CTA per tile, two pixels per thread (rows y and y + 8),
-// splats staged 32 at a time in shared memory.  Per splat, each thread sums its
-// pixels' gradients, a 32-lane butterfly reduce-scatter leaves one component
-// per lane pair, the four warps' partials are added in shared memory, and one
-// atomic add per non-zero (tile, splat, component) lands in v_combined [V,10]
-// = [xy(2), conic(3), rgb(3), alpha, refine].
+// one 128-thread CTA per tile, each warp an 8x8 quadrant, two pixels per
+// thread, splats staged 32 at a time in shared memory.  A warp walks only the
+// splats that can reach its quadrant (reach_rect).  Per splat,
+// each thread sums its pixels' gradients, a 12-shuffle butterfly
+// reduce-scatter leaves one component per lane pair, the four warps' partials
+// are added in shared memory, and one atomic add per non-zero (tile, splat,
+// component) lands in v_combined [V,10] = [xy(2), conic(3), rgb(3), alpha,
+// refine].
 //
 // The replay evaluates exactly the forward's exponent, alpha and transmittance
 // sequence (raster_sigma, vs_expf, the same comparisons), so every
@@ -24,24 +26,26 @@ constexpr uint32_t RB_WARPS = RB_THREADS / 32;
 constexpr uint32_t RB_BATCH = 32;
 constexpr uint32_t NG = 10;
 
-// Butterfly reduce-scatter of 16 values over 32 lanes: afterwards v[0] of lane
-// l holds the warp sum of component (l >> 1) & 15.
-__device__ __forceinline__ float reduce_scatter16(float v[16], uint32_t lane) {
+// Butterfly reduce-scatter of the NG = 10 gradient components over a warp in
+// 12 shuffles (groups of 5 | 3+2 | 2+1 | 1+1 | pair sum).  Afterwards the even
+// lane l holds the warp sum of component reduce10_comp(l) (or nothing, -1).
+__device__ __forceinline__ float reduce10(float v[NG], uint32_t lane) {
   {
     const bool hi = lane & 16u;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float keep = hi ? v[i + 8] : v[i];
-      const float send = hi ? v[i] : v[i + 8];
+    for (int i = 0; i < 5; ++i) {
+      const float keep = hi ? v[i + 5] : v[i];
+      const float send = hi ? v[i] : v[i + 5];
       v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
     }
   }
   {
     const bool hi = lane & 8u;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float keep = hi ? v[i + 4] : v[i];
-      const float send = hi ? v[i] : v[i + 4];
+    for (int i = 0; i < 3; ++i) {
+      const float up = i + 3 < 5 ? v[i + 3] : 0.0f;
+      const float keep = hi ? up : v[i];
+      const float send = hi ? v[i] : up;
       v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
     }
   }
@@ -49,8 +53,9 @@ __device__ __forceinline__ float reduce_scatter16(float v[16], uint32_t lane) {
     const bool hi = lane & 4u;
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const float keep = hi ? v[i + 2] : v[i];
-      const float send = hi ? v[i] : v[i + 2];
+      const float up = i + 2 < 3 ? v[i + 2] : 0.0f;
+      const float keep = hi ? up : v[i];
+      const float send = hi ? v[i] : up;
       v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
     }
   }
@@ -63,28 +68,42 @@ __device__ __forceinline__ float reduce_scatter16(float v[16], uint32_t lane) {
   return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
+// Component left on lane `lane` by reduce10: 5*b4 + 3*b3 + (2*b2 + b1), valid
+// while the offset 2*b2 + b1 is inside its group (3 wide for b3 = 0, else 2).
+__host__ __device__ constexpr int reduce10_comp(uint32_t lane) {
+  return (2u * ((lane >> 2) & 1u) + ((lane >> 1) & 1u)) >= (((lane >> 3) & 1u) ? 2u : 3u)
+             ? -1
+             : (int)(5u * ((lane >> 4) & 1u) + 3u * ((lane >> 3) & 1u) + 2u * ((lane >> 2) & 1u) +
+                     ((lane >> 1) & 1u));
+}
+
 __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
     uint32_t w, uint32_t h, uint32_t tbw, float bg_r, float bg_g, float bg_b, const uint2* __restrict__ ranges,
     const uint32_t* __restrict__ used_end, const uint32_t* __restrict__ isect_compact,
     const float4* __restrict__ projected, const float4* __restrict__ out_img, const float4* __restrict__ v_out,
     float* __restrict__ v_combined) {
-  __shared__ float4 s_a[RB_BATCH];  // x, y, c00, c01
-  __shared__ float4 s_b[RB_BATCH];  // c11, opac, r, g
-  __shared__ float2 s_c[RB_BATCH];  // b, sigma cut
+  __shared__ float4 s_a[RB_BATCH];    // x, y, 0.5 c00, c01
+  __shared__ float4 s_b[RB_BATCH];    // 0.5 c11, opac, r, g
+  __shared__ float2 s_c[RB_BATCH];    // b, sigma cut
+  __shared__ float4 s_rc[RB_BATCH];   // culling constants (reach_cut)
   __shared__ uint32_t s_cid[RB_BATCH];
-  __shared__ float s_part[RB_WARPS][RB_BATCH][NG];
+  __shared__ __align__(16) float s_part[RB_WARPS][RB_BATCH][NG];
 
   const uint32_t tile = blockIdx.x;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-  const uint32_t px = (tile % tbw) * TILE + tid % TILE;
-  const uint32_t py0 = (tile / tbw) * TILE + tid / TILE;
+  // Warp w owns the 8x8 quadrant (w & 1, w >> 1) of the tile; lane l its
+  // pixels (l & 7, l >> 3) and (l & 7, (l >> 3) + 4).
+  const uint32_t qx = (tile % tbw) * TILE + (warp & 1u) * 8u, qy = (tile / tbw) * TILE + (warp >> 1) * 8u;
+  const uint32_t px = qx + (lane & 7u);
+  const float rx0 = (float)qx + 0.5f, rx1 = rx0 + 7.0f, ry0 = (float)qy + 0.5f, ry1 = ry0 + 7.0f;
   const float fx = (float)px + 0.5f;
   const float img_w = (float)w, img_h = (float)h;
+  const int comp = reduce10_comp(lane);
 
   float sr[2], sg[2], sb[2], st[2], vr[2], vg[2], vb[2], vt[2], rs[2], fy[2];
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
-    const uint32_t py = py0 + 8u * k;
+    const uint32_t py = qy + (lane >> 3) + 4u * k;
     fy[k] = (float)py + 0.5f;
     sr[k] = sg[k] = sb[k] = st[k] = vr[k] = vg[k] = vb[k] = vt[k] = rs[k] = 0.0f;
     if (px < w && py < h) {
@@ -107,32 +126,52 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
   const uint32_t lo = ranges[tile].x, hi = used_end[tile];
   for (uint32_t batch = lo; batch < hi; batch += RB_BATCH) {
     const uint32_t cnt = min(RB_BATCH, hi - batch);
+    {
+      float4* z = reinterpret_cast<float4*>(&s_part[0][0][0]);
+      for (uint32_t i = tid; i < RB_WARPS * RB_BATCH * NG / 4; i += RB_THREADS) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     if (tid < cnt) {
       const uint32_t c = isect_compact[batch + tid];
       const float4 a = projected[(size_t)c * PROJ_F4];
       const float4 bb = projected[(size_t)c * PROJ_F4 + 1];
       const float4 cc = projected[(size_t)c * PROJ_F4 + 2];
-      s_a[tid] = a;
-      s_b[tid] = bb;
-      s_c[tid] = make_float2(cc.x, vs_logf(bb.y / ALPHA_EDGE) + 1.0e-3f);
+      const float cut = vs_logf(bb.y / ALPHA_EDGE) + 1.0e-3f;
+      s_a[tid] = make_float4(a.x, a.y, 0.5f * a.z, a.w);
+      s_b[tid] = make_float4(0.5f * bb.x, bb.y, bb.z, bb.w);
+      s_c[tid] = make_float2(cc.x, cut);
+      {
+        const ReachCut rc = reach_cut(0.5f * a.z, a.w, 0.5f * bb.x, cut);
+        s_rc[tid] = make_float4(rc.kx, rc.ky, rc.tcut, 0.0f);
+      }
       s_cid[tid] = c;
     }
     __syncthreads();
-    for (uint32_t t = 0; t < cnt; ++t) {
+    // The warp walks only the splats that can reach its quadrant.
+    bool near = false;
+    if (lane < cnt) {
+      const float4 sa = s_a[lane], rc = s_rc[lane];
+      near = reach_rect(sa.x, sa.y, sa.z, sa.w, s_b[lane].x, ReachCut{rc.x, rc.y, rc.z}, rx0, rx1, ry0, ry1);
+    }
+    uint32_t m = __ballot_sync(0xffffffffu, near);
+    while (m) {
+      const uint32_t t = __ffs(m) - 1;
+      m &= m - 1u;
       const float4 a = s_a[t];
       const float4 bb = s_b[t];
       const float2 cc = s_c[t];
-      const float c00 = a.z, c01 = a.w, c11 = bb.x, opac = bb.y;
+      const float h00 = a.z, c01 = a.w, h11 = bb.x, opac = bb.y;
+      const float c00 = 2.0f * h00, c11 = 2.0f * h11;
       const float cr = fmaxf(bb.z, 0.0f), cg = fmaxf(bb.w, 0.0f), cb = fmaxf(cc.x, 0.0f);
       const float dx = a.x - fx;
-      float g[16];
+      float g[NG];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) g[i] = 0.0f;
+      for (int i = 0; i < (int)NG; ++i) g[i] = 0.0f;
       bool contributes = false;
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const float dy = a.y - fy[k];
-        const float sigma = raster_sigma(0.5f * c00, c01, 0.5f * c11, dx, dy);
+        // coverage decisions: the forward's exact arithmetic
+        const float sigma = raster_sigma(h00, c01, h11, dx, dy);
         if (!(st[k] > 1.0e-4f && sigma <= cc.y)) continue;
         const float gauss = vs_expf(-sigma);
         const float alpha = fminf(0.999f, opac * gauss);
@@ -143,11 +182,12 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
           continue;
         }
         contributes = true;
+        // gradients: the oracle's per-term float steps, summed in another order
         const float vis = alpha * st[k];
         if (bb.z >= 0.0f) g[5] += vis * vr[k];
         if (bb.w >= 0.0f) g[6] += vis * vg[k];
         if (cc.x >= 0.0f) g[7] += vis * vb[k];
-        const float ra = 1.0f / (1.0f - alpha);
+        const float ra = rcp_rn(1.0f - alpha);  // 1 - alpha in [1e-3, 1]
         const float dot =
             ((st[k] * cr - sr[k]) * vr[k] + (st[k] * cg - sg[k]) * vg[k] + (st[k] * cb - sb[k]) * vb[k]) * ra;
         const float v_alpha = dot + vt[k] * ra;
@@ -161,7 +201,7 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
           g[0] += vxx;
           g[1] += vxy;
           g[8] += v_alpha * gauss;
-          g[9] += sqrtf(vxx * img_w * vxx * img_w + vxy * img_h * vxy * img_h) * rs[k];
+          g[9] += sqrt_rn(vxx * img_w * vxx * img_w + vxy * img_h * vxy * img_h) * rs[k];
         }
         sr[k] = sr[k] - vis * cr;
         sg[k] = sg[k] - vis * cg;
@@ -169,20 +209,17 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
         st[k] = next_t;
       }
       if (__any_sync(0xffffffffu, contributes)) {
-        const float sum = reduce_scatter16(g, lane);
-        const uint32_t comp = (lane >> 1) & 15u;
-        if ((lane & 1u) == 0 && comp < NG) s_part[warp][t][comp] = sum;
-      } else if (lane < NG) {
-        s_part[warp][t][lane] = 0.0f;
+        const float sum = reduce10(g, lane);
+        if ((lane & 1u) == 0 && comp >= 0) s_part[warp][t][comp] = sum;
       }
     }
     __syncthreads();
     for (uint32_t idx = tid; idx < cnt * NG; idx += RB_THREADS) {
-      const uint32_t s = idx / NG, comp = idx % NG;
+      const uint32_t s = idx / NG, c = idx % NG;
       float sum = 0.0f;
 #pragma unroll
-      for (uint32_t ww = 0; ww < RB_WARPS; ++ww) sum += s_part[ww][s][comp];
-      if (sum != 0.0f) atomicAdd(&v_combined[(size_t)s_cid[s] * NG + comp], sum);
+      for (uint32_t ww = 0; ww < RB_WARPS; ++ww) sum += s_part[ww][s][c];
+      if (sum != 0.0f) atomicAdd(&v_combined[(size_t)s_cid[s] * NG + c], sum);
     }
     __syncthreads();
   }

@@ -14,6 +14,9 @@
 // colour += max(c, 0) * alpha T (fma), final = colour + T bg (fma).
 // Splats whose exponent exceeds ln(opac / (1/255 - 5e-4)) + 1e-3 cannot pass
 // the alpha test, so their exp is skipped (same decisions, fewer SFU ops).
+// Each warp (an 8x4 pixel block) also skips every splat whose exponent
+// provably exceeds that cut on the whole block (reach_rect), which only drops
+// pixels that would fail the exponent test.
 #include "vs_internal.cuh"
 
 namespace {
@@ -39,15 +42,19 @@ __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
   __shared__ float4 s_a[RF_THREADS];  // x, y, 0.5 c00, c01
   __shared__ float4 s_b[RF_THREADS];  // 0.5 c11, opac, r, g
   __shared__ float2 s_c[RF_THREADS];  // b, sigma cut
+  __shared__ float4 s_rc[RF_THREADS];   // culling constants (reach_cut)
   __shared__ uint32_t s_gid[RF_THREADS];
   __shared__ uint32_t s_hit[RF_THREADS];
   __shared__ uint32_t s_done;
   __shared__ uint32_t s_max_used;
 
   const uint32_t tile = blockIdx.x;
-  const uint32_t tid = threadIdx.x;
+  const uint32_t tid = threadIdx.x, lane = tid & 31u;
   const uint32_t px = (tile % tbw) * TILE + compact_bits(tid);
   const uint32_t py = (tile / tbw) * TILE + compact_bits(tid >> 1);
+  // A warp's 32 Morton-ordered pixels form an 8x4 block.
+  const float rx0 = (float)((tile % tbw) * TILE + compact_bits(tid & ~31u)) + 0.5f, rx1 = rx0 + 7.0f;
+  const float ry0 = (float)((tile / tbw) * TILE + compact_bits((tid & ~31u) >> 1)) + 0.5f, ry1 = ry0 + 3.0f;
   const bool inside = px < w && py < h;
   const uint2 range = ranges[tile];
   const float fx = (float)px + 0.5f, fy = (float)py + 0.5f;
@@ -72,31 +79,51 @@ __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
       const float4 cc = projected[(size_t)c * PROJ_F4 + 2];
       s_a[tid] = make_float4(a.x, a.y, 0.5f * a.z, a.w);
       s_b[tid] = make_float4(0.5f * bb.x, bb.y, bb.z, bb.w);
-      s_c[tid] = make_float2(cc.x, vs_logf(bb.y / ALPHA_EDGE) + 1.0e-3f);
+      const float cut = vs_logf(bb.y / ALPHA_EDGE) + 1.0e-3f;
+      s_c[tid] = make_float2(cc.x, cut);
+      {
+        const ReachCut rc = reach_cut(0.5f * a.z, a.w, 0.5f * bb.x, cut);
+        s_rc[tid] = make_float4(rc.kx, rc.ky, rc.tcut, 0.0f);
+      }
       s_gid[tid] = __float_as_uint(cc.y);
       s_hit[tid] = 0;
     }
     __syncthreads();
     const bool was_done = done;
-    for (uint32_t j = 0; !done && j < cnt; ++j) {
-      const float4 sa = s_a[j];
-      const float4 sb = s_b[j];
-      const float2 sc = s_c[j];
-      const float sigma = raster_sigma(sa.z, sa.w, sb.x, fx - sa.x, fy - sa.y);
-      if (sigma > sc.y) continue;
-      const float alpha = fminf(0.999f, sb.y * vs_expf(-sigma));
-      if (sigma >= 0.0f && alpha >= ALPHA_MIN) {
-        const float next_t = t_acc * (1.0f - alpha);
-        if (next_t <= 1.0e-4f) {
-          done = true;
-        } else {
-          s_hit[j] = 1u;
-          const float vis = alpha * t_acc;
-          r = fmaf(fmaxf(sb.z, 0.0f), vis, r);
-          g = fmaf(fmaxf(sb.w, 0.0f), vis, g);
-          b = fmaf(fmaxf(sc.x, 0.0f), vis, b);
-          t_acc = next_t;
-          last = batch + j + 1;
+    // 32 splats at a time, the warp walks only those that can reach its 8x4
+    // block (reach_rect: the skipped ones fail the exponent test everywhere).
+    for (uint32_t j0 = 0; j0 < cnt; j0 += 32) {
+      if (__all_sync(0xffffffffu, done)) break;
+      const uint32_t jl = j0 + lane;
+      bool near = false;
+      if (jl < cnt) {
+        const float4 sa = s_a[jl], rc = s_rc[jl];
+        near = reach_rect(sa.x, sa.y, sa.z, sa.w, s_b[jl].x, ReachCut{rc.x, rc.y, rc.z}, rx0, rx1, ry0, ry1);
+      }
+      uint32_t m = __ballot_sync(0xffffffffu, near);
+      while (m) {
+        const uint32_t j = j0 + __ffs(m) - 1;
+        m &= m - 1u;
+        if (done) continue;
+        const float4 sa = s_a[j];
+        const float4 sb = s_b[j];
+        const float2 sc = s_c[j];
+        const float sigma = raster_sigma(sa.z, sa.w, sb.x, fx - sa.x, fy - sa.y);
+        if (sigma > sc.y) continue;
+        const float alpha = fminf(0.999f, sb.y * vs_expf(-sigma));
+        if (sigma >= 0.0f && alpha >= ALPHA_MIN) {
+          const float next_t = t_acc * (1.0f - alpha);
+          if (next_t <= 1.0e-4f) {
+            done = true;
+          } else {
+            s_hit[j] = 1u;
+            const float vis = alpha * t_acc;
+            r = fmaf(fmaxf(sb.z, 0.0f), vis, r);
+            g = fmaf(fmaxf(sb.w, 0.0f), vis, g);
+            b = fmaf(fmaxf(sc.x, 0.0f), vis, b);
+            t_acc = next_t;
+            last = batch + j + 1;
+          }
         }
       }
     }

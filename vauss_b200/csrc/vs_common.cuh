@@ -226,6 +226,85 @@ VSD float raster_sigma(float h00, float c01, float h11, float dx, float dy) {
   return fmaf(dx, t, (h11 * dy) * dy);
 }
 
+// Correctly rounded reciprocal, quotient and square root built from the PTX
+// approximations and fma, cheaper than the compiler's general-range sequences
+// for 1/x, x/y and sqrtf (which carry range checks and a slow path).
+//   rcp_rn(b):  one Newton step on rcp.approx; equal to the IEEE reciprocal
+//               for every |b| in [2^-126, 2^126) (checked exhaustively on B200).
+//   div_rn(a, b): q = a y, r = fma(-b, q, a), q + r y with y = rcp_rn(b); by
+//               Markstein's theorem this is the correctly rounded a / b when
+//               |b| is in that range and a, a / b are normal (and it returns
+//               0 for a = 0).
+//   sqrt_rn(v): s = v rsqrt(v) corrected by one fma, with inputs below 2^-100
+//               scaled by 2^64; equal to IEEE sqrtf for every finite v >= 0
+//               (checked exhaustively on B200), +inf and NaN included.
+// The CPU oracle computes the same values with plain 1 / b, a / b and sqrtf.
+VSD float rcp_rn(float b) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+  return fmaf(fmaf(-b, y, 1.0f), y, y);
+}
+VSD float div_rn(float a, float b) {
+  const float y = rcp_rn(b);
+  const float q = a * y;
+  return fmaf(fmaf(-b, q, a), y, q);
+}
+VSD float sqrt_rn(float v) {
+  const bool tiny = v < 7.888609052210118e-31f;  // 2^-100
+  const float vs = tiny ? v * 18446744073709551616.0f : v;  // * 2^64
+  float y;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(vs));
+  float s = vs * y;
+  s = fmaf(fmaf(-s, s, vs), 0.5f * y, s);
+  s = tiny ? s * 2.3283064365386963e-10f : s;  // * 2^-32
+  return (v == 0.0f || v > 3.402823466e38f) ? v : s;  // +-0 and +inf map to themselves
+}
+
+// Warp-level culling of splats against a rectangle of pixel centres.
+//
+// sigma(d) = h00 dx^2 + c01 dx dy + h11 dy^2 (raster_sigma, d = mean - pixel)
+// is a convex quadratic, so its minimum over a rectangle is 0 when the mean
+// lies inside, else it lies on an edge, where sigma is a 1-D quadratic whose
+// unconstrained minimiser is t = -c01 a / (2 h11) (x-edge dx = a) or
+// t = -c01 a / (2 h00) (y-edge dy = a), clamped to the edge.  A splat whose
+// minimum exceeds 1.02 cut + 1e-3 fails the exponent test (sigma <= cut) at
+// every pixel centre of the rectangle: for conics with tr^2 < 1e4 det
+// (condition number below ~1e4) the fp32 evaluation of sigma, at a pixel or at
+// the edge minimiser, is within 1% of the exact form.  Other conics, NaNs and
+// infinities always pass (test cut = +inf or NaN); a negative cut admits no
+// pixel, since the exponent must also be >= 0.
+struct ReachCut {
+  float kx, ky;  // -c01 / (2 h11), -c01 / (2 h00): edge minimisers per unit offset
+  float tcut;    // threshold on the rectangle minimum
+};
+
+VSD ReachCut reach_cut(float h00, float c01, float h11, float cut) {
+  const float c00 = 2.0f * h00, c11 = 2.0f * h11;
+  const float det = c00 * c11 - c01 * c01, tr = c00 + c11;
+  const bool tame = det > 0.0f && tr > 0.0f && tr * tr < 1.0e4f * det;
+  ReachCut r;
+  r.kx = tame ? -c01 / c11 : 0.0f;
+  r.ky = tame ? -c01 / c00 : 0.0f;
+  r.tcut = cut < 0.0f ? -1.0f : (tame ? 1.02f * cut + 1.0e-3f : __int_as_float(0x7f800000));
+  return r;
+}
+
+VSD float edge_min(float h_a, float c01, float h_t, float a, float k, float lo, float hi) {
+  const float t = clampf(k * a, lo, hi);
+  return fmaf(a, fmaf(h_a, a, c01 * t), (h_t * t) * t);
+}
+
+// True unless every pixel centre in [rx0, rx1] x [ry0, ry1] certainly fails
+// sigma <= cut.
+VSD bool reach_rect(float mx, float my, float h00, float c01, float h11, ReachCut rc, float rx0, float rx1,
+                    float ry0, float ry1) {
+  const float dxl = mx - rx1, dxh = mx - rx0, dyl = my - ry1, dyh = my - ry0;
+  if (dxl <= 0.0f && dxh >= 0.0f && dyl <= 0.0f && dyh >= 0.0f) return rc.tcut >= 0.0f || rc.tcut != rc.tcut;
+  const float m = fminf(fminf(edge_min(h00, c01, h11, dxl, rc.kx, dyl, dyh), edge_min(h00, c01, h11, dxh, rc.kx, dyl, dyh)),
+                        fminf(edge_min(h11, c01, h00, dyl, rc.ky, dxl, dxh), edge_min(h11, c01, h00, dyh, rc.ky, dxl, dxh)));
+  return !(m > rc.tcut);
+}
+
 struct Floor { V3 scale; float opac, coef; V3 ratio_sq; bool opac_open; };
 // Mip-Splatting 3D filter floor (kernels/helpers.rs:516-553).
 VSD Floor apply_scale_floor(V3 s, float opac_sig, const float* min_scale, uint32_t g, bool has) {

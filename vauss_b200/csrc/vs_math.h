@@ -62,7 +62,11 @@ VS_HD bool vs_is_finite(float x) { return ((vs_f2u(x) >> 23) & 0xffu) != 0xffu; 
 VS_HD float vs_expf(float x) {
   if (!(x < 88.72283f)) return (x != x) ? x : INFINITY;
   if (x < -87.0f) return 0.0f;
-  const float k = rintf(x * VS_LOG2E);
+  // k = rint(x log2e): adding 1.5 * 2^23 rounds |x log2e| < 2^22 to an integer
+  // (ties to even, the default rounding mode), whose value then sits in the
+  // low mantissa bits, so no float<->int conversion is needed.
+  const float shifted = x * VS_LOG2E + 12582912.0f;
+  const float k = shifted - 12582912.0f;
   float r = fmaf(k, -VS_LN2_HI, x);
   r = fmaf(k, -VS_LN2_LO, r);
   // e^r = sum_{n<=7} r^n / n!
@@ -74,8 +78,8 @@ VS_HD float vs_expf(float x) {
   p = fmaf(p, r, 0.5f);
   p = fmaf(p, r, 1.0f);
   p = fmaf(p, r, 1.0f);
-  const int32_t ki = (int32_t)k;
-  return vs_u2f(vs_f2u(p) + ((uint32_t)ki << 23));
+  const uint32_t ki = vs_f2u(shifted) - 0x4B400000u;  // k as a two's-complement integer
+  return vs_u2f(vs_f2u(p) + (ki << 23));
 }
 
 VS_HD float vs_logf(float x) {
