@@ -251,7 +251,10 @@ VS_API vs_status vs_radix_sort_pairs_static(vs_ctx* ctx, uint32_t* keys, uint32_
                                             uint32_t key_bits);
 /* Inclusive prefix sum of u32 in place; the total (u64) to *total_dev if non-NULL. */
 VS_API vs_status vs_scan_inclusive(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev);
-/* Elementwise vs_expf / vs_logf (the shared deterministic functions). */
+/* Elementwise device math used by the kernels, for tests: which = 0 vs_expf,
+ * 1 vs_logf (the functions shared with the CPU oracle), 2 the fma-refined
+ * square root and 4 the fma-refined reciprocal, with 3 (IEEE sqrtf) and
+ * 5 (IEEE 1 / x) beside them to check that both are correctly rounded. */
 VS_API vs_status vs_math_probe(vs_ctx* ctx, int32_t which, const float* x, float* y, uint32_t n);
 
 #ifdef __cplusplus

@@ -322,13 +322,24 @@ VS_API vs_status vs_scan_inclusive(vs_ctx* ctx, uint32_t* data, uint32_t count, 
 namespace {
 __global__ void math_probe_kernel(int which, const float* x, float* y, uint32_t n) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) y[i] = which == 0 ? vs_expf(x[i]) : vs_logf(x[i]);
+  if (i >= n) return;
+  const float v = x[i];
+  float r;
+  switch (which) {
+    case 0: r = vs_expf(v); break;
+    case 1: r = vs_logf(v); break;
+    case 2: r = vs::sqrt_rn(v); break;
+    case 3: r = sqrtf(v); break;
+    case 4: r = vs::rcp_rn(v); break;
+    default: r = 1.0f / v; break;
+  }
+  y[i] = r;
 }
 }  // namespace
 
 extern "C" VS_API vs_status vs_math_probe(vs_ctx* ctx, int32_t which, const float* x, float* y, uint32_t n) {
   if (!ctx) return VS_ERR_INVALID;
-  if (!x || !y || which < 0 || which > 1) return vs_fail(ctx, VS_ERR_INVALID, "math_probe: bad arguments");
+  if (!x || !y || which < 0 || which > 5) return vs_fail(ctx, VS_ERR_INVALID, "math_probe: bad arguments");
   if (n == 0) return VS_OK;
   math_probe_kernel<<<vs::div_up(n, 256), 256, 0, ctx->stream>>>(which, x, y, n); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "math_probe launch");

@@ -93,10 +93,26 @@ __device__ V3 splat_color(const void* sh, bool half, uint32_t g, int deg, V3 mea
   const V3 d = v3sub(mean, V3{u.cam[0], u.cam[1], u.cam[2]});
   const V3 v = v3scale(d, 1.0f / sqrtf(v3dot(d, d)));
   const int nc = (deg + 1) * (deg + 1);
-  const size_t base = (size_t)g * nc * 3;
-  auto rc = [&](int k) -> V3 {
-    return {sh_load(sh, half, base + k), sh_load(sh, half, base + k + 1), sh_load(sh, half, base + k + 2)};
-  };
+  const int cnt = nc * 3;
+  const size_t base = (size_t)g * cnt;
+  // All coefficients are loaded before any is used: 16-byte loads when the
+  // row is f32 and a multiple of 16 bytes long (degrees 1 and 3).
+  float cf[48];
+  if (!half && (cnt & 3) == 0) {
+    const float4* p4 = reinterpret_cast<const float4*>((const float*)sh + base);
+#pragma unroll
+    for (int q = 0; q < 12; ++q) {
+      const float4 v = 4 * q < cnt ? p4[q] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      cf[4 * q] = v.x;
+      cf[4 * q + 1] = v.y;
+      cf[4 * q + 2] = v.z;
+      cf[4 * q + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 48; ++k) cf[k] = k < cnt ? sh_load(sh, half, base + k) : 0.0f;
+  }
+  auto rc = [&](int k) -> V3 { return {cf[k], cf[k + 1], cf[k + 2]}; };
   V3 color = v3scale(rc(0), SH_C0);
   if (deg >= 1) {
     const float f0a = 0.4886025f;
@@ -170,11 +186,23 @@ __global__ void __launch_bounds__(PROJ_BLOCK, 3) project_kernel(
 
   ProjOut o;
   bool visible = false;
+  float t[10];
   if (g < n) {
-    visible = project_one(transforms + (size_t)g * 10, raw_opac[g], min_scale, g, u, &o);
+    const float2* t2 = reinterpret_cast<const float2*>(transforms + (size_t)g * 10);
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      const float2 v = t2[k];
+      t[2 * k] = v.x;
+      t[2 * k + 1] = v.y;
+    }
+    visible = project_one(t, raw_opac[g], min_scale, g, u, &o);
     opacities[g] = o.floor_reached ? o.floor_opac : 0.0f;
     max_radius[g] = visible ? o.radius : 0.0f;
   }
+  // Colour of the visible splats, before the ranking below, so the SH loads
+  // are in flight while the block waits for its look-back.
+  V3 col = {0.0f, 0.0f, 0.0f};
+  if (visible) col = splat_color(sh, u.sh_half != 0, g, u.sh_degree, V3{t[0], t[1], t[2]}, u);
   // Tile counting (kernels/helpers.rs:254-273); large boxes are walked by the
   // whole warp, one splat at a time (project_forward.rs:198-247).
   uint32_t nb = 0;
@@ -269,8 +297,6 @@ __global__ void __launch_bounds__(PROJ_BLOCK, 3) project_kernel(
   global_from_compact[c] = g;
   depths[c] = o.depth;
   tile_counts[c] = hits;
-  const float* t = transforms + (size_t)g * 10;
-  const V3 col = splat_color(sh, u.sh_half != 0, g, u.sh_degree, V3{t[0], t[1], t[2]}, u);
   float4* row = projected + (size_t)c * PROJ_F4;
   row[0] = make_float4(o.xy_x, o.xy_y, o.conic.c00, o.conic.c01);
   row[1] = make_float4(o.conic.c11, o.opac, col.x, col.y);

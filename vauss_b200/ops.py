@@ -345,5 +345,6 @@ def scan_inclusive(data: torch.Tensor) -> int:
 def math_probe(which: str, x: torch.Tensor) -> torch.Tensor:
     ctx = context(x.device)
     y = torch.empty_like(x)
-    ctx.check(ctx.lib.vs_math_probe(ctx.h, 0 if which == "exp" else 1, _ptr(x), _ptr(y), x.numel()))
+    modes = {"exp": 0, "log": 1, "sqrt_rn": 2, "sqrt_ieee": 3, "rcp_rn": 4, "rcp_ieee": 5}
+    ctx.check(ctx.lib.vs_math_probe(ctx.h, modes[which], _ptr(x), _ptr(y), x.numel()))
     return y
