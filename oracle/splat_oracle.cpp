@@ -921,12 +921,15 @@ OR_API int or_raster_bwd(const Camera* cam, const float* bg, uint32_t nv, const 
             if (p[6] >= 0.0f) a[5] += vis * vr;
             if (p[7] >= 0.0f) a[6] += vis * vg;
             if (p[8] >= 0.0f) a[7] += vis * vb;
+            // The reference's expressions (rasterize_backwards_planes.rs:560-595)
+            // with the multiply-adds fused as written below; the kernel uses the
+            // same fmas, so every per-pixel term matches it bit for bit.
             const float ra = 1.0f / (1.0f - alpha);
-            const float dot = ((st * cr - sr) * vr + (st * cg - sg) * vg + (st * cbb - sb) * vb) * ra;
-            const float v_alpha = dot + vt * ra;
+            const float dot = fmaf(fmaf(st, cr, -sr), vr, fmaf(fmaf(st, cg, -sg), vg, fmaf(st, cbb, -sb) * vb)) * ra;
+            const float v_alpha = fmaf(vt, ra, dot);
             const float v_sigma = -alpha * v_alpha;
-            const float vxx = v_sigma * (p[2] * dx + p[3] * dy);
-            const float vxy = v_sigma * (p[3] * dx + p[4] * dy);
+            const float vxx = v_sigma * fmaf(p[2], dx, p[3] * dy);
+            const float vxy = v_sigma * fmaf(p[3], dx, p[4] * dy);
             if (p[5] * gauss <= 0.999f) {
               a[2] += 0.5f * v_sigma * dx * dx;
               a[3] += v_sigma * dx * dy;
@@ -934,11 +937,12 @@ OR_API int or_raster_bwd(const Camera* cam, const float* bg, uint32_t nv, const 
               a[0] += vxx;
               a[1] += vxy;
               a[8] += v_alpha * gauss;
-              a[9] += sqrtf(vxx * W * vxx * W + vxy * Hh * vxy * Hh) * rscale;
+              const float ax = vxx * W, ay = vxy * Hh;
+              a[9] += sqrtf(fmaf(ax, ax, ay * ay)) * rscale;
             }
-            sr = sr - vis * cr;
-            sg = sg - vis * cg;
-            sb = sb - vis * cbb;
+            sr = fmaf(-vis, cr, sr);
+            sg = fmaf(-vis, cg, sg);
+            sb = fmaf(-vis, cbb, sb);
             st = next_t;
           }
         }

@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
         // coverage decisions: the forward's exact arithmetic
         const float sigma = raster_sigma(h00, c01, h11, dx, dy);
         if (!(st[k] > 1.0e-4f && sigma <= cc.y)) continue;
-        const float gauss = vs_expf(-sigma);
+        const float gauss = vs_expf_core(-sigma);  // = vs_expf: used only for 0 <= sigma <= cut < 6
         const float alpha = fminf(0.999f, opac * gauss);
         if (!(sigma >= 0.0f && alpha >= ALPHA_MIN)) continue;
         const float next_t = st[k] * (1.0f - alpha);
@@ -182,18 +182,19 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
           continue;
         }
         contributes = true;
-        // gradients: the oracle's per-term float steps, summed in another order
+        // gradients: the oracle's per-term float steps (the same fmas), summed
+        // in another order
         const float vis = alpha * st[k];
         if (bb.z >= 0.0f) g[5] += vis * vr[k];
         if (bb.w >= 0.0f) g[6] += vis * vg[k];
         if (cc.x >= 0.0f) g[7] += vis * vb[k];
         const float ra = rcp_rn(1.0f - alpha);  // 1 - alpha in [1e-3, 1]
         const float dot =
-            ((st[k] * cr - sr[k]) * vr[k] + (st[k] * cg - sg[k]) * vg[k] + (st[k] * cb - sb[k]) * vb[k]) * ra;
-        const float v_alpha = dot + vt[k] * ra;
+            fmaf(fmaf(st[k], cr, -sr[k]), vr[k], fmaf(fmaf(st[k], cg, -sg[k]), vg[k], fmaf(st[k], cb, -sb[k]) * vb[k])) * ra;
+        const float v_alpha = fmaf(vt[k], ra, dot);
         const float v_sigma = -alpha * v_alpha;
-        const float vxx = v_sigma * (c00 * dx + c01 * dy);
-        const float vxy = v_sigma * (c01 * dx + c11 * dy);
+        const float vxx = v_sigma * fmaf(c00, dx, c01 * dy);
+        const float vxy = v_sigma * fmaf(c01, dx, c11 * dy);
         if (opac * gauss <= 0.999f) {
           g[2] += 0.5f * v_sigma * dx * dx;
           g[3] += v_sigma * dx * dy;
@@ -201,11 +202,12 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
           g[0] += vxx;
           g[1] += vxy;
           g[8] += v_alpha * gauss;
-          g[9] += sqrt_rn(vxx * img_w * vxx * img_w + vxy * img_h * vxy * img_h) * rs[k];
+          const float ax = vxx * img_w, ay = vxy * img_h;
+          g[9] += sqrt_rn(fmaf(ax, ax, ay * ay)) * rs[k];
         }
-        sr[k] = sr[k] - vis * cr;
-        sg[k] = sg[k] - vis * cg;
-        sb[k] = sb[k] - vis * cb;
+        sr[k] = fmaf(-vis, cr, sr[k]);
+        sg[k] = fmaf(-vis, cg, sg[k]);
+        sb[k] = fmaf(-vis, cb, sb[k]);
         st[k] = next_t;
       }
       if (__any_sync(0xffffffffu, contributes)) {

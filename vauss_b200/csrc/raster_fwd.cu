@@ -40,8 +40,8 @@ __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
     const float4* __restrict__ projected, float4* __restrict__ out_img, float* __restrict__ visible,
     uint32_t* __restrict__ used_end) {
   __shared__ float4 s_a[RF_THREADS];  // x, y, 0.5 c00, c01
-  __shared__ float4 s_b[RF_THREADS];  // 0.5 c11, opac, r, g
-  __shared__ float2 s_c[RF_THREADS];  // b, sigma cut
+  __shared__ float4 s_b[RF_THREADS];  // 0.5 c11, opac, max(r, 0), max(g, 0)
+  __shared__ float2 s_c[RF_THREADS];  // max(b, 0), sigma cut
   __shared__ float4 s_rc[RF_THREADS];   // culling constants (reach_cut)
   __shared__ uint32_t s_gid[RF_THREADS];
   __shared__ uint32_t s_hit[RF_THREADS];
@@ -78,9 +78,9 @@ __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
       const float4 bb = projected[(size_t)c * PROJ_F4 + 1];
       const float4 cc = projected[(size_t)c * PROJ_F4 + 2];
       s_a[tid] = make_float4(a.x, a.y, 0.5f * a.z, a.w);
-      s_b[tid] = make_float4(0.5f * bb.x, bb.y, bb.z, bb.w);
+      s_b[tid] = make_float4(0.5f * bb.x, bb.y, fmaxf(bb.z, 0.0f), fmaxf(bb.w, 0.0f));
       const float cut = vs_logf(bb.y / ALPHA_EDGE) + 1.0e-3f;
-      s_c[tid] = make_float2(cc.x, cut);
+      s_c[tid] = make_float2(fmaxf(cc.x, 0.0f), cut);
       {
         const ReachCut rc = reach_cut(0.5f * a.z, a.w, 0.5f * bb.x, cut);
         s_rc[tid] = make_float4(rc.kx, rc.ky, rc.tcut, 0.0f);
@@ -110,7 +110,9 @@ __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
         const float2 sc = s_c[j];
         const float sigma = raster_sigma(sa.z, sa.w, sb.x, fx - sa.x, fy - sa.y);
         if (sigma > sc.y) continue;
-        const float alpha = fminf(0.999f, sb.y * vs_expf(-sigma));
+        // vs_expf_core = vs_expf wherever the result is used: only when
+        // 0 <= sigma <= cut < 6 is the splat accepted
+        const float alpha = fminf(0.999f, sb.y * vs_expf_core(-sigma));
         if (sigma >= 0.0f && alpha >= ALPHA_MIN) {
           const float next_t = t_acc * (1.0f - alpha);
           if (next_t <= 1.0e-4f) {
@@ -118,9 +120,9 @@ __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
           } else {
             s_hit[j] = 1u;
             const float vis = alpha * t_acc;
-            r = fmaf(fmaxf(sb.z, 0.0f), vis, r);
-            g = fmaf(fmaxf(sb.w, 0.0f), vis, g);
-            b = fmaf(fmaxf(sc.x, 0.0f), vis, b);
+            r = fmaf(sb.z, vis, r);
+            g = fmaf(sb.w, vis, g);
+            b = fmaf(sc.x, vis, b);
             t_acc = next_t;
             last = batch + j + 1;
           }

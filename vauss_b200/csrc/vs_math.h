@@ -59,9 +59,10 @@ VS_HD bool vs_is_finite(float x) { return ((vs_f2u(x) >> 23) & 0xffu) != 0xffu; 
 #define VS_LN2_LO 1.42860682030941723212e-6f /* ln 2 - VS_LN2_HI */
 #define VS_LOG2E 1.44269504088896340736f
 
-VS_HD float vs_expf(float x) {
-  if (!(x < 88.72283f)) return (x != x) ? x : INFINITY;
-  if (x < -87.0f) return 0.0f;
+// vs_expf without its range checks: equal to vs_expf for x in [-87, 88.72283)
+// (outside that range the result is meaningless, so callers use it only
+// where their own tests already reject such inputs).
+VS_HD float vs_expf_core(float x) {
   // k = rint(x log2e): adding 1.5 * 2^23 rounds |x log2e| < 2^22 to an integer
   // (ties to even, the default rounding mode), whose value then sits in the
   // low mantissa bits, so no float<->int conversion is needed.
@@ -80,6 +81,12 @@ VS_HD float vs_expf(float x) {
   p = fmaf(p, r, 1.0f);
   const uint32_t ki = vs_f2u(shifted) - 0x4B400000u;  // k as a two's-complement integer
   return vs_u2f(vs_f2u(p) + (ki << 23));
+}
+
+VS_HD float vs_expf(float x) {
+  if (!(x < 88.72283f)) return (x != x) ? x : INFINITY;
+  if (x < -87.0f) return 0.0f;
+  return vs_expf_core(x);
 }
 
 VS_HD float vs_logf(float x) {

@@ -132,6 +132,7 @@ class SplatTrainer:
         self.optim = None
         self.record: RefineRecord | None = None
         self._buffers = {}
+        self._copy_stream = None
 
     # ---- learning rates (train.rs:859-904) ----
     def lr_unit(self) -> float:
@@ -182,8 +183,20 @@ class SplatTrainer:
         self.step_count += 1
         cam = batch.camera
         gt = batch.img_packed
+        gt_ready = None
         if gt.device != self.device:
-            gt = gt.to(self.device, non_blocking=True)
+            # Upload the target on a side stream: the loss is its first reader,
+            # so the copy overlaps projection, sorting and compositing.  The
+            # copy waits for the previous step (the last reader of the buffer).
+            cur = torch.cuda.current_stream(self.device)
+            if self._copy_stream is None:
+                self._copy_stream = torch.cuda.Stream(self.device)
+            dst = self._buf("gt", tuple(gt.shape), gt.dtype)
+            self._copy_stream.wait_stream(cur)
+            with torch.cuda.stream(self._copy_stream):
+                dst.copy_(gt, non_blocking=True)
+            gt_ready = self._copy_stream.record_event()
+            gt = dst
         bg = self.background()
         n = splats.num_splats
         mode = c.optimizer
@@ -194,6 +207,8 @@ class SplatTrainer:
         out = ops.render(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, frame=self.frame,
                          out_img=self._buf("img", (cam.height, cam.width, 4), torch.float32),
                          visible=self._buf("visible", (n,), torch.float32))
+        if gt_ready is not None:
+            torch.cuda.current_stream(self.device).wait_event(gt_ready)
         loss = ops.image_loss(out.out_img, gt, c.l1_weight, c.ssim_loss_weight)
         vcomb = self._buf("v_combined", (max(n, 1), 10), torch.float32)
         vc = ops.rasterize_bwd(out.frame, out.out_img, loss.dl_dpred, vcomb)
