@@ -183,7 +183,14 @@ def run_ours(args):
     cfg = TrainConfig(optimizer="q8")
     median_scale = float(np.median(np.exp(sp.transforms[:, 7:10])))
     kw = dict(scene_extent=8.0, median_scale=median_scale)
-    trainer = ViewParallelTrainer(cfg, dev, **kw) if world > 1 else SplatTrainer(cfg, dev, **kw)
+    peer = None
+    if world > 1:
+        from vauss_b200.peer import PeerGroup, gather_bytes_nccl
+        peer = PeerGroup(dev, world, rank, lambda b: gather_bytes_nccl(b, dev))
+        trainer = ViewParallelTrainer(cfg, dev, peer=peer, **kw)
+        splats = trainer.adopt(splats)
+    else:
+        trainer = SplatTrainer(cfg, dev, **kw)
 
     def step(k, host=False, pinned=None):
         vi = k % N_TARGETS
@@ -249,7 +256,9 @@ def run_ours(args):
         h2d = int(targets[0].numel() * 4)
         e2e = {"value": world * args.steps / (float(te.item()) / 1e3), "unit": "iters/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-               "api": "SplatTrainer.step (vs_render_forward, vs_loss, vs_rasterize_backward, vs_step_q8)"}
+               "api": ("ViewParallelTrainer.step_views (vs_render_forward, vs_loss, vs_rasterize_backward, "
+                       "vs_vjp_dense, vs_peer_barrier, vs_adam_q8_peer)" if world > 1 else
+                       "SplatTrainer.step (vs_render_forward, vs_loss, vs_rasterize_backward, vs_step_q8)")}
 
     # ---- per-stage device times (CUDA events on the launching stream) ----
     stages = None
@@ -280,7 +289,9 @@ def run_ours(args):
            "config": {"workload": "config 2: 3M SH-3 splats, 1600x1060, 1 view/step/GPU, L1+0.2 D-SSIM, "
                                   "8-bit m+v Adam (block 256)", "splats": splats.num_splats, "width": 1600,
                       "height": 1060, "views_per_step": world, "optimizer": "q8",
-                      "parallelism": f"view-parallel x{world}" if world > 1 else "single GPU",
+                      "parallelism": (f"view-parallel x{world}: dense gradient rows read over NVLink peer "
+                                      f"memory by a sharded fused Adam that stores to every replica"
+                                      if world > 1 else "single GPU"),
                       "l2": "inputs larger than L2 (params + moments ~0.9 GB)", **counts},
            "gpu_launches": int(launches), "clocks": clk.summary()}
     if roofline:
@@ -294,6 +305,13 @@ def run_ours(args):
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        dist.barrier()  # no rank's kernels touch peer buffers any more
+        if peer is not None:
+            peer.check()
+            peer.close()
+        torch.cuda.synchronize(dev)
         dist.barrier()
         dist.destroy_process_group()
 

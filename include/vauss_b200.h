@@ -209,7 +209,10 @@ VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* c
  * project_backwards.rs:282-424 + the dense gather of burn_glue.rs:363-395):
  * ACCUMULATES this frame's gradients into grads [N, 10 + 3(d+1)^2 + 1]
  * (transforms | sh | raw opacity) and refine [N]; with vis_accum != NULL also
- * vis_accum += visible (the per-step count of views that saw each splat). */
+ * vis_accum += visible (the per-step count of views that saw each splat), and
+ * a row whose vis_accum was 0 before the call and whose splat is visible now
+ * is overwritten rather than accumulated, so readers that skip rows with
+ * vis_accum == 0 need grads cleared only once, not every step. */
 VS_API vs_status vs_vjp_dense(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
                               const float* transforms, const void* sh_coeffs, const float* raw_opacities,
                               const float* min_scale, const float* v_combined, float* grads, float* refine,
@@ -222,6 +225,48 @@ VS_API vs_status vs_adam_q8_dense(vs_ctx* ctx, uint32_t num_splats, int32_t sh_d
                                   float* sh_coeffs, float* raw_opacities, const float* grads, vs_q8_tensor mom_t,
                                   vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8,
                                   const float* opacities, const float* visible);
+
+/* ---- view-parallel step over NVLink peer memory -----------------------------
+ * No reference counterpart (the reference trains on one device).  One process
+ * per GPU; each rank renders its views into dense gradient rows, then every
+ * rank updates its shard of the splats from the rows of all ranks read
+ * directly over NVLink and stores the new parameters into every replica. */
+#define VS_PEER_MAX 8
+typedef struct vs_ipc_handle { uint8_t bytes[64]; } vs_ipc_handle;
+/* cudaMalloc'd buffer whose IPC handle other ranks can open. */
+VS_API vs_status vs_peer_alloc(vs_ctx* ctx, uint64_t bytes, void** dev_ptr, vs_ipc_handle* handle);
+VS_API vs_status vs_peer_free(vs_ctx* ctx, void* dev_ptr);
+/* Maps another rank's buffer into this process (peer access over NVLink). */
+VS_API vs_status vs_peer_open(vs_ctx* ctx, const vs_ipc_handle* handle, void** dev_ptr);
+VS_API vs_status vs_peer_close(vs_ctx* ctx, void* dev_ptr);
+/* Stream-ordered barrier of `world` ranks: peer_flags[r] is rank r's u32 flag
+ * array [world] (zeroed once); epoch must grow by one per call on every rank.
+ * A wait that exceeds two seconds sets the ctx's device error, which
+ * vs_ctx_check (or the next render's count readback) reports as
+ * VS_ERR_DEVICE_TIMEOUT. */
+VS_API vs_status vs_peer_barrier(vs_ctx* ctx, uint32_t* const* peer_flags, uint32_t world, uint32_t rank,
+                                 uint32_t epoch);
+/* Synchronises the ctx stream and reports a pending device-side error. */
+VS_API vs_status vs_ctx_check(vs_ctx* ctx);
+
+typedef struct vs_peer_set {
+  uint32_t world, rank;
+  const float* grads[VS_PEER_MAX];  /* [N, width] dense gradient rows of each rank */
+  const float* vis[VS_PEER_MAX];    /* [N] views of each rank that saw the splat (rows with 0 are not read) */
+  float* transforms[VS_PEER_MAX];   /* the replicas, [N,10] */
+  float* sh_coeffs[VS_PEER_MAX];    /* [N,(d+1)^2,3] f32 */
+  float* raw_opacities[VS_PEER_MAX];
+} vs_peer_set;
+/* The 8-bit-moment Adam of vs_adam_q8_dense for splats [splat_begin,
+ * splat_end) only (splat_begin a multiple of 256), with the gradient of each
+ * splat summed in rank order over the ranks whose vis > 0 and the noise gated
+ * on the summed vis; the moments (mom_*) hold that shard only, and the new
+ * parameters go to every rank's replica.  All ranks' gradient rows must be
+ * complete (vs_peer_barrier) before the call, and no rank may read its
+ * replica until every rank's call has finished (a second barrier). */
+VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, uint32_t splat_begin,
+                                 uint32_t splat_end, const vs_peer_set* peers, vs_q8_tensor mom_t,
+                                 vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8);
 
 /* ---- housekeeping (crates/splat-train/src/housekeep.rs:15-39) ------------- */
 VS_API vs_status vs_gather_stats(vs_ctx* ctx, uint32_t n, float* refine_norm, float* vis_count, float* max_screen,

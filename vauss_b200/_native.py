@@ -52,6 +52,19 @@ class Q8Tensor(ctypes.Structure):
     _fields_ = [("m_codes", c_vp), ("v_codes", c_vp), ("m_scales", c_vp), ("v_scales", c_vp)]
 
 
+PEER_MAX = 8
+
+
+class IpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_uint8 * 64)]
+
+
+class PeerSet(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_uint32), ("rank", ctypes.c_uint32), ("grads", c_vp * PEER_MAX),
+                ("vis", c_vp * PEER_MAX), ("transforms", c_vp * PEER_MAX), ("sh_coeffs", c_vp * PEER_MAX),
+                ("raw_opacities", c_vp * PEER_MAX)]
+
+
 class Q8Cfg(ctypes.Structure):
     _fields_ = [("beta1", ctypes.c_float), ("beta2", ctypes.c_float), ("inv1", ctypes.c_float),
                 ("inv2", ctypes.c_float), ("epsilon", ctypes.c_float), ("lr_transforms", ctypes.c_float * 10),
@@ -94,6 +107,15 @@ _SIGS = {
                       c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_adam_q8_dense": ([c_vp, ctypes.c_uint32, ctypes.c_int32, c_vp, c_vp, c_vp, c_vp, Q8Tensor, Q8Tensor,
                           Q8Tensor, ctypes.POINTER(Q8Cfg), c_vp, c_vp], ctypes.c_int),
+    "vs_peer_alloc": ([c_vp, ctypes.c_uint64, ctypes.POINTER(c_vp), ctypes.POINTER(IpcHandle)], ctypes.c_int),
+    "vs_peer_free": ([c_vp, c_vp], ctypes.c_int),
+    "vs_peer_open": ([c_vp, ctypes.POINTER(IpcHandle), ctypes.POINTER(c_vp)], ctypes.c_int),
+    "vs_peer_close": ([c_vp, c_vp], ctypes.c_int),
+    "vs_peer_barrier": ([c_vp, ctypes.POINTER(c_vp), ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32],
+                        ctypes.c_int),
+    "vs_ctx_check": ([c_vp], ctypes.c_int),
+    "vs_adam_q8_peer": ([c_vp, ctypes.c_uint32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint32,
+                         ctypes.POINTER(PeerSet), Q8Tensor, Q8Tensor, Q8Tensor, ctypes.POINTER(Q8Cfg)], ctypes.c_int),
     "vs_gather_stats": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_noise_means": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, ctypes.c_float, ctypes.c_float, ctypes.c_uint32],
                        ctypes.c_int),

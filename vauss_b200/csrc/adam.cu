@@ -227,9 +227,18 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t n, 
                                                         float* __restrict__ vis_accum) {
   const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
   if (g >= n) return;
-  if (vis_accum) vis_accum[g] += visible[g];
+  // A row not seen before in this step (vis_accum was 0) is overwritten, so
+  // readers gated on vis_accum never see an earlier step's values.
+  bool fresh = false;
+  if (vis_accum) {
+    const float seen = vis_accum[g];
+    vis_accum[g] = seen + visible[g];
+    fresh = seen == 0.0f && visible[g] > 0.0f;
+  }
   const uint32_t row = compact_from_global[g];
   if (row == 0) return;
+  const int nc = (u.sh_degree + 1) * (u.sh_degree + 1);
+  const int width = 10 + 3 * nc + 1;
   const float* rg = v_combined + (size_t)(row - 1) * 10;
   float rr[10];
   bool any = false;
@@ -238,9 +247,11 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t n, 
     rr[k] = rg[k];
     any = any || rr[k] != 0.0f;
   }
-  if (!any) return;
-  const int nc = (u.sh_degree + 1) * (u.sh_degree + 1);
-  const int width = 10 + 3 * nc + 1;
+  if (!any) {
+    if (fresh)
+      for (int k = 0; k < width; ++k) grads[(size_t)g * width + k] = 0.0f;
+    return;
+  }
   float tt[10];
 #pragma unroll
   for (int k = 0; k < 10; ++k) tt[k] = transforms[(size_t)g * 10 + k];
@@ -248,15 +259,16 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t n, 
   float* d = grads + (size_t)g * width;
   const float gv[10] = {o.v_mean.x, o.v_mean.y, o.v_mean.z, o.v_q.w, o.v_q.x, o.v_q.y, o.v_q.z,
                         o.v_scale.x, o.v_scale.y, o.v_scale.z};
+  // 0 + x (not x) on a fresh row keeps the sign of zero of an accumulation
 #pragma unroll
-  for (int k = 0; k < 10; ++k) d[k] += gv[k];
+  for (int k = 0; k < 10; ++k) d[k] = (fresh ? 0.0f : d[k]) + gv[k];
   float b[16];
   sh_basis_all(o.dir.x, o.dir.y, o.dir.z, b);
   for (int k = 0; k < nc; ++k) {
 #pragma unroll
-    for (int c = 0; c < 3; ++c) d[10 + k * 3 + c] += rr[5 + c] * b[k];
+    for (int c = 0; c < 3; ++c) d[10 + k * 3 + c] = (fresh ? 0.0f : d[10 + k * 3 + c]) + rr[5 + c] * b[k];
   }
-  d[width - 1] += o.v_raw;
+  d[width - 1] = (fresh ? 0.0f : d[width - 1]) + o.v_raw;
   refine[g] += clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
 }
 
@@ -276,6 +288,19 @@ struct Q8Args {
   uint32_t seed;
   float noise_scale, noise_limit;
   uint32_t noise_seed;
+};
+
+// Sharded update over peer replicas (MODE 2 of q8_kernel); world = 1 and
+// zero offsets otherwise.
+struct PeerArgs {
+  uint32_t world, rank;
+  uint32_t cta_begin;  // first CTA (256 splats) of the shard
+  uint32_t m_off;      // first splat covered by the moment arrays
+  const float* grads[VS_PEER_MAX];
+  const float* vis[VS_PEER_MAX];
+  float* t[VS_PEER_MAX];
+  float* sh[VS_PEER_MAX];
+  float* o[VS_PEER_MAX];
 };
 
 constexpr uint32_t Q8_SPLATS = 256;
@@ -323,6 +348,7 @@ struct Q8Shared {
   const float* bas;    // [256][16]
   const float* noise;  // [256][3]
   const float* lr_t;   // [10]
+  const uint32_t* vmask;  // [256] ranks whose rows are read (MODE 2)
 };
 
 // One 256-value block of one parameter tensor, by one warp.  `W` is the
@@ -332,14 +358,16 @@ struct Q8Shared {
 // and two 4-byte loads per code stream per lane; all loads are issued before
 // any arithmetic.  A block that runs past the tensor's end (only in the last
 // CTA) takes guarded scalar accesses instead.
-template <bool kDense, uint32_t W, int KIND>
+template <int MODE, uint32_t W, int KIND>
 __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t vals_here, float* __restrict__ tensor,
                                          const Q8T& q, size_t t_base, uint32_t salt, const Q8Args& a,
-                                         const Q8Shared& sm, const float* __restrict__ grow, uint32_t width) {
+                                         const Q8Shared& sm, const float* __restrict__ grow, uint32_t width,
+                                         const PeerArgs& pa) {
   float* p = tensor + t_base;
-  uint8_t* mcp = q.mc + t_base;
-  uint8_t* vcp = q.vc + t_base;
-  const size_t blk = t_base / 256u + jb;
+  const size_t mb = MODE == 2 ? t_base - (size_t)pa.m_off * W : t_base;  // offset in the moment arrays
+  uint8_t* mcp = q.mc + mb;
+  uint8_t* vcp = q.vc + mb;
+  const size_t blk = mb / 256u + jb;
   const float ms = q.ms[blk], vsc = q.vs[blk];
   const uint32_t v0 = jb * 256u;
   const bool full = v0 + 256u <= vals_here;
@@ -381,8 +409,20 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
         lr[k] = sm.lr_t[col];
         if (col < 3u) nz[k] = ok ? sm.noise[s * 3u + col] : 0.0f;
       } else if (KIND == 1) {
-        if (kDense) g[k] = ok ? grow[(size_t)s * width + 10u + col] : 0.0f;
-        else g[k] = ok ? sm.vc[s * 3u + r3] * sm.bas[s * 16u + c3] : 0.0f;
+        if (MODE == 1) {
+          g[k] = ok ? grow[(size_t)s * width + 10u + col] : 0.0f;
+        } else if (MODE == 2) {
+          float acc = 0.0f;
+          if (ok) {
+            const uint32_t vm = sm.vmask[s];
+            const size_t off = ((size_t)(t_base / W) + s) * width + 10u + col;
+            for (uint32_t r = 0; r < pa.world; ++r)
+              if ((vm >> r) & 1u) acc += pa.grads[r][off];
+          }
+          g[k] = acc;
+        } else {
+          g[k] = ok ? sm.vc[s * 3u + r3] * sm.bas[s * 16u + c3] : 0.0f;
+        }
         lr[k] = c3 == 0u ? a.lr_dc : a.lr_rest;
       } else {
         g[k] = ok ? sm.go[li] : 0.0f;
@@ -459,8 +499,19 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
       mo |= qm << (8 * e);
       vo |= qr << (8 * e);
     }
+    // MODE 2 stores the parameters into every replica (peers over NVLink)
+    const uint32_t nrep = MODE == 2 ? pa.world : 1u;
+    for (uint32_t r = 0; r < nrep; ++r) {
+      float* pr = MODE == 2 ? (KIND == 0 ? pa.t[r] : (KIND == 1 ? pa.sh[r] : pa.o[r])) + t_base : p;
+      if (full) {
+        *reinterpret_cast<float4*>(pr + li0) = make_float4(pv[4 * h], pv[4 * h + 1], pv[4 * h + 2], pv[4 * h + 3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (li0 + (uint32_t)e < vals_here) pr[li0 + e] = pv[4 * h + e];
+      }
+    }
     if (full) {
-      *reinterpret_cast<float4*>(p + li0) = make_float4(pv[4 * h], pv[4 * h + 1], pv[4 * h + 2], pv[4 * h + 3]);
       *reinterpret_cast<uint32_t*>(mcp + li0) = mo;
       *reinterpret_cast<uint32_t*>(vcp + li0) = vo;
     } else {
@@ -468,7 +519,6 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
       for (int e = 0; e < 4; ++e) {
         const uint32_t li = li0 + (uint32_t)e;
         if (li < vals_here) {
-          p[li] = pv[4 * h + e];
           mcp[li] = (uint8_t)(mo >> (8 * e));
           vcp[li] = (uint8_t)(vo >> (8 * e));
         }
@@ -477,22 +527,28 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
   }
 }
 
-template <bool kDense>
+// MODE 0: single view, VJP fused (v_combined rows); MODE 1: dense gradient
+// rows `grads`; MODE 2: dense rows of every rank summed from peer memory, for
+// the shard of CTAs starting at pa.cta_begin, parameters stored to all
+// replicas.  `n` is one past the last splat this launch may touch.
+template <int MODE>
 __global__ void __launch_bounds__(Q8_SPLATS, 3) q8_kernel(
     Uniforms u, uint32_t n, float* __restrict__ transforms, float* __restrict__ sh, float* __restrict__ raw_opac,
     const float* __restrict__ min_scale, const uint32_t* __restrict__ compact_from_global,
     const float* __restrict__ v_combined, const float* __restrict__ grads, Q8T mt, Q8T msh, Q8T mo, Q8Args a,
     const float* __restrict__ opacities, const float* __restrict__ visible, const float* __restrict__ max_radius,
-    float* __restrict__ refine_norm, float* __restrict__ vis_count, float* __restrict__ max_screen) {
+    float* __restrict__ refine_norm, float* __restrict__ vis_count, float* __restrict__ max_screen, PeerArgs pa) {
   __shared__ float s_gt[Q8_SPLATS * 10];
   __shared__ float s_go[Q8_SPLATS];
   __shared__ float s_vc[Q8_SPLATS * 3];
   __shared__ float s_bas[Q8_SPLATS * 16];
   __shared__ float s_noise[Q8_SPLATS * 3];
+  __shared__ uint32_t s_vmask[MODE == 2 ? Q8_SPLATS : 1];
   __shared__ float s_lr[10];
+  constexpr bool kDense = MODE != 0;
 
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-  const uint32_t base = blockIdx.x * Q8_SPLATS;
+  const uint32_t base = ((MODE == 2 ? pa.cta_begin : 0u) + blockIdx.x) * Q8_SPLATS;
   if (tid == 0) {
 #pragma unroll
     for (int k = 0; k < 10; ++k) s_lr[k] = a.lr_t[k];
@@ -509,12 +565,29 @@ __global__ void __launch_bounds__(Q8_SPLATS, 3) q8_kernel(
     for (int k = 0; k < 10; ++k) gr[k] = 0.0f;
     float go = 0.0f, vc0 = 0.0f, vc1 = 0.0f, vc2 = 0.0f, dx = 0.0f, dy = 0.0f, dz = 1.0f;
     float nx = 0.0f, ny = 0.0f, nz = 0.0f;
+    float vis_g = 0.0f;  // views that saw the splat (MODE 1 and 2)
     if (g < n) {
-      if (kDense) {
+      if (MODE == 2) {
+        uint32_t vm = 0;
+        for (uint32_t r = 0; r < pa.world; ++r) {
+          const float vr = pa.vis[r][g];
+          if (vr > 0.0f) vm |= 1u << r;
+          vis_g += vr;
+        }
+        for (uint32_t r = 0; r < pa.world; ++r) {
+          if (!((vm >> r) & 1u)) continue;
+          const float* d = pa.grads[r] + (size_t)g * width;
+#pragma unroll
+          for (int k = 0; k < 10; ++k) gr[k] += d[k];
+          go += d[width - 1];
+        }
+        s_vmask[tid] = vm;
+      } else if (kDense) {
         const float* d = grads + (size_t)g * width;
 #pragma unroll
         for (int k = 0; k < 10; ++k) gr[k] = d[k];
         go = d[width - 1];
+        if (visible) vis_g = visible[g];
       } else {
         const uint32_t row = compact_from_global[g];
         float refine = 0.0f;
@@ -549,12 +622,12 @@ __global__ void __launch_bounds__(Q8_SPLATS, 3) q8_kernel(
         const float o = 1.0f / (1.0f + vs_expf(-raw_opac[g]));
         go = go + a.opac_reg * o * (1.0f - o);
       }
-      if (visible && a.noise_scale != 0.0f) {
+      if ((visible || MODE == 2) && a.noise_scale != 0.0f) {
         // without per-view opacities (the multi-view path) the gate uses the
         // unfloored sigmoid opacity, which projection also reports when no
         // min_scale floor is set
         const float op = opacities ? opacities[g] : 1.0f / (1.0f + vs_expf(-raw_opac[g]));
-        mean_noise(g, op, visible[g], a.noise_scale, a.noise_limit, a.noise_seed, &nx, &ny, &nz);
+        mean_noise(g, op, kDense ? vis_g : visible[g], a.noise_scale, a.noise_limit, a.noise_seed, &nx, &ny, &nz);
       }
     }
 #pragma unroll
@@ -580,25 +653,33 @@ __global__ void __launch_bounds__(Q8_SPLATS, 3) q8_kernel(
   const uint32_t nb_t = div_up(splats_here * 10u, 256u);
   const uint32_t nb_sh = div_up(splats_here * wsh, 256u);
   const uint32_t total_blocks = nb_t + nb_sh + 1u;
-  const Q8Shared sm{s_gt, s_go, s_vc, s_bas, s_noise, s_lr};
-  const float* grow = kDense ? grads + (size_t)base * width : nullptr;
+  const Q8Shared sm{s_gt, s_go, s_vc, s_bas, s_noise, s_lr, s_vmask};
+  const float* grow = MODE == 1 ? grads + (size_t)base * width : nullptr;
   for (uint32_t job = warp; job < total_blocks; job += Q8_WARPS) {
     if (job < nb_t) {
-      q8_block<kDense, 10, 0>(lane, job, splats_here * 10u, transforms, mt, (size_t)base * 10u, SALT_T, a, sm,
-                              grow, width);
+      q8_block<MODE, 10, 0>(lane, job, splats_here * 10u, transforms, mt, (size_t)base * 10u, SALT_T, a, sm,
+                            grow, width, pa);
     } else if (job < nb_t + nb_sh) {
       const uint32_t jb = job - nb_t;
       const size_t tb = (size_t)base * wsh;
       switch (u.sh_degree) {
-        case 3: q8_block<kDense, 48, 1>(lane, jb, splats_here * 48u, sh, msh, tb, SALT_SH, a, sm, grow, width); break;
-        case 2: q8_block<kDense, 27, 1>(lane, jb, splats_here * 27u, sh, msh, tb, SALT_SH, a, sm, grow, width); break;
-        case 1: q8_block<kDense, 12, 1>(lane, jb, splats_here * 12u, sh, msh, tb, SALT_SH, a, sm, grow, width); break;
-        default: q8_block<kDense, 3, 1>(lane, jb, splats_here * 3u, sh, msh, tb, SALT_SH, a, sm, grow, width); break;
+        case 3: q8_block<MODE, 48, 1>(lane, jb, splats_here * 48u, sh, msh, tb, SALT_SH, a, sm, grow, width, pa); break;
+        case 2: q8_block<MODE, 27, 1>(lane, jb, splats_here * 27u, sh, msh, tb, SALT_SH, a, sm, grow, width, pa); break;
+        case 1: q8_block<MODE, 12, 1>(lane, jb, splats_here * 12u, sh, msh, tb, SALT_SH, a, sm, grow, width, pa); break;
+        default: q8_block<MODE, 3, 1>(lane, jb, splats_here * 3u, sh, msh, tb, SALT_SH, a, sm, grow, width, pa); break;
       }
     } else {
-      q8_block<kDense, 1, 2>(lane, 0, splats_here, raw_opac, mo, (size_t)base, SALT_O, a, sm, grow, width);
+      q8_block<MODE, 1, 2>(lane, 0, splats_here, raw_opac, mo, (size_t)base, SALT_O, a, sm, grow, width, pa);
     }
   }
+  // Peer stores complete before the barrier that follows this kernel.
+  if (MODE == 2) __threadfence_system();
+}
+
+PeerArgs single_rank() {
+  PeerArgs pa{};
+  pa.world = 1;
+  return pa;
 }
 
 __global__ void stats_kernel(uint32_t n, float* norm, float* vis, float* screen, const float* weight,
@@ -709,11 +790,11 @@ VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* c
   if (count_sh >= 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "step_q8: %llu SH values exceed u32 indexing", (unsigned long long)count_sh);
   if (num_splats == 0) return VS_OK;
   const Q8Args a = to_args(*q8);
-  q8_kernel<false><<<vs::div_up(num_splats, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
+  q8_kernel<0><<<vs::div_up(num_splats, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
       frame->u, num_splats, transforms, sh_coeffs, raw_opacities, nullptr,
       (const uint32_t*)frame->compact_from_global.ptr, v_combined, nullptr, to_q8(mom_t), to_q8(mom_sh), to_q8(mom_o),
       a, (const float*)frame->opacities.ptr, visible, (const float*)frame->max_radius.ptr, refine_norm, vis_count,
-      max_screen); ++ctx->launches;
+      max_screen, single_rank()); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "step_q8 launch");
 }
 
@@ -748,10 +829,51 @@ VS_API vs_status vs_adam_q8_dense(vs_ctx* ctx, uint32_t num_splats, int32_t sh_d
   vs::Uniforms u{};
   u.sh_degree = sh_degree;
   const Q8Args a = to_args(*q8);
-  q8_kernel<true><<<vs::div_up(num_splats, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
+  q8_kernel<1><<<vs::div_up(num_splats, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
       u, num_splats, transforms, sh_coeffs, raw_opacities, nullptr, nullptr, nullptr, grads, to_q8(mom_t),
-      to_q8(mom_sh), to_q8(mom_o), a, opacities, visible, nullptr, nullptr, nullptr, nullptr); ++ctx->launches;
+      to_q8(mom_sh), to_q8(mom_o), a, opacities, visible, nullptr, nullptr, nullptr, nullptr, single_rank());
+  ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "adam_q8_dense launch");
+}
+
+VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, uint32_t splat_begin,
+                                 uint32_t splat_end, const vs_peer_set* peers, vs_q8_tensor mom_t,
+                                 vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!q8 || !peers || !q8_valid(mom_t) || !q8_valid(mom_sh) || !q8_valid(mom_o) || sh_degree < 0 || sh_degree > 3)
+    return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: bad arguments");
+  if (peers->world == 0 || peers->world > VS_PEER_MAX || peers->rank >= peers->world)
+    return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: world %u rank %u", peers->world, peers->rank);
+  if (splat_begin % Q8_SPLATS != 0 || splat_begin > splat_end || splat_end > num_splats)
+    return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: shard [%u, %u) of %u splats", splat_begin, splat_end,
+                   num_splats);
+  const uint64_t count_sh = (uint64_t)num_splats * 3 * (sh_degree + 1) * (sh_degree + 1);
+  if (count_sh >= 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "adam_q8_peer: %llu SH values exceed u32 indexing", (unsigned long long)count_sh);
+  PeerArgs pa{};
+  pa.world = peers->world;
+  pa.rank = peers->rank;
+  pa.cta_begin = splat_begin / Q8_SPLATS;
+  pa.m_off = splat_begin;
+  for (uint32_t r = 0; r < peers->world; ++r) {
+    if (!peers->grads[r] || !peers->vis[r] || !peers->transforms[r] || !peers->sh_coeffs[r] ||
+        !peers->raw_opacities[r])
+      return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: null buffer of rank %u", r);
+    pa.grads[r] = peers->grads[r];
+    pa.vis[r] = peers->vis[r];
+    pa.t[r] = peers->transforms[r];
+    pa.sh[r] = peers->sh_coeffs[r];
+    pa.o[r] = peers->raw_opacities[r];
+  }
+  if (splat_end == splat_begin) return VS_OK;
+  vs::Uniforms u{};
+  u.sh_degree = sh_degree;
+  const Q8Args a = to_args(*q8);
+  const uint32_t me = peers->rank;
+  q8_kernel<2><<<vs::div_up(splat_end - splat_begin, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
+      u, splat_end, pa.t[me], pa.sh[me], pa.o[me], nullptr, nullptr, nullptr, nullptr, to_q8(mom_t), to_q8(mom_sh),
+      to_q8(mom_o), a, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, pa);
+  ++ctx->launches;
+  return vs_cuda(ctx, cudaGetLastError(), "adam_q8_peer launch");
 }
 
 VS_API vs_status vs_gather_stats(vs_ctx* ctx, uint32_t n, float* refine_norm, float* vis_count, float* max_screen,

@@ -318,6 +318,15 @@ def adam_q8_dense(sh_degree: int, transforms, sh_coeffs, raw_opacities, grads, m
                                        ctypes.byref(q8), _ptr(opacities), _ptr(visible)))
 
 
+def adam_q8_peer(sh_degree: int, num_splats: int, splat_begin: int, splat_end: int, peers: N.PeerSet,
+                 mom_t: Q8Moments, mom_sh: Q8Moments, mom_o: Q8Moments, q8: N.Q8Cfg, device=None):
+    """Sharded Q8 Adam over the replicas of a view-parallel step (vs_adam_q8_peer);
+    `peers` holds every rank's buffers as raw device addresses."""
+    ctx = context(device)
+    ctx.check(ctx.lib.vs_adam_q8_peer(ctx.h, num_splats, sh_degree, splat_begin, splat_end, ctypes.byref(peers),
+                                      mom_t.c(), mom_sh.c(), mom_o.c(), ctypes.byref(q8)))
+
+
 def gather_stats(refine_norm, vis_count, max_screen, refine_weight, visible, radius):
     ctx = context(refine_norm.device)
     ctx.check(ctx.lib.vs_gather_stats(ctx.h, refine_norm.shape[0], _ptr(refine_norm), _ptr(vis_count),

@@ -9,10 +9,15 @@ one all-reduce (sum) over the ranks gives every replica the gradient of the
 whole batch; each rank then runs the same deterministic 8-bit-moment Adam, so
 the replicas stay bit-identical.
 
-The per-step exchange is one flat buffer: the dense gradient followed by the
-per-splat count of views that saw the splat (the mean-noise gate).  torch.
-distributed (NCCL over NVLink on the GPUs) carries it; `exchange` is injectable
-so the host logic can be exercised with gloo ranks on the CPU.
+Two exchanges are available.  With a `PeerGroup` (the GPU path) the ranks'
+gradient rows, view counts and parameter replicas live in buffers every rank
+maps over NVLink: after a device barrier each rank runs the 8-bit-moment Adam
+on its shard of the splats only (vs_adam_q8_peer), summing the rows of the
+ranks that saw each splat straight from their memory and storing the new
+parameters into every replica, and a second barrier ends the step.  Without
+one, the dense gradient and the view counts go through one flat all-reduce
+(`exchange`, injectable so the host logic runs with gloo ranks on the CPU) and
+every rank runs the full replicated Adam.
 """
 from __future__ import annotations
 
@@ -23,7 +28,9 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
+from . import _native as N
 from . import ops
+from .peer import PeerGroup
 from .trainer import SceneBatch, Splats, SplatTrainer, TrainConfig, TrainStepStats
 
 
@@ -58,25 +65,79 @@ class ViewParallelTrainer(SplatTrainer):
     dense gradient before the replicated Q8 Adam step."""
 
     def __init__(self, config: TrainConfig, device, exchange: Callable[[torch.Tensor], None] = all_reduce_sum,
-                 **kw):
+                 peer: PeerGroup | None = None, **kw):
         assert config.optimizer == "q8", "the view-parallel path steps the 8-bit m+v optimizer"
         super().__init__(config, device, **kw)
         self.exchange = exchange
+        self.peer = peer
         self.flat = None
+        self.peer_set = None
+
+    @staticmethod
+    def shard_of(n: int, world: int, rank: int) -> tuple[int, int]:
+        """Rank's splats [begin, end): contiguous runs of whole 256-splat blocks."""
+        blocks = (n + 255) // 256
+        b0, b1 = rank * blocks // world, (rank + 1) * blocks // world
+        return b0 * 256, min(b1 * 256, n)
+
+    def adopt(self, splats: Splats) -> Splats:
+        """With a peer group, copies the splats (identical on every rank) into
+        replicas that all ranks map and returns them; step_views must be given
+        the returned splats.  Without one, returns `splats` unchanged."""
+        if self.peer is None:
+            return splats
+        g, n = self.peer, splats.num_splats
+        nc = splats.sh_coeffs.shape[1]
+        width = 10 + nc * 3 + 1
+        f32 = torch.float32
+        addr_t, addr_sh, addr_o = g.alloc(n * 10, f32), g.alloc(n * nc * 3, f32), g.alloc(n, f32)
+        addr_g = g.alloc(n * width, f32, zero=True)
+        addr_v = g.alloc(n, f32, zero=True)
+        t = g.local(addr_t, n * 10, f32).view(n, 10)
+        sh = g.local(addr_sh, n * nc * 3, f32).view(n, nc, 3)
+        o = g.local(addr_o, n, f32)
+        t.copy_(splats.transforms)
+        sh.copy_(splats.sh_coeffs.float())
+        o.copy_(splats.raw_opacities)
+        self._grads = g.local(addr_g, n * width, f32).view(n, width)
+        self._vis = g.local(addr_v, n, f32)
+        ps = N.PeerSet()
+        ps.world, ps.rank = g.world, g.rank
+        for r in range(g.world):
+            ps.grads[r], ps.vis[r] = addr_g[r], addr_v[r]
+            ps.transforms[r], ps.sh_coeffs[r], ps.raw_opacities[r] = addr_t[r], addr_sh[r], addr_o[r]
+        self.peer_set = ps
+        self.shard = self.shard_of(n, g.world, g.rank)
+        m = self.shard[1] - self.shard[0]
+        self.optim = dict(t=ops.Q8Moments(m * 10, self.device), sh=ops.Q8Moments(m * nc * 3, self.device),
+                          o=ops.Q8Moments(m, self.device), time=0)
+        self.record = None
+        self._resident = t.data_ptr()
+        return Splats(t, sh, o)
 
     def step_views(self, batches: Sequence[SceneBatch], splats: Splats) -> tuple[Splats, TrainStepStats]:
         c = self.config
+        peer = self.peer
+        if peer is not None and self.peer_set is None:
+            raise RuntimeError("call adopt(splats) before step_views with a peer group")
+        if peer is not None and splats.transforms.data_ptr() != self._resident:
+            raise RuntimeError("step_views needs the splats returned by adopt()")
         if self.optim is None:
             self._init_state(splats)
         self.step_count += 1
         n = splats.num_splats
         width = 10 + splats.sh_coeffs.shape[1] * 3 + 1
-        layout = ExchangeLayout(n, width)
-        if self.flat is None or self.flat.numel() != layout.size:
-            self.flat = torch.zeros(layout.size, dtype=torch.float32, device=self.device)
+        if peer is not None:
+            # rows are overwritten where vis is 0, so only the counts are cleared
+            grads, vis = self._grads, self._vis
+            vis.zero_()
         else:
-            self.flat.zero_()
-        grads, vis = layout.views(self.flat)
+            layout = ExchangeLayout(n, width)
+            if self.flat is None or self.flat.numel() != layout.size:
+                self.flat = torch.zeros(layout.size, dtype=torch.float32, device=self.device)
+            else:
+                self.flat.zero_()
+            grads, vis = layout.views(self.flat)
         refine = self._buf("refine_dense", (n,), torch.float32)
         refine.zero_()
         losses = []
@@ -99,7 +160,8 @@ class ViewParallelTrainer(SplatTrainer):
                           refine, visible=out.visible, vis_accum=vis)
             num_visible += out.num_visible
             num_isect += out.num_intersections
-        self.exchange(self.flat)
+        if peer is None:
+            self.exchange(self.flat)
         self.optim["time"] += 1
         time = self.optim["time"]
         o = self.optim
@@ -108,8 +170,14 @@ class ViewParallelTrainer(SplatTrainer):
                         opac_reg=opac_reg, eps=c.adam_epsilon,
                         noise_scale=c.mean_noise_weight * self.lr_unit() * self.median_scale,
                         noise_limit=self.median_scale, noise_seed=int(self.rng.integers(0, 2 ** 32)))
-        ops.adam_q8_dense(splats.sh_degree, splats.transforms, splats.sh_coeffs, splats.raw_opacities, grads,
-                          o["t"], o["sh"], o["o"], q8, opacities=None, visible=vis)
+        if peer is not None:
+            peer.barrier()  # every rank's rows and counts are complete
+            ops.adam_q8_peer(splats.sh_degree, n, self.shard[0], self.shard[1], self.peer_set, o["t"], o["sh"],
+                             o["o"], q8, device=self.device)
+            peer.barrier()  # every replica holds the new parameters
+        else:
+            ops.adam_q8_dense(splats.sh_degree, splats.transforms, splats.sh_coeffs, splats.raw_opacities, grads,
+                              o["t"], o["sh"], o["o"], q8, opacities=None, visible=vis)
         loss_total = torch.stack(losses).sum() if losses else torch.zeros((), device=self.device)
         stats = TrainStepStats(loss=loss_total, num_visible=num_visible, num_intersections=num_isect,
                                lr_mean=float(self.transforms_lr()[0]), lr_coeffs=c.lr_coeffs_dc, lr_opac=c.lr_opac)
