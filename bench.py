@@ -16,7 +16,13 @@ With N GPUs every rank trains its own view per step and the dense gradient is
 all-reduced over NCCL before the replicated Adam step (weak scaling: one view
 per GPU per step); value = views/s over the whole job = iterations/s at N = 1.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+With --config 3 it runs BASELINE configuration 3 instead: 6,000,000 splats
+(configuration-2 distributions) and a fixed global batch of 8 views of
+1920x1080 (fx = fy = 1600) per step, split evenly over 1, 2, 4 or 8 GPUs
+(strong scaling; value = global-batch steps/s).  Every GPU count, one
+included, runs the peer-memory view-parallel trainer.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--config 2|3]
 """
 from __future__ import annotations
 
@@ -46,10 +52,14 @@ def parse():
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--splats", type=int, default=N_SPLATS)
+    p.add_argument("--splats", type=int, default=None, help="default: 3M (config 2), 6M (config 3)")
+    p.add_argument("--config", type=int, default=2, choices=[2, 3])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
-    return p.parse_args()
+    a = p.parse_args()
+    if a.splats is None:
+        a.splats = N_SPLATS if a.config == 2 else 6_000_000
+    return a
 
 
 def peaks():
@@ -123,9 +133,12 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------ workloads ----
-def make_workload(n_splats: int):
+def make_workload(n_splats: int, config: int = 2):
     from vauss_b200 import scenes
-    sp, cams = scenes.config_train(seed=3, n=n_splats, views=N_VIEWS)
+    if config == 3:
+        sp, cams = scenes.config_multiview(seed=4, n=n_splats, views=8)
+    else:
+        sp, cams = scenes.config_train(seed=3, n=n_splats, views=N_VIEWS)
     tgt = scenes.random_splats(n_splats, 1003, mean_lo=-5.0, mean_hi=5.0, log_scale_mu=-4.5, log_scale_sigma=0.6,
                                opac_mu=0.0, opac_sigma=1.5, sh_degree=3)
     return sp, tgt, cams
@@ -166,12 +179,19 @@ def run_ours(args):
     dev = torch.device(f"cuda:{local}")
     torch.cuda.set_device(dev)
 
-    sp, tgt, cams = make_workload(args.splats)
+    multiview = args.config == 3
+    if multiview and 8 % world:
+        raise SystemExit("config 3 splits its 8 views over 1, 2, 4 or 8 GPUs")
+    sp, tgt, cams = make_workload(args.splats, args.config)
     splats = Splats.from_numpy(sp, dev)
     # targets: rendered from the second splat set, quantised to RGBA8
     tsplats = Splats.from_numpy(tgt, dev)
     cfg_t = ops.render_cfg(3, mip=True)
-    views = [(rank * N_TARGETS + k) % N_VIEWS for k in range(N_TARGETS)]
+    if multiview:  # this rank's share of the fixed global batch
+        per_rank = 8 // world
+        views = [rank * per_rank + k for k in range(per_rank)]
+    else:
+        views = [(rank * N_TARGETS + k) % N_VIEWS for k in range(N_TARGETS)]
     targets = []
     for vi in views:
         out = ops.render(cams[vi], cfg_t, tsplats.transforms, tsplats.sh_coeffs, tsplats.raw_opacities)
@@ -184,18 +204,22 @@ def run_ours(args):
     median_scale = float(np.median(np.exp(sp.transforms[:, 7:10])))
     kw = dict(scene_extent=8.0, median_scale=median_scale)
     peer = None
-    if world > 1:
+    if world > 1 or multiview:
         from vauss_b200.peer import PeerGroup, gather_bytes_nccl
-        peer = PeerGroup(dev, world, rank, lambda b: gather_bytes_nccl(b, dev))
+        gather = (lambda b: gather_bytes_nccl(b, dev)) if world > 1 else (lambda b: [b])
+        peer = PeerGroup(dev, world, rank, gather)
         trainer = ViewParallelTrainer(cfg, dev, peer=peer, **kw)
         splats = trainer.adopt(splats)
     else:
         trainer = SplatTrainer(cfg, dev, **kw)
 
     def step(k, host=False, pinned=None):
+        src = pinned if host else targets
+        if multiview:
+            return trainer.step_views([SceneBatch(src[j], cams[views[j]], views[j]) for j in range(len(views))],
+                                      splats)
         vi = k % N_TARGETS
-        gt = pinned[vi] if host else targets[vi]
-        b = SceneBatch(gt, cams[views[vi]], views[vi])
+        b = SceneBatch(src[vi], cams[views[vi]], views[vi])
         if world > 1:
             return trainer.step_views([b], splats)
         return trainer.step(b, splats)
@@ -231,7 +255,7 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = world * args.steps / (ms_max / 1e3)
+    value = (1 if multiview else world) * args.steps / (ms_max / 1e3)
 
     # ---- end to end through the public API: host GT in, loss out ----
     e2e = None
@@ -253,8 +277,9 @@ def run_ours(args):
         te = torch.tensor([ems], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        h2d = int(targets[0].numel() * 4)
-        e2e = {"value": world * args.steps / (float(te.item()) / 1e3), "unit": "iters/s",
+        h2d = int(sum(tg.numel() * 4 for tg in targets)) if multiview else int(targets[0].numel() * 4)
+        e2e = {"value": (1 if multiview else world) * args.steps / (float(te.item()) / 1e3),
+               "unit": "steps/s" if multiview else "iters/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
                "api": ("ViewParallelTrainer.step_views (vs_render_forward, vs_loss, vs_rasterize_backward, "
                        "vs_vjp_dense, vs_peer_barrier, vs_adam_q8_peer)" if world > 1 else
@@ -263,7 +288,7 @@ def run_ours(args):
     # ---- per-stage device times (CUDA events on the launching stream) ----
     stages = None
     roofline = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not multiview:
         stages = profile_stages(trainer, splats, targets, cams, views, dev, reps=3)
         peak, which = peaks()
         n, v, i = splats.num_splats, stages.pop("_v"), stages.pop("_i")
@@ -280,19 +305,28 @@ def run_ours(args):
                     "note": "raster stages are FP32-issue bound; see profiles/ for issue utilisation"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not multiview:
         cpu = cpu_baseline(sp, tgt, cams, views, gt=targets[0].cpu().numpy().view(np.uint32))
 
-    out = {"metric": METRIC, "value": round(value, 3), "unit": "iters/s", "n_gpus": world, "steps": args.steps,
-           "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
-           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": "config 2: 3M SH-3 splats, 1600x1060, 1 view/step/GPU, L1+0.2 D-SSIM, "
-                                  "8-bit m+v Adam (block 256)", "splats": splats.num_splats, "width": 1600,
-                      "height": 1060, "views_per_step": world, "optimizer": "q8",
+    if multiview:
+        workload = dict(workload="config 3: 6M SH-3 splats, global batch of 8 views of 1920x1080 split over the "
+                                 f"GPUs ({len(views)} per GPU), L1+0.2 D-SSIM, 8-bit m+v Adam (block 256)",
+                        splats=splats.num_splats, width=1920, height=1080, views_per_step=8)
+    else:
+        workload = dict(workload="config 2: 3M SH-3 splats, 1600x1060, 1 view/step/GPU, L1+0.2 D-SSIM, "
+                                 "8-bit m+v Adam (block 256)", splats=splats.num_splats, width=1600, height=1060,
+                        views_per_step=world)
+    out = {"metric": ("view-parallel steps/s @6M splats, 8 views of 1920×1080 per step" if multiview else METRIC),
+           "value": round(value, 3), "unit": "steps/s" if multiview else "iters/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+           "higher_is_better": True, "scaling": "strong" if multiview else "weak", "vs_baseline": None,
+           "dtype": "f32", "data": "synthetic",
+           "config": {**workload, "optimizer": "q8",
                       "parallelism": (f"view-parallel x{world}: dense gradient rows read over NVLink peer "
                                       f"memory by a sharded fused Adam that stores to every replica"
-                                      if world > 1 else "single GPU"),
-                      "l2": "inputs larger than L2 (params + moments ~0.9 GB)", **counts},
+                                      if world > 1 or multiview else "single GPU"),
+                      "l2": ("inputs larger than L2 (params + moments ~%.1f GB)"
+                             % (splats.num_splats * (236 + 122) / 1e9)), **counts},
            "gpu_launches": int(launches), "clocks": clk.summary()}
     if roofline:
         out["roofline"] = roofline
@@ -304,6 +338,10 @@ def run_ours(args):
         out["e2e"] = {k: (round(v, 3) if isinstance(v, float) else v) for k, v in e2e.items()}
     if rank == 0:
         print(json.dumps(out), flush=True)
+    if world == 1 and peer is not None:
+        torch.cuda.synchronize(dev)
+        peer.check()
+        peer.close()
     if world > 1:
         dist.barrier()
         torch.cuda.synchronize(dev)

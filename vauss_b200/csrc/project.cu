@@ -174,6 +174,7 @@ __global__ void __launch_bounds__(PROJ_BLOCK, 3) project_kernel(
   __shared__ uint32_t s_bid;
   __shared__ uint32_t s_warp_cnt[PROJ_BLOCK / 32];
   __shared__ uint32_t s_block_off;
+  __shared__ uint32_t s_total;
   __shared__ unsigned long long s_isect;
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   if (tid == 0) {
@@ -199,8 +200,24 @@ __global__ void __launch_bounds__(PROJ_BLOCK, 3) project_kernel(
     opacities[g] = o.floor_reached ? o.floor_opac : 0.0f;
     max_radius[g] = visible ? o.radius : 0.0f;
   }
-  // Colour of the visible splats, before the ranking below, so the SH loads
-  // are in flight while the block waits for its look-back.
+  // Block-level ranking of the visible splats; the block's count is published
+  // for the look-back at once, and the heavy work below (SH colour, tile
+  // counting) runs before this block looks back itself, so by then the blocks
+  // before it have usually published theirs.
+  const uint32_t ballot = __ballot_sync(0xffffffffu, visible);
+  const uint32_t warp_rank = __popc(ballot & ((1u << lane) - 1u));
+  if (lane == 0) s_warp_cnt[warp] = __popc(ballot);
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t total = 0;
+    for (uint32_t w = 0; w < PROJ_BLOCK / 32; ++w) {
+      const uint32_t c = s_warp_cnt[w];
+      s_warp_cnt[w] = total;
+      total += c;
+    }
+    s_total = total;
+    lb_store(&lookback[bid], ((bid == 0 ? 2ull : 1ull) << 32) | total);
+  }
   V3 col = {0.0f, 0.0f, 0.0f};
   if (visible) col = splat_color(sh, u.sh_half != 0, g, u.sh_degree, V3{t[0], t[1], t[2]}, u);
   // Tile counting (kernels/helpers.rs:254-273); large boxes are walked by the
@@ -228,27 +245,14 @@ __global__ void __launch_bounds__(PROJ_BLOCK, 3) project_kernel(
     pending &= pending - 1u;
   }
 
-  // Block-level ranking of the visible splats.
-  const uint32_t ballot = __ballot_sync(0xffffffffu, visible);
-  const uint32_t warp_rank = __popc(ballot & ((1u << lane) - 1u));
-  if (lane == 0) s_warp_cnt[warp] = __popc(ballot);
   unsigned long long hsum = hits;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) hsum += __shfl_xor_sync(0xffffffffu, hsum, off);
   if (lane == 0 && hsum) atomicAdd(&s_isect, hsum);
   __syncthreads();
   if (warp == 0) {
-    uint32_t total = 0;
-    if (lane == 0) {
-      for (uint32_t w = 0; w < PROJ_BLOCK / 32; ++w) {
-        const uint32_t c = s_warp_cnt[w];
-        s_warp_cnt[w] = total;
-        total += c;
-      }
-      if (s_isect) atomicAdd(isect_total, s_isect);
-      lb_store(&lookback[bid], ((bid == 0 ? 2ull : 1ull) << 32) | total);
-    }
-    total = __shfl_sync(0xffffffffu, total, 0);
+    const uint32_t total = s_total;
+    if (lane == 0 && s_isect) atomicAdd(isect_total, s_isect);
     // Decoupled look-back, a warp at a time: lane l reads the status of block
     // hi - l; the nearest published inclusive prefix ends the walk.  Positions
     // before block 0 read as an inclusive prefix of 0.

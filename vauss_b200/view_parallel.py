@@ -144,14 +144,32 @@ class ViewParallelTrainer(SplatTrainer):
         num_visible = num_isect = 0
         if self.frame is None:
             self.frame = ops.Frame(ops.context(self.device))
-        for b in batches:
-            gt = b.img_packed if b.img_packed.device == self.device else b.img_packed.to(self.device,
-                                                                                         non_blocking=True)
+        # host targets go up on a side stream, overlapped with the renders
+        gts, ready = [], []
+        host = [b for b in batches if b.img_packed.device != self.device]
+        if host:
+            cur = torch.cuda.current_stream(self.device)
+            if self._copy_stream is None:
+                self._copy_stream = torch.cuda.Stream(self.device)
+            self._copy_stream.wait_stream(cur)  # the previous step no longer reads the buffers
+        for i, b in enumerate(batches):
+            if b.img_packed.device == self.device:
+                gts.append(b.img_packed)
+                ready.append(None)
+                continue
+            dst = self._buf(f"gt{i}", tuple(b.img_packed.shape), b.img_packed.dtype)
+            with torch.cuda.stream(self._copy_stream):
+                dst.copy_(b.img_packed, non_blocking=True)
+            gts.append(dst)
+            ready.append(self._copy_stream.record_event())
+        for b, gt, ev in zip(batches, gts, ready):
             cam = b.camera
             cfg = ops.render_cfg(splats.sh_degree, mip=c.render_mode_mip, background=self.background())
             out = ops.render(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, frame=self.frame,
                              out_img=self._buf("img", (cam.height, cam.width, 4), torch.float32),
                              visible=self._buf("visible", (n,), torch.float32))
+            if ev is not None:
+                torch.cuda.current_stream(self.device).wait_event(ev)
             loss = ops.image_loss(out.out_img, gt, c.l1_weight, c.ssim_loss_weight)
             losses.append(loss.loss.clone())
             vc = ops.rasterize_bwd(out.frame, out.out_img, loss.dl_dpred,
