@@ -126,6 +126,17 @@ VS_API vs_status vs_render_project(vs_ctx* ctx, vs_frame* frame, const vs_camera
 VS_API vs_status vs_render_bin(vs_ctx* ctx, vs_frame* frame);
 VS_API vs_status vs_render_rasterize(vs_ctx* ctx, vs_frame* frame, float* out_img, float* visible);
 
+/* Inference render: render_splats with RasterPass::Forward (crates/splat-train-
+ * render/src/gaussian_splats.rs:511-527; kernels/rasterize.rs:380-410 with
+ * bwd_info off): the same projection, binning and compositing, written as
+ * packed RGBA8 out_rgba8 [H,W] u32 (r in the low byte; each channel
+ * clamp(255 c, 0, 255) converted toward zero, alpha = 1 - T), with no
+ * visible marks and no backward state (the frame cannot be differentiated). */
+VS_API vs_status vs_render_image(vs_ctx* ctx, vs_frame* frame, const vs_camera* cam, const vs_render_cfg* cfg,
+                                 uint32_t num_splats, const float* transforms, const void* sh_coeffs,
+                                 const float* raw_opacities, const float* min_scale, uint32_t* out_rgba8,
+                                 vs_render_counts* counts_out);
+
 /* ---- loss ------------------------------------------------------------------
  * Replaces LossOps::image_loss_forward_train + image_loss_backward_coeffs
  * (crates/splat-train-loss/src/lib.rs:238-469, :821-1028) fused in one pass:
@@ -176,7 +187,10 @@ VS_API vs_status vs_sh_step(vs_ctx* ctx, uint32_t num_splats, uint32_t row_width
                             const float* variance, const float* lr_scale, float beta, float factor, float inv1,
                             float inv2, float epsilon, float lr, uint32_t round_seed);
 
-/* ---- optimizer, 8-bit m+v mode (the benchmark configuration) -------------- */
+/* ---- optimizer, 8-bit m+v mode (the benchmark configuration) --------------
+ * The Q8 entry points move parameters and codes in 16-byte pieces: the
+ * parameter arrays (transforms, sh_coeffs, raw_opacities) and the code arrays
+ * must start on 16-byte boundaries (VS_ERR_INVALID otherwise). */
 typedef struct vs_q8_tensor { /* one parameter tensor's moments */
   uint8_t* m_codes;           /* [count] +128-biased signed codes */
   uint8_t* v_codes;           /* [count] sqrt(v) codes */

@@ -155,3 +155,18 @@ def test_abi_rejects_bad_arguments(cuda):
     st = ctx.lib.vs_render_project(ctx.h, fr.h, ctypes.byref(cam), ctypes.byref(cfg4), 1, None, None, None, None,
                                    None)
     assert st == 5
+
+
+def test_q8_rejects_unaligned_arrays(cuda):
+    """The Q8 kernels move parameters and codes in 16-byte pieces; a parameter
+    array that starts off a 16-byte boundary is refused before any launch."""
+    n = 300
+    t = torch.zeros(n * 10 + 1, device=cuda)[1:].view(n, 10)  # 4 bytes past an aligned start
+    sh = torch.zeros(n, 16, 3, device=cuda)
+    o = torch.zeros(n, device=cuda)
+    grads = torch.zeros(n, 10 + 48 + 1, device=cuda)
+    mom = [ops.Q8Moments(c, cuda) for c in (n * 10, n * 48, n)]
+    q8 = ops.q8_cfg(1, [1e-3] * 10, 1e-3, 1e-4, 1e-2)
+    with pytest.raises(_native.VsError) as e:
+        ops.adam_q8_dense(3, t, sh, o, grads, *mom, q8)
+    assert e.value.status == 1 and "16-byte aligned" in str(e.value)

@@ -92,6 +92,8 @@ _SIGS = {
                            c_vp, c_vp, c_vp, ctypes.POINTER(RenderCounts)], ctypes.c_int),
     "vs_render_bin": ([c_vp, c_vp], ctypes.c_int),
     "vs_render_rasterize": ([c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
+    "vs_render_image": ([c_vp, c_vp, ctypes.POINTER(VsCamera), ctypes.POINTER(RenderCfg), ctypes.c_uint32, c_vp, c_vp,
+                         c_vp, c_vp, c_vp, ctypes.POINTER(RenderCounts)], ctypes.c_int),
     "vs_loss": ([c_vp, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, ctypes.c_float, ctypes.c_float, c_vp, c_vp,
                  c_vp], ctypes.c_int),
     "vs_rasterize_backward": ([c_vp, c_vp, c_vp, c_vp, c_vp], ctypes.c_int),

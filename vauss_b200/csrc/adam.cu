@@ -721,6 +721,15 @@ Q8Args to_args(const vs_q8_cfg& c) {
 
 bool q8_valid(const vs_q8_tensor& t) { return t.m_codes && t.v_codes && t.m_scales && t.v_scales; }
 
+// The Q8 kernels move parameters and codes in 16-byte pieces (bulk copies and
+// vector accesses).
+bool a16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+bool q8_aligned(const void* t, const void* sh, const void* o, const vs_q8_tensor& mt, const vs_q8_tensor& msh,
+                const vs_q8_tensor& mo) {
+  return a16(t) && a16(sh) && a16(o) && a16(mt.m_codes) && a16(mt.v_codes) && a16(msh.m_codes) &&
+         a16(msh.v_codes) && a16(mo.m_codes) && a16(mo.v_codes);
+}
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -786,6 +795,8 @@ VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* c
     return vs_fail(ctx, VS_ERR_INVALID, "step_q8: null buffer");
   if ((refine_norm || vis_count || max_screen || q8->noise_scale != 0.0f) && !visible)
     return vs_fail(ctx, VS_ERR_INVALID, "step_q8: statistics and noise need `visible`");
+  if (!q8_aligned(transforms, sh_coeffs, raw_opacities, mom_t, mom_sh, mom_o))
+    return vs_fail(ctx, VS_ERR_INVALID, "step_q8: parameter and code arrays must be 16-byte aligned");
   const uint64_t count_sh = (uint64_t)num_splats * 3 * (cfg->sh_degree + 1) * (cfg->sh_degree + 1);
   if (count_sh >= 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "step_q8: %llu SH values exceed u32 indexing", (unsigned long long)count_sh);
   if (num_splats == 0) return VS_OK;
@@ -825,6 +836,8 @@ VS_API vs_status vs_adam_q8_dense(vs_ctx* ctx, uint32_t num_splats, int32_t sh_d
   if (!q8 || !transforms || !sh_coeffs || !raw_opacities || !grads || !q8_valid(mom_t) || !q8_valid(mom_sh) ||
       !q8_valid(mom_o) || sh_degree < 0 || sh_degree > 3)
     return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_dense: bad arguments");
+  if (!q8_aligned(transforms, sh_coeffs, raw_opacities, mom_t, mom_sh, mom_o))
+    return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_dense: parameter and code arrays must be 16-byte aligned");
   if (num_splats == 0) return VS_OK;
   vs::Uniforms u{};
   u.sh_degree = sh_degree;
@@ -858,6 +871,8 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
     if (!peers->grads[r] || !peers->vis[r] || !peers->transforms[r] || !peers->sh_coeffs[r] ||
         !peers->raw_opacities[r])
       return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: null buffer of rank %u", r);
+    if (!q8_aligned(peers->transforms[r], peers->sh_coeffs[r], peers->raw_opacities[r], mom_t, mom_sh, mom_o))
+      return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: parameter and code arrays must be 16-byte aligned");
     pa.grads[r] = peers->grads[r];
     pa.vis[r] = peers->vis[r];
     pa.t[r] = peers->transforms[r];

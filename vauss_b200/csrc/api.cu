@@ -274,6 +274,21 @@ VS_API vs_status vs_render_forward(vs_ctx* ctx, vs_frame* f, const vs_camera* ca
   return vs_render_rasterize(ctx, f, out_img, visible);
 }
 
+VS_API vs_status vs_render_image(vs_ctx* ctx, vs_frame* f, const vs_camera* cam, const vs_render_cfg* cfg,
+                                 uint32_t num_splats, const float* transforms, const void* sh_coeffs,
+                                 const float* raw_opacities, const float* min_scale, uint32_t* out_rgba8,
+                                 vs_render_counts* counts_out) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!out_rgba8) return vs_fail(ctx, VS_ERR_INVALID, "render_image: null output");
+  VS_TRY(vs_render_project(ctx, f, cam, cfg, num_splats, transforms, sh_coeffs, raw_opacities, min_scale,
+                           counts_out));
+  VS_TRY(vs_render_bin(ctx, f));
+  VS_TRY(set_device(ctx));
+  VS_TRY(launch_raster_packed(ctx, f, out_rgba8));
+  f->rendered = false;  // no backward information was recorded
+  return VS_OK;
+}
+
 VS_API vs_status vs_loss(vs_ctx* ctx, uint32_t h, uint32_t w, const float* pred, const uint32_t* gt_packed,
                          float l1_w, float ssim_w, float* partials, float* loss_dev, float* dl_dpred) {
   if (!ctx) return VS_ERR_INVALID;

@@ -34,11 +34,14 @@ __device__ __forceinline__ uint32_t compact_bits(uint32_t v) {
   return x;
 }
 
+// kPacked: the inference pass (the reference's bwd_info = false) -- packed
+// RGBA8 output, no visible marks, no used range ends.
+template <bool kPacked>
 __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
     uint32_t w, uint32_t h, uint32_t tbw, float bg_r, float bg_g, float bg_b,
     const uint2* __restrict__ ranges, const uint32_t* __restrict__ isect_compact,
     const float4* __restrict__ projected, float4* __restrict__ out_img, float* __restrict__ visible,
-    uint32_t* __restrict__ used_end) {
+    uint32_t* __restrict__ used_end, uint32_t* __restrict__ out_packed) {
   __shared__ float4 s_a[RF_THREADS];  // x, y, 0.5 c00, c01
   __shared__ float4 s_b[RF_THREADS];  // 0.5 c11, opac, max(r, 0), max(g, 0)
   __shared__ float2 s_c[RF_THREADS];  // max(b, 0), sigma cut
@@ -118,7 +121,7 @@ __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
           if (next_t <= 1.0e-4f) {
             done = true;
           } else {
-            s_hit[j] = 1u;
+            if (!kPacked) s_hit[j] = 1u;
             const float vis = alpha * t_acc;
             r = fmaf(sb.z, vis, r);
             g = fmaf(sb.w, vis, g);
@@ -131,12 +134,19 @@ __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
     }
     if (!was_done && done) atomicAdd(&s_done, 1u);
     __syncthreads();
-    if (tid < cnt && s_hit[tid]) visible[s_gid[tid]] = 1.0f;
+    if (!kPacked && tid < cnt && s_hit[tid]) visible[s_gid[tid]] = 1.0f;
   }
-  if (inside) {
-    out_img[(size_t)py * w + px] = make_float4(fmaf(t_acc, bg_r, r), fmaf(t_acc, bg_g, g), fmaf(t_acc, bg_b, b),
-                                               1.0f - t_acc);
+  const float fr = fmaf(t_acc, bg_r, r), fg = fmaf(t_acc, bg_g, g), fb = fmaf(t_acc, bg_b, b), fa = 1.0f - t_acc;
+  if (kPacked) {
+    // rasterize.rs:401-409: clamp(255 c, 0, 255) converted toward zero, r in the low byte
+    if (inside) {
+      const uint32_t cr = (uint32_t)clampf(fr * 255.0f, 0.0f, 255.0f), cg = (uint32_t)clampf(fg * 255.0f, 0.0f, 255.0f);
+      const uint32_t cb = (uint32_t)clampf(fb * 255.0f, 0.0f, 255.0f), ca = (uint32_t)clampf(fa * 255.0f, 0.0f, 255.0f);
+      out_packed[(size_t)py * w + px] = cr | (cg << 8) | (cb << 16) | (ca << 24);
+    }
+    return;
   }
+  if (inside) out_img[(size_t)py * w + px] = make_float4(fr, fg, fb, fa);
   atomicMax(&s_max_used, last);
   __syncthreads();
   if (tid == 0) used_end[tile] = s_max_used;
@@ -147,9 +157,18 @@ __global__ void __launch_bounds__(RF_THREADS) raster_fwd_kernel(
 vs_status launch_raster_fwd(vs_ctx* ctx, vs_frame* f, float* out_img, float* visible) {
   if (f->n > 0) VS_CUDA(ctx, cudaMemsetAsync(visible, 0, (size_t)f->n * 4, ctx->stream));
   if (f->T == 0) return VS_OK;
-  raster_fwd_kernel<<<f->T, RF_THREADS, 0, ctx->stream>>>(
+  raster_fwd_kernel<false><<<f->T, RF_THREADS, 0, ctx->stream>>>(
       f->u.w, f->u.h, f->u.tbw, f->u.bg[0], f->u.bg[1], f->u.bg[2], (const uint2*)f->tile_ranges.ptr,
       (const uint32_t*)f->isect_compact.ptr, (const float4*)f->projected.ptr, (float4*)out_img, visible,
-      (uint32_t*)f->tile_used_end.ptr); ++ctx->launches;
+      (uint32_t*)f->tile_used_end.ptr, nullptr); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "raster_fwd launch");
+}
+
+vs_status launch_raster_packed(vs_ctx* ctx, vs_frame* f, uint32_t* out_rgba8) {
+  if (f->T == 0) return VS_OK;
+  raster_fwd_kernel<true><<<f->T, RF_THREADS, 0, ctx->stream>>>(
+      f->u.w, f->u.h, f->u.tbw, f->u.bg[0], f->u.bg[1], f->u.bg[2], (const uint2*)f->tile_ranges.ptr,
+      (const uint32_t*)f->isect_compact.ptr, (const float4*)f->projected.ptr, nullptr, nullptr, nullptr, out_rgba8);
+  ++ctx->launches;
+  return vs_cuda(ctx, cudaGetLastError(), "raster_packed launch");
 }

@@ -66,6 +66,7 @@ vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t
 vs_status scan_inclusive_u32(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev);
 vs_status launch_bin(vs_ctx* ctx, vs_frame* f);
 vs_status launch_raster_fwd(vs_ctx* ctx, vs_frame* f, float* out_img, float* visible);
+vs_status launch_raster_packed(vs_ctx* ctx, vs_frame* f, uint32_t* out_rgba8);
 vs_status launch_raster_bwd(vs_ctx* ctx, vs_frame* f, const float* out_img, const float* v_out, float* v_combined);
 vs_status launch_loss(vs_ctx* ctx, uint32_t h, uint32_t w, const float* pred, const uint32_t* gt, float l1_w,
                       float ssim_w, float* partials, float* loss_dev, float* dl_dpred);

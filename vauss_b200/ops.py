@@ -159,6 +159,27 @@ def render(camera: Camera, cfg: N.RenderCfg, transforms: torch.Tensor, sh_coeffs
     return RenderOutput(out_img, visible, frame)
 
 
+def render_image(camera: Camera, cfg: N.RenderCfg, transforms: torch.Tensor, sh_coeffs: torch.Tensor,
+                 raw_opacities: torch.Tensor, min_scale: torch.Tensor | None = None, frame: Frame | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Inference render (render_splats with RasterPass::Forward,
+    crates/splat-train-render/src/gaussian_splats.rs:511-527): packed RGBA8
+    [H, W] (int32 storage of the u32 words, r in the low byte)."""
+    ctx = context(transforms.device)
+    n = transforms.shape[0]
+    assert transforms.shape == (n, 10) and raw_opacities.shape == (n,)
+    assert sh_coeffs.shape[0] == n and sh_coeffs.shape[2] == 3 and sh_coeffs.shape[1] == (cfg.sh_degree + 1) ** 2
+    assert (sh_coeffs.dtype == torch.float16) == bool(cfg.sh_half)
+    frame = frame or Frame(ctx)
+    if out is None:
+        out = torch.empty(camera.height, camera.width, dtype=torch.int32, device=transforms.device)
+    cam = camera.to_c()
+    ctx.check(ctx.lib.vs_render_image(ctx.h, frame.h, ctypes.byref(cam), ctypes.byref(cfg), n, _ptr(transforms),
+                                      _ptr(sh_coeffs), _ptr(raw_opacities), _ptr(min_scale), _ptr(out),
+                                      ctypes.byref(frame.counts)))
+    return out
+
+
 def render_stages(camera: Camera, cfg: N.RenderCfg, transforms, sh_coeffs, raw_opacities, frame: Frame, out_img,
                   visible, min_scale=None, hook=None) -> RenderOutput:
     """``render`` as its three stages (project, bin, rasterize); ``hook(name)``
