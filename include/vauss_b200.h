@@ -282,6 +282,43 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
                                  uint32_t splat_end, const vs_peer_set* peers, vs_q8_tensor mom_t,
                                  vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8);
 
+/* ---- refinement: densify and prune -----------------------------------------
+ * The GPU side of SplatTrainer::refine (crates/splat-train/src/train.rs:
+ * 1779-2104, refine_splats :2110-2300); the sampling of parents and the
+ * budgets are host decisions made from one readback of the table. */
+typedef struct vs_refine_cfg {
+  float min_opacity;          /* prune below this opacity (1/255) */
+  float max_bound;            /* prune scales or |mean - center| beyond this (100 x scene extent) */
+  float center[3];            /* scene bounds centre */
+  float split_at_screen_size; /* oversized flag threshold (fraction of the image); 0 disables */
+} vs_refine_cfg;
+/* table [N,8] f32 per splat: prune, non-finite, opacity*visible, oversized,
+ * refine_weight*visible, mean xyz (train.rs:1822-1883); visible = vis_weight > 0.
+ * sh_width = values per SH row (3 (d+1)^2), sh_half = SH stored as binary16. */
+VS_API vs_status vs_refine_table(vs_ctx* ctx, uint32_t num_splats, const float* transforms, const void* sh_coeffs,
+                                 uint32_t sh_width, int32_t sh_half, const float* raw_opacities,
+                                 const float* refine_weight, const float* vis_weight, const float* max_screen,
+                                 const vs_refine_cfg* cfg, float* table);
+/* Splits parents[i] into itself and children[i] (device i32 arrays of
+ * `count` distinct rows; a child row is a pruned slot or a row appended after
+ * the old count, all < num_splats): covariance-aware shrink with split_at_
+ * screen_size capping (screen_sizes = per-splat max screen extent, may be NULL
+ * when the cap is 0), +- rotated offset, opacity 1 - (1 - o)^(1/sqrt 2) on
+ * both, SH row copied to the child (train.rs:2142-2252).  empty_rows get
+ * finite invisible filler rows (:2259-2283). */
+VS_API vs_status vs_refine_split(vs_ctx* ctx, uint32_t num_splats, float* transforms, void* sh_coeffs,
+                                 uint32_t sh_width, int32_t sh_half, float* raw_opacities, uint32_t count,
+                                 const int32_t* parents, const int32_t* children, const float* screen_sizes,
+                                 float split_at_screen_size, float min_opacity, uint32_t empty_count,
+                                 const int32_t* empty_rows);
+/* Zeroes both moments of `count` rows (row width `row_width` values) in place
+ * (optim.rs:188-215 for the 8-bit moments: zero codes under the unchanged
+ * block scales).  Rows appended to a tensor are zero codes too. */
+VS_API vs_status vs_q8_reset_rows(vs_ctx* ctx, vs_q8_tensor mom, uint32_t row_width, uint32_t count,
+                                  const int32_t* rows);
+/* raw = logit(clamp(sigmoid(raw) - amount, 1e-12, 1 - 1e-12)) (train.rs:2285-2296). */
+VS_API vs_status vs_opacity_decay(vs_ctx* ctx, uint32_t num_splats, float* raw_opacities, float amount);
+
 /* ---- housekeeping (crates/splat-train/src/housekeep.rs:15-39) ------------- */
 VS_API vs_status vs_gather_stats(vs_ctx* ctx, uint32_t n, float* refine_norm, float* vis_count, float* max_screen,
                                  const float* refine_weight, const float* visible, const float* radius);

@@ -292,6 +292,51 @@ def noise_means(transforms, opacities, visible, scale, limit, seed):
     return t
 
 
+def refine_table(transforms, sh, raw_opac, refine_weight, vis_weight, max_screen, min_opacity, max_bound, center,
+                 split_at_screen_size):
+    """Per-splat refine decision table [N, 8] (train.rs:1822-1883)."""
+    L = lib()
+    t, o = _f32(transforms), _f32(raw_opac)
+    n = t.shape[0]
+    shf = _f32(np.asarray(sh, np.float32).reshape(n, -1))
+    table = np.zeros((max(n, 1), 8), np.float32)
+    c = np.asarray(center, np.float32)
+    rc = L.or_refine_table(ctypes.c_uint32(n), _p(t, F32P), _p(shf, F32P), ctypes.c_uint32(shf.shape[1]),
+                           _p(o, F32P), _p(_f32(refine_weight), F32P), _p(_f32(vis_weight), F32P),
+                           _p(_f32(max_screen), F32P), ctypes.c_float(min_opacity), ctypes.c_float(max_bound),
+                           _p(c, F32P), ctypes.c_float(split_at_screen_size), _p(table, F32P))
+    assert rc == 0
+    return table[:n]
+
+
+def refine_split(transforms, sh, raw_opac, parents, children, screen, split_at_screen_size, min_opacity,
+                 empty_rows=()):
+    """Split of every parent into itself and its child row, plus filler rows
+    (train.rs:2142-2283); returns updated copies."""
+    L = lib()
+    t, o = _f32(transforms).copy(), _f32(raw_opac).copy()
+    n = t.shape[0]
+    shf = _f32(np.asarray(sh, np.float32).reshape(n, -1)).copy()
+    par = np.ascontiguousarray(parents, np.int32)
+    ch = np.ascontiguousarray(children, np.int32)
+    emp = np.ascontiguousarray(empty_rows, np.int32)
+    scr = _f32(screen) if screen is not None else np.zeros(1, np.float32)
+    I32P = ctypes.POINTER(ctypes.c_int32)
+    rc = L.or_refine_split(_p(t, F32P), _p(shf, F32P), ctypes.c_uint32(shf.shape[1]), _p(o, F32P),
+                           ctypes.c_uint32(len(par)), _p(par if len(par) else np.zeros(1, np.int32), I32P),
+                           _p(ch if len(ch) else np.zeros(1, np.int32), I32P), _p(scr, F32P),
+                           ctypes.c_float(split_at_screen_size), ctypes.c_float(min_opacity),
+                           ctypes.c_uint32(len(emp)), _p(emp if len(emp) else np.zeros(1, np.int32), I32P))
+    assert rc == 0
+    return t, shf.reshape(np.asarray(sh).shape), o
+
+
+def opacity_decay(raw_opac, amount):
+    o = _f32(raw_opac).copy()
+    lib().or_opacity_decay(ctypes.c_uint32(o.shape[0]), _p(o, F32P), ctypes.c_float(amount))
+    return o
+
+
 def splitmix_shuffle(n: int, seed: int) -> np.ndarray:
     keys = np.empty(n, np.uint32)
     lib().or_splitmix_shuffle(_p(keys, U32P), ctypes.c_uint64(n), ctypes.c_uint64(seed))

@@ -1426,3 +1426,105 @@ OR_API void or_f16_batch(const float* x, uint16_t* h, float* back, size_t n) {
     back[i] = vs_f16_to_f32(h[i]);
   }
 }
+
+// ===========================================================================
+// Refinement.  Reference: crates/splat-train/src/train.rs:1822-1883 (the
+// per-splat decision table), :2142-2252 (refine_splats: the split of each
+// parent into itself and a child), :2259-2283 (filler rows), :2285-2296
+// (opacity decay), crates/splat-train/src/quat_vec.rs (rotating the offset).
+// ===========================================================================
+OR_API int or_refine_table(uint32_t n, const float* transforms, const float* sh, uint32_t sh_width,
+                           const float* raw_opac, const float* refine_weight, const float* vis_weight,
+                           const float* max_screen, float min_opacity, float max_bound, const float* center,
+                           float split_at_screen_size, float* table) {
+  for (uint32_t g = 0; g < n; ++g) {
+    const float* t = transforms + (size_t)g * 10;
+    bool finite = vs_is_finite(raw_opac[g]);
+    for (int k = 0; k < 10; ++k) finite = finite && vs_is_finite(t[k]);
+    for (uint32_t k = 0; k < sh_width; ++k) finite = finite && vs_is_finite(sh[(size_t)g * sh_width + k]);
+    const float opac = vs_sigmoid(raw_opac[g]);
+    bool big = false, far = false;
+    for (int k = 0; k < 3; ++k) {
+      if (vs_expf(t[7 + k]) > max_bound) big = true;
+      if (fabsf(t[k] - center[k]) > max_bound) far = true;
+    }
+    const float vis = vis_weight[g] > 0.0f ? 1.0f : 0.0f;
+    float* row = table + (size_t)g * 8;
+    row[0] = (opac < min_opacity || big || far || !finite) ? 1.0f : 0.0f;
+    row[1] = finite ? 0.0f : 1.0f;
+    row[2] = opac * vis;
+    row[3] = (split_at_screen_size > 0.0f && max_screen[g] > split_at_screen_size && vis > 0.0f) ? 1.0f : 0.0f;
+    row[4] = refine_weight[g] * vis;
+    row[5] = t[0];
+    row[6] = t[1];
+    row[7] = t[2];
+  }
+  return 0;
+}
+
+OR_API int or_refine_split(float* transforms, float* sh, uint32_t sh_width, float* raw_opac, uint32_t count,
+                           const int32_t* parents, const int32_t* children, const float* screen,
+                           float split_at_screen_size, float min_opacity, uint32_t empty_count,
+                           const int32_t* empty_rows) {
+  const float r2 = 0.70710678118654752440f;  // 1/sqrt(2)
+  for (uint32_t i = 0; i < count; ++i) {
+    const size_t p = (size_t)parents[i], c = (size_t)children[i];
+    float t[10];
+    memcpy(t, transforms + p * 10, sizeof(t));
+    // cur_rots = raw / max(|raw|, 1e-32)
+    const float norm = sqrtf(((t[3] * t[3] + t[4] * t[4]) + t[5] * t[5]) + t[6] * t[6]);
+    const float mag = fmaxf(norm, 1.0e-32f);
+    const float q[4] = {t[3] / mag, t[4] / mag, t[5] / mag, t[6] / mag};
+    // k per axis = 1 - (s_k^2 / max s^2) (1 - k_max)
+    float scale[3], sq[3];
+    for (int k = 0; k < 3; ++k) {
+      scale[k] = vs_expf(t[7 + k]);
+      sq[k] = scale[k] * scale[k];
+    }
+    const float mx = fmaxf(fmaxf(fmaxf(sq[0], sq[1]), sq[2]), 1.0e-30f);
+    const float k_max = split_at_screen_size > 0.0f
+        ? fminf(split_at_screen_size * (1.0f / fmaxf(screen[p], 1.0e-6f)), r2) : r2;
+    float v[3], logs[3];
+    for (int k = 0; k < 3; ++k) {
+      const float kk = -((sq[k] / mx) * (-k_max + 1.0f)) + 1.0f;
+      v[k] = sqrtf(fmaxf(-(kk * kk) + 1.0f, 0.0f)) * scale[k];
+      logs[k] = t[7 + k] + vs_logf(kk);
+    }
+    // offset rotated by q (quat_vec.rs)
+    const float w2 = q[0] * q[0], x2 = q[1] * q[1], y2 = q[2] * q[2], z2 = q[3] * q[3];
+    const float xy = q[1] * q[2], xz = q[1] * q[3], yz = q[2] * q[3];
+    const float wx = q[0] * q[1], wy = q[0] * q[2], wz = q[0] * q[3];
+    const float ox = (((w2 + x2) - y2) - z2) * v[0] + ((((xy * v[1] + xz * v[2]) + wy * v[2]) - wz * v[1]) * 2.0f);
+    const float oy = (((w2 - x2) + y2) - z2) * v[1] + ((((xy * v[0] + yz * v[2]) + wz * v[0]) - wx * v[2]) * 2.0f);
+    const float oz = (((w2 - x2) - y2) + z2) * v[2] + ((((xz * v[0] + yz * v[1]) + wx * v[1]) - wy * v[0]) * 2.0f);
+    // both halves: opacity 1 - (1 - o)^(1/sqrt 2), logit of its clamp
+    const float o = vs_sigmoid(raw_opac[p]);
+    const float po = 1.0f - vs_expf(vs_logf(1.0f - o) * r2);
+    const float cl = fminf(fmaxf(po, min_opacity), 1.0f - min_opacity);
+    const float raw = vs_logf(cl / (1.0f - cl));
+    float* tc = transforms + c * 10;
+    float* tp = transforms + p * 10;
+    const float child[10] = {t[0] + ox, t[1] + oy, t[2] + oz, q[0], q[1], q[2], q[3], logs[0], logs[1], logs[2]};
+    const float parent[10] = {t[0] - ox, t[1] - oy, t[2] - oz, t[3], t[4], t[5], t[6], logs[0], logs[1], logs[2]};
+    memcpy(tc, child, sizeof(child));
+    memcpy(tp, parent, sizeof(parent));
+    raw_opac[p] = raw;
+    raw_opac[c] = raw;
+    memcpy(sh + c * sh_width, sh + p * sh_width, sh_width * sizeof(float));
+  }
+  for (uint32_t i = 0; i < empty_count; ++i) {
+    const size_t r = (size_t)empty_rows[i];
+    const float row[10] = {0.0f, 0.0f, 0.0f, 1.0f, 0.0f, 0.0f, 0.0f, -10.0f, -10.0f, -10.0f};
+    memcpy(transforms + r * 10, row, sizeof(row));
+    raw_opac[r] = -20.0f;
+    for (uint32_t k = 0; k < sh_width; ++k) sh[r * sh_width + k] = 0.0f;
+  }
+  return 0;
+}
+
+OR_API void or_opacity_decay(uint32_t n, float* raw_opac, float amount) {
+  for (uint32_t g = 0; g < n; ++g) {
+    const float o = fminf(fmaxf(vs_sigmoid(raw_opac[g]) - amount, 1.0e-12f), 1.0f - 1.0e-12f);
+    raw_opac[g] = vs_logf(o / (1.0f - o));
+  }
+}

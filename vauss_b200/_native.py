@@ -65,6 +65,11 @@ class PeerSet(ctypes.Structure):
                 ("raw_opacities", c_vp * PEER_MAX)]
 
 
+class RefineCfg(ctypes.Structure):
+    _fields_ = [("min_opacity", ctypes.c_float), ("max_bound", ctypes.c_float), ("center", ctypes.c_float * 3),
+                ("split_at_screen_size", ctypes.c_float)]
+
+
 class Q8Cfg(ctypes.Structure):
     _fields_ = [("beta1", ctypes.c_float), ("beta2", ctypes.c_float), ("inv1", ctypes.c_float),
                 ("inv2", ctypes.c_float), ("epsilon", ctypes.c_float), ("lr_transforms", ctypes.c_float * 10),
@@ -118,6 +123,12 @@ _SIGS = {
     "vs_ctx_check": ([c_vp], ctypes.c_int),
     "vs_adam_q8_peer": ([c_vp, ctypes.c_uint32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint32,
                          ctypes.POINTER(PeerSet), Q8Tensor, Q8Tensor, Q8Tensor, ctypes.POINTER(Q8Cfg)], ctypes.c_int),
+    "vs_refine_table": ([c_vp, ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint32, ctypes.c_int32, c_vp, c_vp, c_vp, c_vp,
+                         ctypes.POINTER(RefineCfg), c_vp], ctypes.c_int),
+    "vs_refine_split": ([c_vp, ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint32, ctypes.c_int32, c_vp, ctypes.c_uint32,
+                         c_vp, c_vp, c_vp, ctypes.c_float, ctypes.c_float, ctypes.c_uint32, c_vp], ctypes.c_int),
+    "vs_q8_reset_rows": ([c_vp, Q8Tensor, ctypes.c_uint32, ctypes.c_uint32, c_vp], ctypes.c_int),
+    "vs_opacity_decay": ([c_vp, ctypes.c_uint32, c_vp, ctypes.c_float], ctypes.c_int),
     "vs_gather_stats": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_noise_means": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, ctypes.c_float, ctypes.c_float, ctypes.c_uint32],
                        ctypes.c_int),

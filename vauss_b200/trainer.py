@@ -52,6 +52,14 @@ class TrainConfig:
     render_mode_mip: bool = True
     optimizer: str = "q8"  # "q8" | "reference"
     adam_epsilon: float = 1e-15
+    # refinement (config.rs:238-290)
+    refine_every: int = 200
+    growth_start_iter: int = 500
+    growth_stop_iter: int = 15_000
+    max_splats: int = 0
+    max_budget: bool = False
+    split_at_screen_size: float = 0.5
+    opac_decay: float = 0.004
 
     @property
     def l1_weight(self) -> float:
@@ -133,6 +141,33 @@ class SplatTrainer:
         self.record: RefineRecord | None = None
         self._buffers = {}
         self._copy_stream = None
+        self.refiner = None
+        self.train_pixels = 0  # pixels of one training image (the refine budget limit); 0 = unlimited
+        self.view_centers = None  # [V, 3] camera centres (far-share of the refine budget)
+
+    # ---- refinement (train.rs:1779-2300; vauss_b200/refine.py) ----
+    def should_refine(self, step: int) -> bool:
+        """The training loop's refine schedule (crates/splat-brush/src/train.rs:1136)."""
+        c = self.config
+        return step > 0 and step % c.refine_every == 0 and step / max(c.total_train_iters, 1) <= 0.95
+
+    def refine(self, it: int, splats: Splats):
+        """Prune, replace and grow the splats; returns (splats, RefineStats).
+        The optimizer moments follow the rows; the refine statistics restart."""
+        from .refine import Bounds, Refiner
+        if self.config.optimizer != "q8":
+            raise NotImplementedError("refinement is implemented for the 8-bit-moment optimizer")
+        if self.optim is None or self.record is None:
+            raise RuntimeError("refine needs at least one training step first")
+        if self.refiner is None:
+            means = splats.transforms[:, :3].detach().cpu().numpy()
+            self.refiner = Refiner(self.config, Bounds.from_means(means), self.rng, self.train_pixels,
+                                   self.view_centers)
+        splats, stats = self.refiner.refine(it, splats, self.record, self.optim, self.device)
+        n = splats.num_splats
+        dev = self.device
+        self.record = RefineRecord(torch.zeros(n, device=dev), torch.zeros(n, device=dev), torch.zeros(n, device=dev))
+        return splats, stats
 
     # ---- learning rates (train.rs:859-904) ----
     def lr_unit(self) -> float:
