@@ -319,6 +319,56 @@ VS_API vs_status vs_q8_reset_rows(vs_ctx* ctx, vs_q8_tensor mom, uint32_t row_wi
 /* raw = logit(clamp(sigmoid(raw) - amount, 1e-12, 1 - 1e-12)) (train.rs:2285-2296). */
 VS_API vs_status vs_opacity_decay(vs_ctx* ctx, uint32_t num_splats, float* raw_opacities, float amount);
 
+/* ---- dataset feed: packed RGBA8 ground truth -------------------------------
+ * Replaces SceneLoader (crates/splat-train-dataset/src/scene_loader.rs:59-184)
+ * and view_to_packed_data (scene.rs:113-161) for decoded 8-bit images.
+ * Packing: one u32 per pixel, r in the low byte, a in the high byte; 1, 2, 3
+ * or 4 source channels (L, LA, RGB, RGBA); a missing alpha is 255;
+ * with alpha and VS_ALPHA_TRANSPARENT the colours are premultiplied in byte
+ * space, (c * a + 127) / 255. */
+#define VS_ALPHA_MASKED 0
+#define VS_ALPHA_TRANSPARENT 1
+/* Packs device pixels [height*width*channels] u8 into out [height*width] u32
+ * on the ctx stream.  Returns whether the source has alpha in *has_alpha. */
+VS_API vs_status vs_pack_view(vs_ctx* ctx, const uint8_t* pixels, uint32_t width, uint32_t height,
+                              uint32_t channels, int32_t alpha_mode, uint32_t* out, int32_t* has_alpha);
+
+typedef struct vs_feed vs_feed;
+typedef struct vs_feed_cfg {
+  uint32_t num_views;
+  uint32_t ring_slots;   /* batches staged ahead of the consumer (>= 2; 4 like the reference's channel) */
+  uint32_t workers;      /* host threads that copy pixels into pinned memory (0: one per slot) */
+  uint32_t hold;         /* batches the consumer uses at once (>= 1) */
+  uint64_t cache_bytes;  /* HBM budget for packed views kept resident (max_scene_batch_cache_size) */
+  uint64_t seed;
+} vs_feed_cfg;
+typedef struct vs_scene_batch {
+  const uint32_t* img_packed; /* device [height, width]; ready on the ctx stream */
+  uint32_t width, height;
+  uint32_t view_index;
+  int32_t has_alpha;
+  int32_t alpha_mode;
+  int32_t cached;             /* 1: a resident copy that stays valid until vs_feed_destroy */
+  uint64_t h2d_bytes;         /* host-to-device bytes copied for this batch */
+} vs_scene_batch;
+/* The feed stages views on its own copy stream and worker threads: pinned
+ * host slots, device staging slots and the packing kernel, ring_slots batches
+ * ahead of the consumer.  Views are visited in epochs, each a fresh seeded
+ * shuffle of all views.  A packed view that fits the cache budget (and whose
+ * slot is empty) stays resident in HBM, so later visits copy nothing. */
+VS_API vs_status vs_feed_create(vs_ctx* ctx, const vs_feed_cfg* cfg, vs_feed** out);
+/* Registers view `index` (host pixels, read until vs_feed_destroy: keep them
+ * alive and unchanged).  All views are set before the first vs_feed_next. */
+VS_API vs_status vs_feed_set_view(vs_feed* feed, uint32_t index, const uint8_t* pixels, uint32_t width,
+                                  uint32_t height, uint32_t channels, int32_t alpha_mode);
+/* The next batch.  A batch k that is not `cached` stays valid (in stream
+ * order on the ctx stream) until the call that hands out batch k + hold. */
+VS_API vs_status vs_feed_next(vs_feed* feed, vs_scene_batch* out);
+VS_API void vs_feed_destroy(vs_feed* feed);
+/* The visiting order (host only, no GPU): `count` view indices from the start
+ * of the sequence a feed with this seed and view count follows. */
+VS_API vs_status vs_feed_order(uint64_t seed, uint32_t num_views, uint32_t count, uint32_t* out);
+
 /* ---- housekeeping (crates/splat-train/src/housekeep.rs:15-39) ------------- */
 VS_API vs_status vs_gather_stats(vs_ctx* ctx, uint32_t n, float* refine_norm, float* vis_count, float* max_screen,
                                  const float* refine_weight, const float* visible, const float* radius);

@@ -374,3 +374,17 @@ def render_forward(cam, cfg, splats, bg=(0.0, 0.0, 0.0)):
     after = dict(binning)
     after["tile_offsets"] = fwd["tile_offsets"]
     return dict(proj=proj, binning=binning, binning_after=after, tile_offsets_pre=pre_offsets, **fwd)
+
+
+def pack_view(pixels, alpha_mode: int = 0):
+    """view_to_packed_data (scene.rs:113-161): u8 [H, W] or [H, W, C] with
+    C in 1..4 -> (u32 [H, W], has_alpha).  alpha_mode 1 = transparent."""
+    px = np.ascontiguousarray(pixels, dtype=np.uint8)
+    if px.ndim == 2:
+        px = px[..., None]
+    h, w, c = px.shape
+    out = np.zeros((h, w), np.uint32)
+    rc = lib().or_pack_view(_p(px, U8P), ctypes.c_uint32(w), ctypes.c_uint32(h), ctypes.c_uint32(c),
+                            ctypes.c_int32(alpha_mode), _p(out, U32P))
+    assert rc == 0
+    return out, c in (2, 4)

@@ -1528,3 +1528,33 @@ OR_API void or_opacity_decay(uint32_t n, float* raw_opac, float amount) {
     raw_opac[g] = vs_logf(o / (1.0f - o));
   }
 }
+
+// ---- dataset feed: view_to_packed_data (crates/splat-train-dataset/src/
+// scene.rs:113-161) for 8-bit sources.  L / LA widen to RGBA the way
+// DynamicImage::into_rgba8 does (l, l, l[, a]); a missing alpha is 255; with
+// alpha and the transparent mode each colour byte becomes (c * a + 127) / 255.
+OR_API int or_pack_view(const uint8_t* px, uint32_t width, uint32_t height, uint32_t channels, int32_t alpha_mode,
+                        uint32_t* out) {
+  if (channels < 1 || channels > 4) return 1;
+  const bool has_alpha = channels == 2 || channels == 4;
+  const bool premultiply = has_alpha && alpha_mode == 1;
+  const size_t n = (size_t)width * height;
+  for (size_t i = 0; i < n; ++i) {
+    const uint8_t* p = px + i * channels;
+    uint32_t r, g, b, a = 255;
+    if (channels <= 2) {
+      r = g = b = p[0];
+      if (channels == 2) a = p[1];
+    } else {
+      r = p[0], g = p[1], b = p[2];
+      if (channels == 4) a = p[3];
+    }
+    if (premultiply) {
+      r = (r * a + 127) / 255;
+      g = (g * a + 127) / 255;
+      b = (b * a + 127) / 255;
+    }
+    out[i] = r | g << 8 | b << 16 | a << 24;
+  }
+  return 0;
+}

@@ -70,6 +70,17 @@ class RefineCfg(ctypes.Structure):
                 ("split_at_screen_size", ctypes.c_float)]
 
 
+class FeedCfg(ctypes.Structure):
+    _fields_ = [("num_views", ctypes.c_uint32), ("ring_slots", ctypes.c_uint32), ("workers", ctypes.c_uint32),
+                ("hold", ctypes.c_uint32), ("cache_bytes", ctypes.c_uint64), ("seed", ctypes.c_uint64)]
+
+
+class SceneBatchC(ctypes.Structure):
+    _fields_ = [("img_packed", c_vp), ("width", ctypes.c_uint32), ("height", ctypes.c_uint32),
+                ("view_index", ctypes.c_uint32), ("has_alpha", ctypes.c_int32), ("alpha_mode", ctypes.c_int32),
+                ("cached", ctypes.c_int32), ("h2d_bytes", ctypes.c_uint64)]
+
+
 class Q8Cfg(ctypes.Structure):
     _fields_ = [("beta1", ctypes.c_float), ("beta2", ctypes.c_float), ("inv1", ctypes.c_float),
                 ("inv2", ctypes.c_float), ("epsilon", ctypes.c_float), ("lr_transforms", ctypes.c_float * 10),
@@ -129,6 +140,14 @@ _SIGS = {
                          c_vp, c_vp, c_vp, ctypes.c_float, ctypes.c_float, ctypes.c_uint32, c_vp], ctypes.c_int),
     "vs_q8_reset_rows": ([c_vp, Q8Tensor, ctypes.c_uint32, ctypes.c_uint32, c_vp], ctypes.c_int),
     "vs_opacity_decay": ([c_vp, ctypes.c_uint32, c_vp, ctypes.c_float], ctypes.c_int),
+    "vs_pack_view": ([c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int32, c_vp,
+                      ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
+    "vs_feed_create": ([c_vp, ctypes.POINTER(FeedCfg), ctypes.POINTER(c_vp)], ctypes.c_int),
+    "vs_feed_set_view": ([c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                          ctypes.c_int32], ctypes.c_int),
+    "vs_feed_next": ([c_vp, ctypes.POINTER(SceneBatchC)], ctypes.c_int),
+    "vs_feed_destroy": ([c_vp], None),
+    "vs_feed_order": ([ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, c_vp], ctypes.c_int),
     "vs_gather_stats": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_noise_means": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, ctypes.c_float, ctypes.c_float, ctypes.c_uint32],
                        ctypes.c_int),

@@ -79,6 +79,8 @@ class SceneBatch:
     img_packed: torch.Tensor
     camera: Camera
     view_index: int = 0
+    has_alpha: bool = False
+    alpha_mode: int = 0
 
 
 @dataclass
