@@ -369,6 +369,27 @@ VS_API void vs_feed_destroy(vs_feed* feed);
  * of the sequence a feed with this seed and view count follows. */
 VS_API vs_status vs_feed_order(uint64_t seed, uint32_t num_views, uint32_t count, uint32_t* out);
 
+/* ---- checkpoint I/O: PLY vertex rows ---------------------------------------
+ * Bytes of one PLY vertex row at an SH degree (0 if the degree is not 0..3):
+ * 4 * (14 + 3 ((d+1)^2 - 1)). */
+VS_API uint64_t vs_ply_row_bytes(int32_t sh_degree);
+/* Replaces the row encoding of splat_to_ply (crates/splat-train-serde/src/
+ * export.rs:322-425): writes num_splats rows of little-endian f32 to HOST
+ * memory host_out (num_splats * vs_ply_row_bytes bytes, pinned or pageable):
+ * x y z scale_0..2 opacity rot_0..3 (divided by max(|q|, 1e-12)) f_dc_0..2
+ * f_rest_0.. (channel-major).  Blocks until the rows are on the host. */
+VS_API vs_status vs_ply_encode(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, const float* transforms,
+                               const void* sh_coeffs, int32_t sh_half, const float* raw_opacities, void* host_out);
+/* Replaces the row decoding of parse_ply (import.rs:386-510): reads
+ * num_splats HOST rows of row_bytes and writes transforms [N,10], sh_coeffs
+ * [N,C,3] f32 and raw_opacities [N].  offsets / defaults (host, 11 + 3 C
+ * entries) describe each output value in the order transforms 0..9,
+ * opacity, SH (coefficient-major, channel-minor): the byte offset of its f32
+ * in a row (a multiple of 4), or -1 to write the default.  Blocks until done. */
+VS_API vs_status vs_ply_decode(vs_ctx* ctx, uint32_t num_splats, const void* host_rows, uint32_t row_bytes,
+                               uint32_t sh_coeffs_per_channel, const int32_t* offsets, const float* defaults,
+                               float* transforms, float* sh_coeffs, float* raw_opacities);
+
 /* ---- housekeeping (crates/splat-train/src/housekeep.rs:15-39) ------------- */
 VS_API vs_status vs_gather_stats(vs_ctx* ctx, uint32_t n, float* refine_norm, float* vis_count, float* max_screen,
                                  const float* refine_weight, const float* visible, const float* radius);

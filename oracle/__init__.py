@@ -388,3 +388,16 @@ def pack_view(pixels, alpha_mode: int = 0):
                             ctypes.c_int32(alpha_mode), _p(out, U32P))
     assert rc == 0
     return out, c in (2, 4)
+
+
+def ply_encode(transforms, sh, raw_opac):
+    """PLY vertex rows [N, 14 + 3 rest] f32 (export.rs:393-417); sh [N, C, 3]."""
+    t, o = _f32(transforms), _f32(raw_opac)
+    s = _f32(np.asarray(sh, np.float32))
+    n, coeffs = t.shape[0], s.shape[1]
+    degree = int(round(coeffs ** 0.5)) - 1
+    out = np.zeros((max(n, 1), 14 + 3 * (coeffs - 1)), np.float32)
+    rc = lib().or_ply_encode(ctypes.c_uint32(n), ctypes.c_int32(degree), _p(t, F32P), _p(s, F32P), _p(o, F32P),
+                             _p(out, F32P))
+    assert rc == 0
+    return out[:n]

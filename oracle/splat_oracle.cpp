@@ -1558,3 +1558,26 @@ OR_API int or_pack_view(const uint8_t* px, uint32_t width, uint32_t height, uint
   }
   return 0;
 }
+
+// ---- checkpoint I/O: PLY vertex rows (crates/splat-train-serde/src/
+// export.rs:393-417, the encode closure of write_splat_ply).  sh is f32
+// [n, coeffs, 3]; each row is x y z scale_0..2 opacity rot_0..3 (divided by
+// max(sqrt(((r0 r0 + r1 r1) + r2 r2) + r3 r3), 1e-12)), f_dc_0..2, then the
+// rest coefficients channel-major.
+OR_API int or_ply_encode(uint32_t n, int32_t degree, const float* transforms, const float* sh, const float* raw_opac,
+                         float* out) {
+  if (degree < 0 || degree > 3) return 1;
+  const uint32_t coeffs = (uint32_t)((degree + 1) * (degree + 1)), rest = coeffs - 1, stride = 14 + 3 * rest;
+  for (uint32_t i = 0; i < n; ++i) {
+    const float* t = transforms + (size_t)i * 10;
+    float* w = out + (size_t)i * stride;
+    const float rn = fmaxf(sqrtf(((t[3] * t[3] + t[4] * t[4]) + t[5] * t[5]) + t[6] * t[6]), 1.0e-12f);
+    const float head[11] = {t[0], t[1], t[2], t[7], t[8], t[9], raw_opac[i], t[3] / rn, t[4] / rn, t[5] / rn, t[6] / rn};
+    for (int k = 0; k < 11; ++k) w[k] = head[k];
+    const float* s = sh + (size_t)i * coeffs * 3;
+    for (int ch = 0; ch < 3; ++ch) w[11 + ch] = s[ch];
+    for (uint32_t ch = 0; ch < 3; ++ch)
+      for (uint32_t k = 1; k <= rest; ++k) w[14 + ch * rest + (k - 1)] = s[k * 3 + ch];
+  }
+  return 0;
+}

@@ -148,6 +148,10 @@ _SIGS = {
     "vs_feed_next": ([c_vp, ctypes.POINTER(SceneBatchC)], ctypes.c_int),
     "vs_feed_destroy": ([c_vp], None),
     "vs_feed_order": ([ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, c_vp], ctypes.c_int),
+    "vs_ply_row_bytes": ([ctypes.c_int32], ctypes.c_uint64),
+    "vs_ply_encode": ([c_vp, ctypes.c_uint32, ctypes.c_int32, c_vp, c_vp, ctypes.c_int32, c_vp, c_vp], ctypes.c_int),
+    "vs_ply_decode": ([c_vp, ctypes.c_uint32, c_vp, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp],
+                      ctypes.c_int),
     "vs_gather_stats": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_noise_means": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp, ctypes.c_float, ctypes.c_float, ctypes.c_uint32],
                        ctypes.c_int),

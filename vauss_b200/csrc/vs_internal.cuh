@@ -25,6 +25,7 @@ struct vs_ctx {
   bool taps_ready = false;         // SSIM window uploaded to this device's constant memory
   // scratch shared by calls on this ctx (stream-ordered reuse)
   DevBuf sort_keys, sort_vals, sort_hist, scan_sums, misc;
+  DevBuf io_stage;  // checkpoint I/O chunks (two halves)
 };
 
 struct vs_frame {
