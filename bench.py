@@ -144,6 +144,13 @@ def make_workload(n_splats: int, config: int = 2):
     return sp, tgt, cams
 
 
+# DRAM bytes (read + write) per launch of each stage's kernel, from one ncu
+# capture of this workload (config 2 at 3M splats; profiles/<kernel>_config2_3M.md
+# give the command).  Below the algorithmic bytes for the raster kernels:
+# L2 (126 MB) serves a projected row to the neighbouring tiles that gather it.
+MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 235.05e6, "raster_fwd": 142.5e6, "project": 641.9e6, "loss": 60.8e6}
+
+
 def stage_bytes(name: str, n: int, v: int, i: int, p: int, t: int) -> float:
     """Algorithmic (compulsory) DRAM bytes of one launch of each stage:
     each logically required byte counted once, no cross-CTA reuse."""
@@ -312,7 +319,8 @@ def run_ours(args):
         dom = max(stages, key=lambda k: stages[k]["ms"])
         ach = stages[dom]["gbs"]
         roofline = {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                    "frac": round(ach / peak, 4), "traffic": None, "peak_source": which,
+                    "frac": round(ach / peak, 4),
+                    "traffic": (MEASURED_TRAFFIC_CONFIG2.get(dom) if n == N_SPLATS else None), "peak_source": which,
                     "note": "raster stages are FP32-issue bound; see profiles/ for issue utilisation"}
 
     cpu = None
