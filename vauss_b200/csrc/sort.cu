@@ -9,7 +9,8 @@
 // Per 8-bit pass: (1) each block histograms its 2048-key tile into a
 // digit-major table hist[digit][tile]; (2) an exclusive scan of that table
 // gives every (digit, tile) its global output offset; (3) each block ranks its
-// keys stably (every warp ranks a contiguous 256-key slice with match_any,
+// keys stably (every warp ranks a contiguous 256-key slice, equal digits found
+// by one ballot per digit bit,
 // warps are combined through per-digit counts), scatters them into shared
 // memory in digit order and writes contiguous per-digit runs to global memory.
 #include <mutex>
@@ -34,14 +35,13 @@ __global__ void __launch_bounds__(SORT_THREADS) hist_kernel(const uint32_t* __re
   s_hist[tid] = 0;
   __syncthreads();
   const uint32_t base = blockIdx.x * SORT_TILE;
-  const uint32_t lane = tid & 31u;
 #pragma unroll
   for (uint32_t r = 0; r < ITEMS; ++r) {
     const uint32_t i = base + r * SORT_THREADS + tid;
     const bool valid = i < count;
-    const uint32_t d = valid ? ((keys[i] >> shift) & mask) : RADIX;
-    const uint32_t peers = __match_any_sync(0xffffffffu, d);
-    if (valid && (uint32_t)(__ffs(peers) - 1) == lane) atomicAdd(&s_hist[d], (uint32_t)__popc(peers));
+    // plain shared-memory atomics: cheaper on sm_100 than grouping equal
+    // digits with match_any first
+    if (valid) atomicAdd(&s_hist[(keys[i] >> shift) & mask], 1u);
   }
   __syncthreads();
   hist[tid * tiles + blockIdx.x] = s_hist[tid];
@@ -75,7 +75,15 @@ __global__ void __launch_bounds__(SORT_THREADS) scatter_kernel(
   }
 #pragma unroll
   for (uint32_t r = 0; r < ITEMS; ++r) {
-    const uint32_t peers = __match_any_sync(0xffffffffu, d[r]);
+    // lanes holding the same digit (9 bits: an invalid lane holds 256), by
+    // one ballot per bit -- cheaper on sm_100 than match_any
+    uint32_t peers = 0xffffffffu;
+#pragma unroll
+    for (uint32_t b = 0; b < 9; ++b) {
+      const uint32_t bit = (d[r] >> b) & 1u;
+      const uint32_t bal = __ballot_sync(0xffffffffu, bit);
+      peers &= bit ? bal : ~bal;
+    }
     const uint32_t leader = __ffs(peers) - 1;
     uint32_t before = 0;
     if (lane == leader && d[r] < RADIX) {
