@@ -544,6 +544,8 @@ __global__ void __launch_bounds__(Q8_SPLATS, 3) q8_kernel(
   __shared__ float s_bas[Q8_SPLATS * 16];
   __shared__ float s_noise[Q8_SPLATS * 3];
   __shared__ uint32_t s_vmask[MODE == 2 ? Q8_SPLATS : 1];
+  __shared__ uint32_t s_list[MODE == 0 ? Q8_SPLATS : 1];  // splats with a gradient row (MODE 0)
+  __shared__ uint32_t s_wact[Q8_WARPS];
   __shared__ float s_lr[10];
   constexpr bool kDense = MODE != 0;
 
@@ -557,15 +559,19 @@ __global__ void __launch_bounds__(Q8_SPLATS, 3) q8_kernel(
   const uint32_t wsh = 3u * (uint32_t)nc;
   const uint32_t width = 10u + wsh + 1u;
 
-  // ---- phase 1: one splat per thread ----
+  // ---- phase 1: per-splat gradients into shared memory ----
+  // MODE 0 runs the VJP only for the splats with a non-zero gradient row,
+  // compacted first so that whole warps work on them (at a typical 60 %
+  // visibility every warp of 32 consecutive splats would otherwise carry the
+  // VJP with idle lanes); every value written is the same as per-thread code.
   {
     const uint32_t g = base + tid;
     float gr[10];
 #pragma unroll
     for (int k = 0; k < 10; ++k) gr[k] = 0.0f;
-    float go = 0.0f, vc0 = 0.0f, vc1 = 0.0f, vc2 = 0.0f, dx = 0.0f, dy = 0.0f, dz = 1.0f;
-    float nx = 0.0f, ny = 0.0f, nz = 0.0f;
+    float go = 0.0f;
     float vis_g = 0.0f;  // views that saw the splat (MODE 1 and 2)
+    bool active = false;
     if (g < n) {
       if (MODE == 2) {
         uint32_t vm = 0;
@@ -594,33 +600,72 @@ __global__ void __launch_bounds__(Q8_SPLATS, 3) q8_kernel(
         if (row > 0) {
           const float* rg = v_combined + (size_t)(row - 1) * 10;
           float rr[10];
-          bool any = false;
 #pragma unroll
           for (int k = 0; k < 10; ++k) {
             rr[k] = rg[k];
-            any = any || rr[k] != 0.0f;
+            active = active || rr[k] != 0.0f;
           }
-          if (any) {
-            float tt[10];
-#pragma unroll
-            for (int k = 0; k < 10; ++k) tt[k] = transforms[(size_t)g * 10 + k];
-            const VjpOut o = splat_vjp(tt, raw_opac[g], sh, min_scale, g, rr, u);
-            gr[0] = o.v_mean.x; gr[1] = o.v_mean.y; gr[2] = o.v_mean.z;
-            gr[3] = o.v_q.w; gr[4] = o.v_q.x; gr[5] = o.v_q.y; gr[6] = o.v_q.z;
-            gr[7] = o.v_scale.x; gr[8] = o.v_scale.y; gr[9] = o.v_scale.z;
-            go = o.v_raw;
-            vc0 = rr[5]; vc1 = rr[6]; vc2 = rr[7];
-            dx = o.dir.x; dy = o.dir.y; dz = o.dir.z;
-            refine = clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
-          }
+          if (active) refine = clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
         }
         if (refine_norm) refine_norm[g] = fmaxf(refine_norm[g], refine);
         if (vis_count) vis_count[g] += visible[g];
         if (max_screen) max_screen[g] = fmaxf(max_screen[g], max_radius[g]);
       }
+    }
+#pragma unroll
+    for (int k = 0; k < 10; ++k) s_gt[tid * 10 + k] = gr[k];
+    s_go[tid] = go;
+    s_vc[tid * 3 + 0] = 0.0f;
+    s_vc[tid * 3 + 1] = 0.0f;
+    s_vc[tid * 3 + 2] = 0.0f;
+    if (!kDense) {
+      // a splat without gradient has colour gradient 0: its bases only have
+      // to be finite
+#pragma unroll
+      for (int k = 0; k < 16; ++k) s_bas[tid * 16 + k] = 0.0f;
+      const uint32_t bal = __ballot_sync(0xffffffffu, active);
+      if (lane == 0) s_wact[warp] = __popc(bal);
+      __syncthreads();
+      uint32_t off = 0, total = 0;
+#pragma unroll
+      for (uint32_t w = 0; w < Q8_WARPS; ++w) {
+        const uint32_t c = s_wact[w];
+        off += w < warp ? c : 0u;
+        total += c;
+      }
+      if (active) s_list[off + __popc(bal & ((1u << lane) - 1u))] = tid;
+      __syncthreads();
+      for (uint32_t k = tid; k < total; k += Q8_SPLATS) {
+        const uint32_t t = s_list[k];
+        const uint32_t gg = base + t;
+        const float* rg = v_combined + (size_t)(compact_from_global[gg] - 1) * 10;
+        float rr[10], tt[10];
+#pragma unroll
+        for (int j = 0; j < 10; ++j) rr[j] = rg[j];
+#pragma unroll
+        for (int j = 0; j < 10; ++j) tt[j] = transforms[(size_t)gg * 10 + j];
+        const VjpOut o = splat_vjp(tt, raw_opac[gg], sh, min_scale, gg, rr, u);
+        float* dst = s_gt + t * 10;
+        dst[0] = o.v_mean.x; dst[1] = o.v_mean.y; dst[2] = o.v_mean.z;
+        dst[3] = o.v_q.w; dst[4] = o.v_q.x; dst[5] = o.v_q.y; dst[6] = o.v_q.z;
+        dst[7] = o.v_scale.x; dst[8] = o.v_scale.y; dst[9] = o.v_scale.z;
+        s_go[t] = o.v_raw;
+        s_vc[t * 3 + 0] = rr[5];
+        s_vc[t * 3 + 1] = rr[6];
+        s_vc[t * 3 + 2] = rr[7];
+        float b[16];
+        sh_basis_all(o.dir.x, o.dir.y, o.dir.z, b);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) s_bas[t * 16 + j] = b[j];
+      }
+      __syncthreads();
+    }
+    // opacity regulariser and mean noise, one splat per thread again
+    float nx = 0.0f, ny = 0.0f, nz = 0.0f;
+    if (g < n) {
       if (a.opac_reg != 0.0f) {
         const float o = 1.0f / (1.0f + vs_expf(-raw_opac[g]));
-        go = go + a.opac_reg * o * (1.0f - o);
+        s_go[tid] = s_go[tid] + a.opac_reg * o * (1.0f - o);
       }
       if ((visible || MODE == 2) && a.noise_scale != 0.0f) {
         // without per-view opacities (the multi-view path) the gate uses the
@@ -629,18 +674,6 @@ __global__ void __launch_bounds__(Q8_SPLATS, 3) q8_kernel(
         const float op = opacities ? opacities[g] : 1.0f / (1.0f + vs_expf(-raw_opac[g]));
         mean_noise(g, op, kDense ? vis_g : visible[g], a.noise_scale, a.noise_limit, a.noise_seed, &nx, &ny, &nz);
       }
-    }
-#pragma unroll
-    for (int k = 0; k < 10; ++k) s_gt[tid * 10 + k] = gr[k];
-    s_go[tid] = go;
-    s_vc[tid * 3 + 0] = vc0;
-    s_vc[tid * 3 + 1] = vc1;
-    s_vc[tid * 3 + 2] = vc2;
-    if (!kDense) {
-      float b[16];
-      sh_basis_all(dx, dy, dz, b);
-#pragma unroll
-      for (int k = 0; k < 16; ++k) s_bas[tid * 16 + k] = b[k];
     }
     s_noise[tid * 3 + 0] = nx;
     s_noise[tid * 3 + 1] = ny;
