@@ -1286,12 +1286,15 @@ OR_API int or_vjp_dense(const Camera* cam, const RenderCfg* cfg, uint32_t n, con
 //  * blocks of 256 consecutive values of one parameter tensor;
 //  * m: signed codes (+128 bias), scale = absmax|m| / 127;
 //  * v: sqrt(v) as unsigned codes, scale = absmax sqrt(v) / 255;
-//  * both re-encoded with stochastic rounding from vs_mix_hash(index,
-//    step ^ salt): m code = floor(m/scale + u1), r code = floor(r/scale + u2);
+//  * both re-encoded with stochastic rounding: h = vs_mix_hash(index / 2,
+//    step ^ salt); value index i takes the bytes 2 (i % 2) and 2 (i % 2) + 1
+//    of h as b_m, b_v and uniforms u = (b + 1/2) / 256:
+//    m code = floor(m/scale + u1), r code = floor(r/scale + u2);
 //  * scales enter as reciprocals: code = floor(m * (1/scale) + u);
-//  * step = (m1 inv1) / max(sqrt(v1) sqrt(inv2) + eps, |m1 inv1| / 8): the
-//    normalized update is bounded by 8, the bound the reference's packed
-//    geometry codec imposes (src/bwd/kernels/geo_moments.rs:186,192).
+//  * step = (m1 inv1) * (1 / d), d = max(sqrt(v1) sqrt(inv2) + eps,
+//    |m1 inv1| / 8), with 1 / d taken as 0 for d >= 2^126: the normalized
+//    update is bounded by 8, the bound the reference's packed geometry codec
+//    imposes (src/bwd/kernels/geo_moments.rs:186,192).
 // grads [count] (dense); lr per column: lr_col[index % row_width] * lr.
 // Optional weight decay of zero gradients is not applied (dense Adam).
 // ===========================================================================
@@ -1318,7 +1321,8 @@ OR_API int or_adam_q8(size_t count, uint32_t row_width, float* params, const flo
       const float r = sqrtf(v);
       const float mh = m * inv1;
       const float denom = fmaxf(r * sqrt_inv2 + eps, fabsf(mh) * 0.125f);
-      params[i] = params[i] - (mh / denom) * (lr_col[col] * lr);
+      const float inv_d = denom < 8.5070592e37f ? 1.0f / denom : 0.0f;
+      params[i] = params[i] - (mh * inv_d) * (lr_col[col] * lr);
       m1[j] = m;
       r1[j] = r;
     }
@@ -1333,8 +1337,9 @@ OR_API int or_adam_q8(size_t count, uint32_t row_width, float* params, const flo
     v_scales[bi] = nvs;
     for (size_t j = 0; j < nb; ++j) {
       const size_t i = b0 + j;
-      const uint32_t hsh = vs_mix_hash((uint32_t)i, seed);
-      const float u1 = (float)(hsh >> 16) * (1.0f / 65536.0f), u2 = (float)(hsh & 0xffffu) * (1.0f / 65536.0f);
+      const uint32_t hb = vs_mix_hash((uint32_t)(i >> 1), seed) >> (16 * (i & 1));
+      const float u1 = ((float)(hb & 0xffu) + 0.5f) * (1.0f / 256.0f);
+      const float u2 = ((float)((hb >> 8) & 0xffu) + 0.5f) * (1.0f / 256.0f);
       float qm = 0.0f, qr = 0.0f;
       if (nms > 0.0f) qm = clampf(floorf(m1[j] * inv_ms + u1), -127.0f, 127.0f);
       if (nvs > 0.0f) qr = clampf(floorf(r1[j] * inv_vs + u2), 0.0f, 255.0f);

@@ -454,7 +454,9 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
     const float r = sqrt_rn(v);
     const float mh = m * a.inv1;
     const float denom = fmaxf(r * a.sqrt_inv2 + a.eps, fabsf(mh) * 0.125f);
-    float pn = pv[k] - div_rn(mh, denom) * lr[k];
+    // mh / denom as mh times the correctly rounded reciprocal (0 from 2^126 on)
+    const float inv_d = denom < 8.5070592e37f ? rcp_rn(denom) : 0.0f;
+    float pn = pv[k] - (mh * inv_d) * lr[k];
     if (KIND == 0) pn = pn + nz[k];
     pv[k] = pn;
     m1[k] = m;
@@ -480,13 +482,17 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
   for (int h = 0; h < 2; ++h) {
     const uint32_t li0 = v0 + 128u * h + 4u * lane;
     uint32_t mo = 0u, vo = 0u;
+    // one hash per pair of values: bytes 0/1 are the m and sqrt(v) uniforms of
+    // the even value, bytes 2/3 those of the odd one
+    const uint32_t hp[2] = {vs_mix_hash((hbase + li0) >> 1, a.seed ^ salt),
+                            vs_mix_hash(((hbase + li0) >> 1) + 1u, a.seed ^ salt)};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int k = 4 * h + e;
-      const uint32_t hsh = vs_mix_hash(hbase + li0 + (uint32_t)e, a.seed ^ salt);
-      // h / 65536 for a 16-bit h, exactly: (1 + h 2^-16) - 1
-      const float u1 = __uint_as_float(0x3F800000u | ((hsh >> 16) << 7)) - 1.0f;
-      const float u2 = __uint_as_float(0x3F800000u | ((hsh & 0xffffu) << 7)) - 1.0f;
+      const uint32_t hb = hp[e >> 1] >> (16 * (e & 1));
+      // (b + 1/2) / 256 for a byte b, exactly: (1 + b 2^-8 + 2^-9) - 1
+      const float u1 = __uint_as_float(0x3F804000u | ((hb & 0xffu) << 15)) - 1.0f;
+      const float u2 = __uint_as_float(0x3F804000u | (((hb >> 8) & 0xffu) << 15)) - 1.0f;
       // clamp(floor(x), lo, hi) = floor(clamp(x, lo, hi)) for integer bounds
       // (NaN clamps to lo either way); floor of |y| < 2^22 is the low
       // mantissa of y + 1.5 2^23 rounded toward -inf.
@@ -532,7 +538,7 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
 // the shard of CTAs starting at pa.cta_begin, parameters stored to all
 // replicas.  `n` is one past the last splat this launch may touch.
 template <int MODE>
-__global__ void __launch_bounds__(Q8_SPLATS, 3) q8_kernel(
+__global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
     Uniforms u, uint32_t n, float* __restrict__ transforms, float* __restrict__ sh, float* __restrict__ raw_opac,
     const float* __restrict__ min_scale, const uint32_t* __restrict__ compact_from_global,
     const float* __restrict__ v_combined, const float* __restrict__ grads, Q8T mt, Q8T msh, Q8T mo, Q8Args a,
