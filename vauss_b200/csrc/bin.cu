@@ -16,7 +16,6 @@ using namespace vs;
 
 constexpr uint32_t BIN_BLOCK = 256;
 constexpr uint32_t BIG_BOX = 16;
-constexpr uint32_t EMIT_CAP = 4096;  // pairs a block assembles in shared memory
 
 __global__ void depth_keys_kernel(const float* __restrict__ depths, uint32_t v, uint32_t* __restrict__ keys,
                                   uint32_t* __restrict__ ids) {
@@ -36,32 +35,14 @@ __global__ void gather_counts_kernel(const uint32_t* __restrict__ order, const u
 // One thread per depth-sorted splat; large boxes are walked by the whole warp
 // (map_gaussians.rs:117-173).  Emission stops at the splat's counted budget
 // and pads any shortfall with the sentinel tile id T (map_gaussians.rs:76-113).
-// A block's splats are consecutive in depth order, so their pairs form one
-// contiguous range of the output; when it fits, the pairs are assembled in
-// shared memory and written out coalesced (each thread's own run would
-// otherwise be a separate 4-byte store per lane).
 __global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v, const uint32_t* __restrict__ order,
                                                          const uint32_t* __restrict__ cum,
                                                          const float4* __restrict__ projected,
                                                          uint32_t* __restrict__ tile_keys,
                                                          uint32_t* __restrict__ compact_vals) {
-  __shared__ uint32_t s_key[EMIT_CAP], s_val[EMIT_CAP];
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t lane = threadIdx.x & 31u;
   const bool active = i < v;
-  const uint32_t first = blockIdx.x * blockDim.x, last = min(v, first + blockDim.x) - 1u;
-  const uint32_t blk_start = first ? cum[first - 1] : 0u;
-  const uint32_t blk_len = cum[last] - blk_start;
-  const bool staged = blk_len <= EMIT_CAP;  // uniform over the block
-  auto put = [&](uint32_t idx, uint32_t key, uint32_t val) {
-    if (staged) {
-      s_key[idx - blk_start] = key;
-      s_val[idx - blk_start] = val;
-    } else {
-      tile_keys[idx] = key;
-      compact_vals[idx] = val;
-    }
-  };
   const uint32_t T = u.tbw * u.tbh;
   uint32_t c = 0, start = 0, budget = 0, nb = 0, bw = 0;
   float px = 0.f, py = 0.f, pt = 0.f;
@@ -87,12 +68,14 @@ __global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v,
     for (uint32_t k = 0; k < nb && slot < budget; ++k) {
       const uint32_t tx = k % bw + b.x0, ty = k / bw + b.y0;
       if (tile_hit(tx, ty, px, py, conic, pt)) {
-        put(start + slot, tx + ty * u.tbw, c);
+        tile_keys[start + slot] = tx + ty * u.tbw;
+        compact_vals[start + slot] = c;
         ++slot;
       }
     }
     for (; slot < budget; ++slot) {
-      put(start + slot, T, c);
+      tile_keys[start + slot] = T;
+      compact_vals[start + slot] = c;
     }
   }
   uint32_t pending = __ballot_sync(0xffffffffu, active && nb > BIG_BOX);
@@ -118,21 +101,16 @@ __global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v,
       const uint32_t mask = __ballot_sync(0xffffffffu, hit);
       const uint32_t slot = emitted + __popc(mask & ((1u << lane) - 1u));
       if (hit && slot < lbudget) {
-        put(lstart + slot, tx + ty * u.tbw, lc_id);
+        tile_keys[lstart + slot] = tx + ty * u.tbw;
+        compact_vals[lstart + slot] = lc_id;
       }
       emitted += __popc(mask);
     }
     for (uint32_t p = min(emitted, lbudget) + lane; p < lbudget; p += 32) {
-      put(lstart + p, T, lc_id);
+      tile_keys[lstart + p] = T;
+      compact_vals[lstart + p] = lc_id;
     }
     pending &= pending - 1u;
-  }
-  if (staged) {
-    __syncthreads();
-    for (uint32_t j = threadIdx.x; j < blk_len; j += blockDim.x) {
-      tile_keys[blk_start + j] = s_key[j];
-      compact_vals[blk_start + j] = s_val[j];
-    }
   }
 }
 
