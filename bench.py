@@ -53,12 +53,12 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--splats", type=int, default=None, help="default: 3M (config 2), 6M (config 3)")
-    p.add_argument("--config", type=int, default=2, choices=[2, 3])
+    p.add_argument("--config", type=int, default=2, choices=[2, 3, 4])
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     a = p.parse_args()
     if a.splats is None:
-        a.splats = N_SPLATS if a.config == 2 else 6_000_000
+        a.splats = {2: N_SPLATS, 3: 6_000_000, 4: 10_000_000}[a.config]
     return a
 
 
@@ -148,7 +148,8 @@ def make_workload(n_splats: int, config: int = 2):
 # capture of this workload (config 2 at 3M splats; profiles/<kernel>_config2_3M.md
 # give the command).  Below the algorithmic bytes for the raster kernels:
 # L2 (126 MB) serves a projected row to the neighbouring tiles that gather it.
-MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 235.05e6, "raster_fwd": 142.5e6, "project": 641.9e6, "loss": 60.8e6}
+MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 235.05e6, "raster_fwd": 142.5e6, "project": 641.9e6, "loss": 60.8e6,
+                           "optimizer": 2.335e9}
 
 
 def stage_bytes(name: str, n: int, v: int, i: int, p: int, t: int) -> float:
@@ -500,10 +501,91 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_sort_stress(args):
+    """BASELINE config 4 (sort/overlap stress): 10M splats with large
+    footprints (log-scales N(-2.5, 0.5), opacity logits N(1, 1), config-2
+    means and SH), one 3840x2160 view, fx = fy = 3000.  Times projection,
+    binning (intersection emission, depth and tile radix sorts, tile ranges),
+    the forward and the backward under an N(0, 1e-3) upstream gradient.  The
+    metric is intersections per second through intersect + sort + ranges.
+    One view: under torchrun only rank 0 runs (replicas only)."""
+    import torch
+    from vauss_b200 import ops, scenes
+    from vauss_b200.camera import look_at
+    from vauss_b200.trainer import Splats
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    n = args.splats
+    sp = scenes.random_splats(n, 4004, mean_lo=-5.0, mean_hi=5.0, log_scale_mu=-2.5, log_scale_sigma=0.5,
+                              opac_mu=1.0, opac_sigma=1.0, sh_degree=3)
+    cam = look_at((0.0, -3.0, 8.0), (0.0, 0.0, 0.0), 3840, 2160, 3000.0)
+    splats = Splats.from_numpy(sp, dev)
+    del sp
+    frame = ops.Frame(ops.context(dev))
+    cfg = ops.render_cfg(3, mip=True)
+    img = torch.empty(cam.height, cam.width, 4, device=dev)
+    vis = torch.empty(n, device=dev)
+    v_out = torch.randn(cam.height, cam.width, 4, device=dev, generator=torch.Generator(device=dev).manual_seed(1)) * 1e-3
+    vc = torch.empty(n, 10, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    names = ("project", "bin", "raster_fwd", "raster_bwd")
+    acc = {k: 0.0 for k in names}
+
+    def step(timed):
+        evs = [torch.cuda.Event(enable_timing=True)]
+        evs[0].record(stream)
+
+        def hook(name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            evs.append(e)
+        out = ops.render_stages(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, frame, img, vis,
+                                hook=hook)
+        ops.rasterize_bwd(out.frame, out.out_img, v_out, vc)
+        hook("raster_bwd")
+        torch.cuda.synchronize()
+        if timed:
+            for k, (e0, e1) in zip(names, zip(evs[:-1], evs[1:])):
+                acc[k] += e0.elapsed_time(e1)
+
+    for _ in range(args.warmup):
+        step(False)
+    gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    with ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}") as clk:
+        clk.mark("start")
+        for _ in range(args.steps):
+            step(True)
+        clk.mark("stop")
+    counts = frame.counts
+    isect, visible = int(counts.num_intersections), int(counts.num_visible)
+    ms = {k: acc[k] / args.steps for k in names}
+    sort_ms = ms["project"] + ms["bin"]
+    peak, which = peaks()
+    bin_bytes = stage_bytes("bin", n, visible, isect, cam.width * cam.height, cam.num_tiles)
+    out = {"metric": "sort stress: intersections/s through intersect + radix sort + tile ranges @10M large splats 3840x2160",
+           "value": round(isect / (sort_ms / 1e3), 1), "unit": "intersections/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(sum(ms.values()), 3), "higher_is_better": True,
+           "scaling": "replicas only", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "config 4: 10M SH-3 splats, log-scales N(-2.5,0.5), opacity logits N(1,1), one "
+                                  "3840x2160 view, fx=fy=3000, project+bin+raster fwd+raster bwd (N(0,1e-3) upstream)",
+                      "splats": n, "visible": visible, "intersections": isect,
+                      "l2": "inputs larger than L2"},
+           "stages": {k: {"ms": round(v, 3)} for k, v in ms.items()},
+           "roofline": {"bound": "hbm", "kernel": "bin", "achieved": round(bin_bytes / (ms["bin"] / 1e3) / 1e9, 1),
+                        "peak": peak, "unit": "GB/s", "frac": round(bin_bytes / (ms["bin"] / 1e3) / 1e9 / peak, 4),
+                        "traffic": None, "peak_source": which},
+           "clocks": clk.summary()}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == 4:
+        run_sort_stress(args)
     else:
         run_ours(args)
 
