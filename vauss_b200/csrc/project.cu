@@ -164,7 +164,7 @@ __device__ __forceinline__ void lb_store(unsigned long long* p, unsigned long lo
   r.store(v, cuda::memory_order_release);
 }
 
-__global__ void __launch_bounds__(PROJ_BLOCK, 3) project_kernel(
+__global__ void __launch_bounds__(PROJ_BLOCK, 4) project_kernel(
     Uniforms u, uint32_t n, const float* __restrict__ transforms, const void* __restrict__ sh,
     const float* __restrict__ raw_opac, const float* __restrict__ min_scale, uint32_t* __restrict__ compact_from_global,
     float* __restrict__ opacities, float* __restrict__ max_radius, uint32_t* __restrict__ global_from_compact,
