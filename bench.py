@@ -479,6 +479,8 @@ def _q8_zero(count):
 def cpu_baseline(sp, tgt, cams, views, steps=1, warmup=0, gt=None):
     import oracle
     from vauss_b200 import scenes
+    # all host cores, whatever OMP_NUM_THREADS a launcher set for this process
+    cores = oracle.set_num_threads(os.cpu_count() or 1)
     cam = cams[views[0]]
     cfg = oracle.make_cfg(3, mip=True)
     if gt is None:
@@ -491,7 +493,6 @@ def cpu_baseline(sp, tgt, cams, views, steps=1, warmup=0, gt=None):
     for k in range(steps):
         oracle_step(sp, cam, gt, mom, warmup + k + 1)
     dt = (time.perf_counter() - t0) / steps
-    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
     return {"value": round(1.0 / dt, 5), "unit": "iters/s", "cores": cores, "kind": "port",
             "sample": f"{steps} full config-2 step(s) of the C++ oracle (OpenMP), after {warmup} warm-up"}
 

@@ -401,3 +401,9 @@ def ply_encode(transforms, sh, raw_opac):
                              _p(out, F32P))
     assert rc == 0
     return out[:n]
+
+
+def set_num_threads(n: int) -> int:
+    """Threads for the OpenMP loops; returns the count now in effect."""
+    lib().or_set_num_threads(ctypes.c_int(int(n)))
+    return int(lib().or_max_threads())

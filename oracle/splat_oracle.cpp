@@ -20,6 +20,7 @@
 // Reductions whose order differs on the GPU (atomics in the rasterizer
 // backward) are compared with a tolerance by the tests.
 
+#include <omp.h>
 #include <stdint.h>
 #include <string.h>
 #include <math.h>
@@ -1586,3 +1587,8 @@ OR_API int or_ply_encode(uint32_t n, int32_t degree, const float* transforms, co
   }
   return 0;
 }
+
+// Thread count of the OpenMP loops above (a launcher such as torchrun sets
+// OMP_NUM_THREADS=1 in every process; the CPU baseline asks for all cores).
+OR_API void or_set_num_threads(int n) { omp_set_num_threads(n > 0 ? n : 1); }
+OR_API int or_max_threads(void) { return omp_get_max_threads(); }
