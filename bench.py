@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the Gaussian-splat training step (fwd + bwd + Adam).
 
-Workload ("full training iteration at scale"):
+Workload (benchmark configuration 2, "full training iteration at scale"):
 3,000,000 SH-degree-3 splats (means U[-5,5]^3, log-scales N(-4.5, 0.6),
 opacity logits N(0, 1.5), DC colours U[0,1], higher bands N(0, 0.05)),
 200 pinhole views of 1600x1060 (fx = fy = 1300) on a jittered sphere of
@@ -12,17 +12,22 @@ Synthetic data stand in for the reference's capture datasets.
 
 One step = project/sort/rasterize forward, fused loss forward+backward,
 rasterizer backward, projection VJP + Adam + refine statistics + mean noise.
-With N GPUs every rank trains its own view per step and the dense gradient is
-all-reduced over NCCL before the replicated Adam step (weak scaling: one view
-per GPU per step); value = views/s over the whole job = iterations/s at N = 1.
+With N GPUs every rank trains its own view per step; the ranks' dense
+gradient rows are read over NVLink peer memory by a sharded fused Adam that
+stores the new parameters into every replica (weak scaling: one view per GPU
+per step); value = views/s over the whole job = iterations/s at N = 1.
 
-With --config 3 it runs BASELINE configuration 3 instead: 6,000,000 splats
+With --config 3 it runs benchmark configuration 3 instead: 6,000,000 splats
 (configuration-2 distributions) and a fixed global batch of 8 views of
 1920x1080 (fx = fy = 1600) per step, split evenly over 1, 2, 4 or 8 GPUs
 (strong scaling; value = global-batch steps/s).  Every GPU count, one
 included, runs the peer-memory view-parallel trainer.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--config 2|3]
+With --config 4 it runs the sort/overlap stress (configuration 4, one GPU):
+10,000,000 large splats, one 3840x2160 view; value = intersections/s through
+intersect + radix sort + tile ranges.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--config 2|3|4]
 """
 from __future__ import annotations
 
@@ -523,7 +528,7 @@ def run_reference(args):
 
 
 def run_sort_stress(args):
-    """BASELINE config 4 (sort/overlap stress): 10M splats with large
+    """Benchmark configuration 4 (sort/overlap stress): 10M splats with large
     footprints (log-scales N(-2.5, 0.5), opacity logits N(1, 1), config-2
     means and SH), one 3840x2160 view, fx = fy = 3000.  Times projection,
     binning (intersection emission, depth and tile radix sorts, tile ranges),

@@ -256,7 +256,7 @@ def vjp_dense(cam, cfg, transforms, sh, raw_opac, compact_from_global, v_combine
 
 def adam_q8(params, grads, grad_stride, grad_offset, row_width, m_codes, v_codes, m_scales, v_scales, lr_col, lr,
             b1, b2, inv1, inv2, eps, seed):
-    """BASELINE 8-bit m+v Adam on one flattened parameter tensor (copies)."""
+    """The benchmark's 8-bit m+v Adam on one flattened parameter tensor (copies)."""
     L = lib()
     p = _f32(params).copy()
     count = p.size

@@ -1282,8 +1282,9 @@ OR_API int or_vjp_dense(const Camera* cam, const RenderCfg* cfg, uint32_t n, con
 }
 
 // ===========================================================================
-// Adam with 8-bit block-quantized first AND second moments (the BASELINE
-// "Q8" optimizer; no reference counterpart, defined by this project):
+// Adam with 8-bit block-quantized first AND second moments (the benchmark
+// configurations' "Q8" optimizer; no reference counterpart, defined by this
+// project):
 //  * blocks of 256 consecutive values of one parameter tensor;
 //  * m: signed codes (+128 bias), scale = absmax|m| / 127;
 //  * v: sqrt(v) as unsigned codes, scale = absmax sqrt(v) / 255;
