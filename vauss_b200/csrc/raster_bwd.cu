@@ -4,9 +4,10 @@
 // Replaces rasterize_backwards_planes_kernel (crates/splat-train-render/src/
 // bwd/kernels/rasterize_backwards_planes.rs:112-682, gaussian branch):
 // one 128-thread CTA per tile, each warp an 8x8 quadrant, two pixels per
-// thread, splats staged 32 at a time in shared memory.  A warp walks only the
-// splats that can reach its quadrant (reach_rect).  Per splat,
-// each thread sums its pixels' gradients, a 12-shuffle butterfly
+// thread, splats staged 128 at a time in shared memory (one per thread; larger
+// batches halve the barriers and partial-buffer work per splat each time they
+// double).  A warp walks only the splats that can reach its quadrant
+// (reach_rect).  Per splat, each thread sums its pixels' gradients, a 12-shuffle butterfly
 // reduce-scatter leaves one component per lane pair, the four warps' partials
 // are added in shared memory, and one atomic add per non-zero (tile, splat,
 // component) lands in v_combined [V,10] = [xy(2), conic(3), rgb(3), alpha,
@@ -23,7 +24,7 @@ using namespace vs;
 
 constexpr uint32_t RB_THREADS = 128;
 constexpr uint32_t RB_WARPS = RB_THREADS / 32;
-constexpr uint32_t RB_BATCH = 32;
+constexpr uint32_t RB_BATCH = 128;
 constexpr uint32_t NG = 10;
 
 // Butterfly reduce-scatter of the NG = 10 gradient components over a warp in
@@ -146,73 +147,77 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
       s_cid[tid] = c;
     }
     __syncthreads();
-    // The warp walks only the splats that can reach its quadrant.
-    bool near = false;
-    if (lane < cnt) {
-      const float4 sa = s_a[lane], rc = s_rc[lane];
-      near = reach_rect(sa.x, sa.y, sa.z, sa.w, s_b[lane].x, ReachCut{rc.x, rc.y, rc.z}, rx0, rx1, ry0, ry1);
-    }
-    uint32_t m = __ballot_sync(0xffffffffu, near);
-    while (m) {
-      const uint32_t t = __ffs(m) - 1;
-      m &= m - 1u;
-      const float4 a = s_a[t];
-      const float4 bb = s_b[t];
-      const float2 cc = s_c[t];
-      const float h00 = a.z, c01 = a.w, h11 = bb.x, opac = bb.y;
-      const float c00 = 2.0f * h00, c11 = 2.0f * h11;
-      const float cr = fmaxf(bb.z, 0.0f), cg = fmaxf(bb.w, 0.0f), cb = fmaxf(cc.x, 0.0f);
-      const float dx = a.x - fx;
-      float g[NG];
-#pragma unroll
-      for (int i = 0; i < (int)NG; ++i) g[i] = 0.0f;
-      bool contributes = false;
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const float dy = a.y - fy[k];
-        // coverage decisions: the forward's exact arithmetic
-        const float sigma = raster_sigma(h00, c01, h11, dx, dy);
-        if (!(st[k] > 1.0e-4f && sigma <= cc.y)) continue;
-        const float gauss = vs_expf_core(-sigma);  // = vs_expf: used only for 0 <= sigma <= cut < 6
-        const float alpha = fminf(0.999f, opac * gauss);
-        if (!(sigma >= 0.0f && alpha >= ALPHA_MIN)) continue;
-        const float next_t = st[k] * (1.0f - alpha);
-        if (next_t <= 1.0e-4f) {
-          st[k] = 0.0f;
-          continue;
-        }
-        contributes = true;
-        // gradients: the oracle's per-term float steps (the same fmas), summed
-        // in another order
-        const float vis = alpha * st[k];
-        if (bb.z >= 0.0f) g[5] += vis * vr[k];
-        if (bb.w >= 0.0f) g[6] += vis * vg[k];
-        if (cc.x >= 0.0f) g[7] += vis * vb[k];
-        const float ra = rcp_rn(1.0f - alpha);  // 1 - alpha in [1e-3, 1]
-        const float dot =
-            fmaf(fmaf(st[k], cr, -sr[k]), vr[k], fmaf(fmaf(st[k], cg, -sg[k]), vg[k], fmaf(st[k], cb, -sb[k]) * vb[k])) * ra;
-        const float v_alpha = fmaf(vt[k], ra, dot);
-        const float v_sigma = -alpha * v_alpha;
-        const float vxx = v_sigma * fmaf(c00, dx, c01 * dy);
-        const float vxy = v_sigma * fmaf(c01, dx, c11 * dy);
-        if (opac * gauss <= 0.999f) {
-          g[2] += 0.5f * v_sigma * dx * dx;
-          g[3] += v_sigma * dx * dy;
-          g[4] += 0.5f * v_sigma * dy * dy;
-          g[0] += vxx;
-          g[1] += vxy;
-          g[8] += v_alpha * gauss;
-          const float ax = vxx * img_w, ay = vxy * img_h;
-          g[9] += sqrt_rn(fmaf(ax, ax, ay * ay)) * rs[k];
-        }
-        sr[k] = fmaf(-vis, cr, sr[k]);
-        sg[k] = fmaf(-vis, cg, sg[k]);
-        sb[k] = fmaf(-vis, cb, sb[k]);
-        st[k] = next_t;
+    // The warp walks only the splats that can reach its quadrant, testing 32
+    // staged splats at a time (a lane each).
+    for (uint32_t half = 0; half < RB_BATCH / 32u; ++half) {
+      const uint32_t sl = half * 32u + lane;
+      bool near = false;
+      if (sl < cnt) {
+        const float4 sa = s_a[sl], rc = s_rc[sl];
+        near = reach_rect(sa.x, sa.y, sa.z, sa.w, s_b[sl].x, ReachCut{rc.x, rc.y, rc.z}, rx0, rx1, ry0, ry1);
       }
-      if (__any_sync(0xffffffffu, contributes)) {
-        const float sum = reduce10(g, lane);
-        if ((lane & 1u) == 0 && comp >= 0) s_part[warp][t][comp] = sum;
+      uint32_t m = __ballot_sync(0xffffffffu, near);
+      while (m) {
+        const uint32_t t = half * 32u + __ffs(m) - 1;
+        m &= m - 1u;
+        const float4 a = s_a[t];
+        const float4 bb = s_b[t];
+        const float2 cc = s_c[t];
+        const float h00 = a.z, c01 = a.w, h11 = bb.x, opac = bb.y;
+        const float c00 = 2.0f * h00, c11 = 2.0f * h11;
+        const float cr = fmaxf(bb.z, 0.0f), cg = fmaxf(bb.w, 0.0f), cb = fmaxf(cc.x, 0.0f);
+        const float dx = a.x - fx;
+        float g[NG];
+  #pragma unroll
+        for (int i = 0; i < (int)NG; ++i) g[i] = 0.0f;
+        bool contributes = false;
+  #pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const float dy = a.y - fy[k];
+          // coverage decisions: the forward's exact arithmetic
+          const float sigma = raster_sigma(h00, c01, h11, dx, dy);
+          if (!(st[k] > 1.0e-4f && sigma <= cc.y)) continue;
+          const float gauss = vs_expf_core(-sigma);  // = vs_expf: used only for 0 <= sigma <= cut < 6
+          const float alpha = fminf(0.999f, opac * gauss);
+          if (!(sigma >= 0.0f && alpha >= ALPHA_MIN)) continue;
+          const float next_t = st[k] * (1.0f - alpha);
+          if (next_t <= 1.0e-4f) {
+            st[k] = 0.0f;
+            continue;
+          }
+          contributes = true;
+          // gradients: the oracle's per-term float steps (the same fmas), summed
+          // in another order
+          const float vis = alpha * st[k];
+          if (bb.z >= 0.0f) g[5] += vis * vr[k];
+          if (bb.w >= 0.0f) g[6] += vis * vg[k];
+          if (cc.x >= 0.0f) g[7] += vis * vb[k];
+          const float ra = rcp_rn(1.0f - alpha);  // 1 - alpha in [1e-3, 1]
+          const float dot =
+              fmaf(fmaf(st[k], cr, -sr[k]), vr[k], fmaf(fmaf(st[k], cg, -sg[k]), vg[k], fmaf(st[k], cb, -sb[k]) * vb[k])) * ra;
+          const float v_alpha = fmaf(vt[k], ra, dot);
+          const float v_sigma = -alpha * v_alpha;
+          const float vxx = v_sigma * fmaf(c00, dx, c01 * dy);
+          const float vxy = v_sigma * fmaf(c01, dx, c11 * dy);
+          if (opac * gauss <= 0.999f) {
+            g[2] += 0.5f * v_sigma * dx * dx;
+            g[3] += v_sigma * dx * dy;
+            g[4] += 0.5f * v_sigma * dy * dy;
+            g[0] += vxx;
+            g[1] += vxy;
+            g[8] += v_alpha * gauss;
+            const float ax = vxx * img_w, ay = vxy * img_h;
+            g[9] += sqrt_rn(fmaf(ax, ax, ay * ay)) * rs[k];
+          }
+          sr[k] = fmaf(-vis, cr, sr[k]);
+          sg[k] = fmaf(-vis, cg, sg[k]);
+          sb[k] = fmaf(-vis, cb, sb[k]);
+          st[k] = next_t;
+        }
+        if (__any_sync(0xffffffffu, contributes)) {
+          const float sum = reduce10(g, lane);
+          if ((lane & 1u) == 0 && comp >= 0) s_part[warp][t][comp] = sum;
+        }
       }
     }
     __syncthreads();
