@@ -153,7 +153,7 @@ def make_workload(n_splats: int, config: int = 2):
 # capture of this workload (config 2 at 3M splats; profiles/<kernel>_config2_3M.md
 # give the command).  Below the algorithmic bytes for the raster kernels:
 # L2 (126 MB) serves a projected row to the neighbouring tiles that gather it.
-MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 235.05e6, "raster_fwd": 142.5e6, "project": 641.9e6, "loss": 60.8e6,
+MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 272.8e6, "raster_fwd": 142.5e6, "project": 686.8e6, "loss": 60.8e6,
                            "optimizer": 2.335e9}
 
 
