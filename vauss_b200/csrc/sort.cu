@@ -13,6 +13,7 @@
 // by one ballot per digit bit,
 // warps are combined through per-digit counts), scatters them into shared
 // memory in digit order and writes contiguous per-digit runs to global memory.
+#include <cuda/atomic>
 #include <mutex>
 
 #include "vs_internal.cuh"
@@ -229,20 +230,117 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_apply_kernel(uint32_t* __re
   }
 }
 
+// ---- device-wide scan in one launch: decoupled look-back ----
+// Chunks of 4096 values are taken in launch order (an atomic ticket, so a
+// chunk only waits on chunks that have started).  Each publishes its sum at
+// once, then warp 0 walks back over the status words, 32 at a time, to the
+// nearest inclusive prefix (flag 2), publishes its own inclusive prefix and
+// the chunk writes its values.  Status word: flag in the high half (1 =
+// chunk sum, 2 = inclusive prefix), value in the low half.  Waits are bounded:
+// a walk that gives up sets VS_DERR_WAIT and the chunk writes nothing.
+constexpr uint32_t SCAN_SPIN_LIMIT = 1u << 22;
+
+__device__ __forceinline__ unsigned long long scan_status_load(unsigned long long* p) {
+  cuda::atomic_ref<unsigned long long, cuda::thread_scope_device> r(*p);
+  return r.load(cuda::memory_order_acquire);
+}
+__device__ __forceinline__ void scan_status_store(unsigned long long* p, unsigned long long v) {
+  cuda::atomic_ref<unsigned long long, cuda::thread_scope_device> r(*p);
+  r.store(v, cuda::memory_order_release);
+}
+
+template <bool kInclusive>
+__global__ void __launch_bounds__(SCAN_THREADS) scan_lookback_kernel(uint32_t* __restrict__ data, uint32_t count,
+                                                                     uint32_t nchunks, unsigned long long* status,
+                                                                     uint32_t* ticket, unsigned long long* total_dev,
+                                                                     uint32_t* err) {
+  __shared__ uint32_t s_warp[32];
+  __shared__ uint32_t s_chunk, s_prefix, s_fail;
+  const uint32_t tid = threadIdx.x, lane = tid & 31u;
+  if (tid == 0) {
+    s_chunk = atomicAdd(ticket, 1u);
+    s_fail = 0u;
+  }
+  __syncthreads();
+  const uint32_t chunk = s_chunk;
+  const uint32_t base = chunk * SCAN_CHUNK + tid * SCAN_ITEMS;
+  uint32_t x[SCAN_ITEMS];
+  uint32_t sum = 0;
+#pragma unroll
+  for (uint32_t i = 0; i < SCAN_ITEMS; ++i) {
+    x[i] = (base + i < count) ? data[base + i] : 0u;
+    sum += x[i];
+  }
+  uint32_t total;
+  const uint32_t in_chunk = block_exclusive_scan(sum, s_warp, &total);
+  if (tid == 0) scan_status_store(&status[chunk], ((chunk == 0 ? 2ull : 1ull) << 32) | total);
+  if (tid < 32) {
+    uint32_t exclusive = 0;
+    if (chunk > 0) {
+      int64_t hi = (int64_t)chunk - 1;
+      uint32_t spins = 0;
+      while (true) {
+        const int64_t q = hi - (int64_t)lane;
+        const unsigned long long st = q >= 0 ? scan_status_load(&status[q]) : (2ull << 32);
+        const uint32_t flag = (uint32_t)(st >> 32);
+        const uint32_t incl = __ballot_sync(0xffffffffu, flag == 2u);
+        const uint32_t pending = __ballot_sync(0xffffffffu, flag == 0u);
+        const uint32_t first = incl ? (uint32_t)(__ffs(incl) - 1) : 32u;
+        const uint32_t needed = first >= 31u ? 0xffffffffu : ((2u << first) - 1u);
+        if (pending & needed) {
+          if (++spins > SCAN_SPIN_LIMIT) {
+            if (lane == 0) {
+              atomicOr(err, VS_DERR_WAIT);
+              s_fail = 1u;
+            }
+            break;
+          }
+          if (spins > 32) __nanosleep(64);
+          continue;
+        }
+        uint32_t part = lane <= first ? (uint32_t)st : 0u;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+        exclusive += part;
+        if (first < 32u) break;
+        hi -= 32;
+      }
+      if (lane == 0) scan_status_store(&status[chunk], (2ull << 32) | (exclusive + total));
+    }
+    if (lane == 0) {
+      s_prefix = exclusive;
+      if (chunk == nchunks - 1 && total_dev) *total_dev = (unsigned long long)exclusive + total;
+    }
+  }
+  __syncthreads();
+  if (s_fail) return;
+  uint32_t run = s_prefix + in_chunk;
+#pragma unroll
+  for (uint32_t i = 0; i < SCAN_ITEMS; ++i) {
+    if (kInclusive) run += x[i];
+    if (base + i < count) data[base + i] = run;
+    if (!kInclusive) run += x[i];
+  }
+}
+
 vs_status scan_impl(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev, bool inclusive) {
   if (count == 0) {
     if (total_dev) VS_CUDA(ctx, cudaMemsetAsync(total_dev, 0, 8, ctx->stream));
     return VS_OK;
   }
   const uint32_t chunks = div_up(count, SCAN_CHUNK);
-  VS_TRY(vs_ensure(ctx, ctx->scan_sums, (size_t)chunks * sizeof(uint32_t)));
-  uint32_t* sums = (uint32_t*)ctx->scan_sums.ptr;
-  scan_reduce_kernel<<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums); ++ctx->launches;
-  scan_sums_kernel<<<1, 1024, 0, ctx->stream>>>(sums, chunks, (unsigned long long*)total_dev); ++ctx->launches;
+  // one launch: status words (8 B per chunk) and a ticket, cleared first
+  const size_t bytes = (size_t)chunks * 8 + 16;
+  VS_TRY(vs_ensure(ctx, ctx->scan_sums, bytes));
+  unsigned long long* status = (unsigned long long*)ctx->scan_sums.ptr;
+  uint32_t* ticket = (uint32_t*)(status + chunks);
+  VS_CUDA(ctx, cudaMemsetAsync(status, 0, bytes, ctx->stream));
   if (inclusive)
-    scan_apply_kernel<true><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums);
+    scan_lookback_kernel<true><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, chunks, status, ticket,
+                                                                      (unsigned long long*)total_dev, ctx->d_err);
   else
-    scan_apply_kernel<false><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, sums);
+    scan_lookback_kernel<false><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, chunks, status, ticket,
+                                                                       (unsigned long long*)total_dev, ctx->d_err);
   ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "scan launch");
 }
