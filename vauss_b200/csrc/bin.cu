@@ -26,12 +26,6 @@ __global__ void depth_keys_kernel(const float* __restrict__ depths, uint32_t v, 
   }
 }
 
-__global__ void gather_counts_kernel(const uint32_t* __restrict__ order, const uint32_t* __restrict__ counts,
-                                     uint32_t v, uint32_t* __restrict__ out) {
-  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < v) out[i] = counts[order[i]];
-}
-
 // One thread per depth-sorted splat; large boxes are walked by the whole warp
 // (map_gaussians.rs:117-173).  Emission stops at the splat's counted budget
 // and pads any shortfall with the sentinel tile id T (map_gaussians.rs:76-113).
@@ -118,12 +112,28 @@ __global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v,
 // [0, 0) from the preceding memset.  Sentinel ids (>= T) are skipped.
 __global__ void tile_ranges_kernel(const uint32_t* __restrict__ tiles_sorted, uint32_t count, uint32_t T,
                                    uint2* __restrict__ ranges) {
-  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= count) return;
-  const uint32_t t = tiles_sorted[i];
-  if (t >= T) return;
-  if (i == 0 || tiles_sorted[i - 1] != t) ranges[t].x = i;
-  if (i + 1 == count || tiles_sorted[i + 1] != t) ranges[t].y = i + 1;
+  // four consecutive entries per thread (one 16-byte load) and their two
+  // neighbours; ~0u stands for "no entry" before the first and after the last
+  const uint32_t q = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t i0 = q * 4u;
+  if (i0 >= count) return;
+  uint32_t t[6];
+  t[0] = i0 ? tiles_sorted[i0 - 1] : ~0u;
+  if (i0 + 4u <= count) {
+    const uint4 v4 = reinterpret_cast<const uint4*>(tiles_sorted)[q];
+    t[1] = v4.x, t[2] = v4.y, t[3] = v4.z, t[4] = v4.w;
+  } else {
+#pragma unroll
+    for (uint32_t k = 0; k < 4; ++k) t[1 + k] = i0 + k < count ? tiles_sorted[i0 + k] : ~0u;
+  }
+  t[5] = i0 + 4u < count ? tiles_sorted[i0 + 4u] : ~0u;
+#pragma unroll
+  for (uint32_t k = 0; k < 4; ++k) {
+    const uint32_t i = i0 + k, cur = t[1 + k];
+    if (i >= count || cur >= T) continue;
+    if (t[k] != cur) ranges[cur].x = i;
+    if (t[k + 2] != cur) ranges[cur].y = i + 1;
+  }
 }
 
 }  // namespace
@@ -148,16 +158,16 @@ vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
   uint32_t* v0 = (uint32_t*)ctx->sort_vals.ptr;
   uint32_t* v1 = v0 + scratch / 4;
   const uint32_t blocks_v = div_up(v, BIN_BLOCK);
-  depth_keys_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const float*)f->depths.ptr, v, k0, v0); ++ctx->launches;
+  // the ids are sorted in the frame's depth_order (an even number of passes
+  // leaves the result there; otherwise it is copied back)
+  uint32_t* order = (uint32_t*)f->depth_order.ptr;
+  depth_keys_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const float*)f->depths.ptr, v, k0, order); ++ctx->launches;
   bool alt = false;
-  VS_TRY(radix_sort_pairs(ctx, k0, v0, k1, v1, v, 32, &alt));
-  uint32_t* order = alt ? v1 : v0;
-  VS_CUDA(ctx, cudaMemcpyAsync(f->depth_order.ptr, order, (size_t)v * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  VS_TRY(radix_sort_pairs(ctx, k0, order, k1, v1, v, 32, &alt));
+  if (alt) VS_CUDA(ctx, cudaMemcpyAsync(order, v1, (size_t)v * 4, cudaMemcpyDeviceToDevice, ctx->stream));
   // tile counts in depth order, inclusive scan -> emission offsets
   uint32_t* cum = alt ? k0 : k1;  // free half of the key scratch
-  gather_counts_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const uint32_t*)f->depth_order.ptr,
-                                                                 (const uint32_t*)f->tile_counts.ptr, v, cum); ++ctx->launches;
-  VS_TRY(scan_inclusive_u32(ctx, cum, v, nullptr));
+  VS_TRY(scan_gather_inclusive_u32(ctx, cum, (const uint32_t*)f->tile_counts.ptr, order, v));
   VS_TRY(vs_ensure(ctx, f->isect_tile, (size_t)(I + 1) * 4));
   VS_TRY(vs_ensure(ctx, f->isect_compact, (size_t)(I + 1) * 4));
   if (I == 0) return VS_OK;
@@ -175,7 +185,7 @@ vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
     VS_CUDA(ctx, cudaMemcpyAsync(tkeys, sk, (size_t)I * 4, cudaMemcpyDeviceToDevice, ctx->stream));
     VS_CUDA(ctx, cudaMemcpyAsync(tvals, sv, (size_t)I * 4, cudaMemcpyDeviceToDevice, ctx->stream));
   }
-  tile_ranges_kernel<<<div_up((uint32_t)I, 256), 256, 0, ctx->stream>>>(tkeys, (uint32_t)I, T,
+  tile_ranges_kernel<<<div_up(div_up((uint32_t)I, 4u), 256), 256, 0, ctx->stream>>>(tkeys, (uint32_t)I, T,
                                                                         (uint2*)f->tile_ranges.ptr); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "bin launch");
 }

@@ -249,11 +249,14 @@ __device__ __forceinline__ void scan_status_store(unsigned long long* p, unsigne
   r.store(v, cuda::memory_order_release);
 }
 
-template <bool kInclusive>
+// kGather: the values are src[idx[i]] instead of data[i] (data is only
+// written).
+template <bool kInclusive, bool kGather>
 __global__ void __launch_bounds__(SCAN_THREADS) scan_lookback_kernel(uint32_t* __restrict__ data, uint32_t count,
                                                                      uint32_t nchunks, unsigned long long* status,
                                                                      uint32_t* ticket, unsigned long long* total_dev,
-                                                                     uint32_t* err) {
+                                                                     uint32_t* err, const uint32_t* __restrict__ src,
+                                                                     const uint32_t* __restrict__ idx) {
   __shared__ uint32_t s_warp[32];
   __shared__ uint32_t s_chunk, s_prefix, s_fail;
   const uint32_t tid = threadIdx.x, lane = tid & 31u;
@@ -268,7 +271,7 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_lookback_kernel(uint32_t* _
   uint32_t sum = 0;
 #pragma unroll
   for (uint32_t i = 0; i < SCAN_ITEMS; ++i) {
-    x[i] = (base + i < count) ? data[base + i] : 0u;
+    x[i] = (base + i < count) ? (kGather ? src[idx[base + i]] : data[base + i]) : 0u;
     sum += x[i];
   }
   uint32_t total;
@@ -323,7 +326,8 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_lookback_kernel(uint32_t* _
   }
 }
 
-vs_status scan_impl(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev, bool inclusive) {
+vs_status scan_impl(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev, bool inclusive,
+                    const uint32_t* src = nullptr, const uint32_t* idx = nullptr) {
   if (count == 0) {
     if (total_dev) VS_CUDA(ctx, cudaMemsetAsync(total_dev, 0, 8, ctx->stream));
     return VS_OK;
@@ -335,12 +339,17 @@ vs_status scan_impl(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total
   unsigned long long* status = (unsigned long long*)ctx->scan_sums.ptr;
   uint32_t* ticket = (uint32_t*)(status + chunks);
   VS_CUDA(ctx, cudaMemsetAsync(status, 0, bytes, ctx->stream));
-  if (inclusive)
-    scan_lookback_kernel<true><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, chunks, status, ticket,
-                                                                      (unsigned long long*)total_dev, ctx->d_err);
+  unsigned long long* tot = (unsigned long long*)total_dev;
+  if (src)
+    scan_lookback_kernel<true, true><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, chunks, status, ticket,
+                                                                            tot, ctx->d_err, src, idx);
+  else if (inclusive)
+    scan_lookback_kernel<true, false><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, chunks, status, ticket,
+                                                                             tot, ctx->d_err, nullptr, nullptr);
   else
-    scan_lookback_kernel<false><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, chunks, status, ticket,
-                                                                       (unsigned long long*)total_dev, ctx->d_err);
+    scan_lookback_kernel<false, false><<<chunks, SCAN_THREADS, 0, ctx->stream>>>(data, count, chunks, status,
+                                                                              ticket, tot, ctx->d_err, nullptr,
+                                                                              nullptr);
   ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "scan launch");
 }
@@ -349,6 +358,12 @@ vs_status scan_impl(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total
 
 vs_status scan_inclusive_u32(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev) {
   return scan_impl(ctx, data, count, total_dev, true);
+}
+
+vs_status scan_gather_inclusive_u32(vs_ctx* ctx, uint32_t* out, const uint32_t* src, const uint32_t* idx,
+                                    uint32_t count) {
+  if (count == 0) return VS_OK;
+  return scan_impl(ctx, out, count, nullptr, true, src, idx);
 }
 
 vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,

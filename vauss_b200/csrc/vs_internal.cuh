@@ -65,6 +65,9 @@ vs_status launch_project(vs_ctx* ctx, vs_frame* f, const float* transforms, cons
 vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
                            uint32_t count, uint32_t key_bits, bool* result_in_alt);
 vs_status scan_inclusive_u32(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev);
+// out[i] = src[idx[0]] + ... + src[idx[i]]
+vs_status scan_gather_inclusive_u32(vs_ctx* ctx, uint32_t* out, const uint32_t* src, const uint32_t* idx,
+                                    uint32_t count);
 vs_status launch_bin(vs_ctx* ctx, vs_frame* f);
 vs_status launch_raster_fwd(vs_ctx* ctx, vs_frame* f, float* out_img, float* visible);
 vs_status launch_raster_packed(vs_ctx* ctx, vs_frame* f, uint32_t* out_rgba8);
