@@ -9,9 +9,11 @@
 //     blocks, one warp per block (crates/splat-train/src/quant_kernels.rs:
 //     597-714).
 // Q8 mode (the benchmark's optimizer: 8-bit m AND v, 256-value blocks):
-//   q8_kernel<false> -- single view: VJP + Adam on all 59 parameters +
+//   vjp_rows_kernel + q8_kernel<0> -- single view: the projection VJP of
+//     each visible splat into a compact row, then Adam on all 59 parameters +
 //     refine statistics + mean noise, one CTA per 256 splats;
-//   q8_kernel<true>  -- the same Adam from an all-reduced dense gradient;
+//   q8_kernel<1>  -- the same Adam from an all-reduced dense gradient;
+//   q8_kernel<2>  -- the same Adam for one rank's shard over peer memory;
 //   vjp_dense_kernel -- accumulates one view's dense gradient rows.
 #include "vjp.cuh"
 #include "vs_internal.cuh"
@@ -270,6 +272,53 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t n, 
   }
   d[width - 1] = (fresh ? 0.0f : d[width - 1]) + o.v_raw;
   refine[g] += clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
+}
+
+// ---- single-view VJP rows (the first half of the fused Q8 step) ----
+// One row of VJP_ROW floats per visible splat, in compact (projection) order:
+// 0-9 transforms gradient, 10 raw-opacity gradient, 11-13 colour gradient
+// (rasterizer rgb), 14-16 view direction, 17 refine weight, 18 = 1 when the
+// rasterizer row has a non-zero value (else the whole row is 0), 19 unused.
+// Running the VJP here, over the visible rows only and at full occupancy,
+// keeps its dependent gathers and its code out of the optimizer kernel.
+constexpr uint32_t VJP_ROW = 20;
+
+__global__ void __launch_bounds__(128) vjp_rows_kernel(Uniforms u, uint32_t v, const uint32_t* __restrict__ global_from_compact,
+                                                       const float* __restrict__ transforms, const float* __restrict__ sh,
+                                                       const float* __restrict__ raw_opac,
+                                                       const float* __restrict__ v_combined, float4* __restrict__ rows) {
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= v) return;
+  const float* rg = v_combined + (size_t)c * 10;
+  float rr[10];
+  bool active = false;
+#pragma unroll
+  for (int k = 0; k < 10; ++k) {
+    rr[k] = rg[k];
+    active = active || rr[k] != 0.0f;
+  }
+  float o[VJP_ROW];
+#pragma unroll
+  for (int k = 0; k < (int)VJP_ROW; ++k) o[k] = 0.0f;
+  if (active) {
+    const uint32_t g = global_from_compact[c];
+    float tt[10];
+#pragma unroll
+    for (int k = 0; k < 10; ++k) tt[k] = transforms[(size_t)g * 10 + k];
+    // the Q8 step takes no min_scale floor (its launcher rejects frames with one)
+    const VjpOut r = splat_vjp(tt, raw_opac[g], sh, nullptr, g, rr, u);
+    o[0] = r.v_mean.x; o[1] = r.v_mean.y; o[2] = r.v_mean.z;
+    o[3] = r.v_q.w; o[4] = r.v_q.x; o[5] = r.v_q.y; o[6] = r.v_q.z;
+    o[7] = r.v_scale.x; o[8] = r.v_scale.y; o[9] = r.v_scale.z;
+    o[10] = r.v_raw;
+    o[11] = rr[5]; o[12] = rr[6]; o[13] = rr[7];
+    o[14] = r.dir.x; o[15] = r.dir.y; o[16] = r.dir.z;
+    o[17] = clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
+    o[18] = 1.0f;
+  }
+  float4* d = rows + (size_t)c * (VJP_ROW / 4);
+#pragma unroll
+  for (int k = 0; k < (int)(VJP_ROW / 4); ++k) d[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
 }
 
 // ---- Q8 Adam ----
@@ -533,15 +582,15 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
   }
 }
 
-// MODE 0: single view, VJP fused (v_combined rows); MODE 1: dense gradient
+// MODE 0: single view, VJP rows of vjp_rows_kernel; MODE 1: dense gradient
 // rows `grads`; MODE 2: dense rows of every rank summed from peer memory, for
 // the shard of CTAs starting at pa.cta_begin, parameters stored to all
 // replicas.  `n` is one past the last splat this launch may touch.
 template <int MODE>
 __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
     Uniforms u, uint32_t n, float* __restrict__ transforms, float* __restrict__ sh, float* __restrict__ raw_opac,
-    const float* __restrict__ min_scale, const uint32_t* __restrict__ compact_from_global,
-    const float* __restrict__ v_combined, const float* __restrict__ grads, Q8T mt, Q8T msh, Q8T mo, Q8Args a,
+    const uint32_t* __restrict__ compact_from_global, const float4* __restrict__ vjp_rows,
+    const float* __restrict__ grads, Q8T mt, Q8T msh, Q8T mo, Q8Args a,
     const float* __restrict__ opacities, const float* __restrict__ visible, const float* __restrict__ max_radius,
     float* __restrict__ refine_norm, float* __restrict__ vis_count, float* __restrict__ max_screen, PeerArgs pa) {
   __shared__ float s_gt[Q8_SPLATS * 10];
@@ -550,8 +599,6 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
   __shared__ float s_bas[Q8_SPLATS * 16];
   __shared__ float s_noise[Q8_SPLATS * 3];
   __shared__ uint32_t s_vmask[MODE == 2 ? Q8_SPLATS : 1];
-  __shared__ uint32_t s_list[MODE == 0 ? Q8_SPLATS : 1];  // splats with a gradient row (MODE 0)
-  __shared__ uint32_t s_wact[Q8_WARPS];
   __shared__ float s_lr[10];
   constexpr bool kDense = MODE != 0;
 
@@ -566,10 +613,9 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
   const uint32_t width = 10u + wsh + 1u;
 
   // ---- phase 1: per-splat gradients into shared memory ----
-  // MODE 0 runs the VJP only for the splats with a non-zero gradient row,
-  // compacted first so that whole warps work on them (at a typical 60 %
-  // visibility every warp of 32 consecutive splats would otherwise carry the
-  // VJP with idle lanes); every value written is the same as per-thread code.
+  // MODE 0 reads the splat's VJP row (vjp_rows_kernel) and rebuilds its 16 SH
+  // bases from the stored view direction; a splat without a gradient row has
+  // zero gradients and bases.
   {
     const uint32_t g = base + tid;
     float gr[10];
@@ -577,7 +623,10 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
     for (int k = 0; k < 10; ++k) gr[k] = 0.0f;
     float go = 0.0f;
     float vis_g = 0.0f;  // views that saw the splat (MODE 1 and 2)
-    bool active = false;
+    float vc[3] = {0.0f, 0.0f, 0.0f};
+    float b[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) b[k] = 0.0f;
     if (g < n) {
       if (MODE == 2) {
         uint32_t vm = 0;
@@ -604,14 +653,16 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
         const uint32_t row = compact_from_global[g];
         float refine = 0.0f;
         if (row > 0) {
-          const float* rg = v_combined + (size_t)(row - 1) * 10;
-          float rr[10];
-#pragma unroll
-          for (int k = 0; k < 10; ++k) {
-            rr[k] = rg[k];
-            active = active || rr[k] != 0.0f;
+          const float4* r4 = vjp_rows + (size_t)(row - 1) * (VJP_ROW / 4);
+          const float4 x0 = r4[0], x1 = r4[1], x2 = r4[2], x3 = r4[3], x4 = r4[4];
+          if (x4.z != 0.0f) {
+            gr[0] = x0.x; gr[1] = x0.y; gr[2] = x0.z; gr[3] = x0.w;
+            gr[4] = x1.x; gr[5] = x1.y; gr[6] = x1.z; gr[7] = x1.w;
+            gr[8] = x2.x; gr[9] = x2.y; go = x2.z;
+            vc[0] = x2.w; vc[1] = x3.x; vc[2] = x3.y;
+            sh_basis_all(x3.z, x3.w, x4.x, b);
+            refine = x4.y;
           }
-          if (active) refine = clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
         }
         if (refine_norm) refine_norm[g] = fmaxf(refine_norm[g], refine);
         if (vis_count) vis_count[g] += visible[g];
@@ -621,50 +672,12 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
 #pragma unroll
     for (int k = 0; k < 10; ++k) s_gt[tid * 10 + k] = gr[k];
     s_go[tid] = go;
-    s_vc[tid * 3 + 0] = 0.0f;
-    s_vc[tid * 3 + 1] = 0.0f;
-    s_vc[tid * 3 + 2] = 0.0f;
+    s_vc[tid * 3 + 0] = vc[0];
+    s_vc[tid * 3 + 1] = vc[1];
+    s_vc[tid * 3 + 2] = vc[2];
     if (!kDense) {
-      // a splat without gradient has colour gradient 0: its bases only have
-      // to be finite
 #pragma unroll
-      for (int k = 0; k < 16; ++k) s_bas[tid * 16 + k] = 0.0f;
-      const uint32_t bal = __ballot_sync(0xffffffffu, active);
-      if (lane == 0) s_wact[warp] = __popc(bal);
-      __syncthreads();
-      uint32_t off = 0, total = 0;
-#pragma unroll
-      for (uint32_t w = 0; w < Q8_WARPS; ++w) {
-        const uint32_t c = s_wact[w];
-        off += w < warp ? c : 0u;
-        total += c;
-      }
-      if (active) s_list[off + __popc(bal & ((1u << lane) - 1u))] = tid;
-      __syncthreads();
-      for (uint32_t k = tid; k < total; k += Q8_SPLATS) {
-        const uint32_t t = s_list[k];
-        const uint32_t gg = base + t;
-        const float* rg = v_combined + (size_t)(compact_from_global[gg] - 1) * 10;
-        float rr[10], tt[10];
-#pragma unroll
-        for (int j = 0; j < 10; ++j) rr[j] = rg[j];
-#pragma unroll
-        for (int j = 0; j < 10; ++j) tt[j] = transforms[(size_t)gg * 10 + j];
-        const VjpOut o = splat_vjp(tt, raw_opac[gg], sh, min_scale, gg, rr, u);
-        float* dst = s_gt + t * 10;
-        dst[0] = o.v_mean.x; dst[1] = o.v_mean.y; dst[2] = o.v_mean.z;
-        dst[3] = o.v_q.w; dst[4] = o.v_q.x; dst[5] = o.v_q.y; dst[6] = o.v_q.z;
-        dst[7] = o.v_scale.x; dst[8] = o.v_scale.y; dst[9] = o.v_scale.z;
-        s_go[t] = o.v_raw;
-        s_vc[t * 3 + 0] = rr[5];
-        s_vc[t * 3 + 1] = rr[6];
-        s_vc[t * 3 + 2] = rr[7];
-        float b[16];
-        sh_basis_all(o.dir.x, o.dir.y, o.dir.z, b);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) s_bas[t * 16 + j] = b[j];
-      }
-      __syncthreads();
+      for (int k = 0; k < 16; ++k) s_bas[tid * 16 + k] = b[k];
     }
     // opacity regulariser and mean noise, one splat per thread again
     float nx = 0.0f, ny = 0.0f, nz = 0.0f;
@@ -829,6 +842,8 @@ VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* c
   if (!frame || !frame->rendered || !cfg || !q8) return vs_fail(ctx, VS_ERR_INVALID, "step_q8: missing frame/config");
   if (num_splats != frame->n) return vs_fail(ctx, VS_ERR_INVALID, "step_q8: %u splats, frame has %u", num_splats, frame->n);
   if (cfg->sh_half) return vs_fail(ctx, VS_ERR_UNSUPPORTED, "step_q8: SH coefficients must be f32");
+  if (frame->u.has_min_scale)
+    return vs_fail(ctx, VS_ERR_UNSUPPORTED, "step_q8: frames rendered with a min_scale floor need the dense path");
   if (!transforms || !sh_coeffs || !raw_opacities || (frame->v && !v_combined) || !q8_valid(mom_t) ||
       !q8_valid(mom_sh) || !q8_valid(mom_o))
     return vs_fail(ctx, VS_ERR_INVALID, "step_q8: null buffer");
@@ -840,10 +855,17 @@ VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* c
   if (count_sh >= 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "step_q8: %llu SH values exceed u32 indexing", (unsigned long long)count_sh);
   if (num_splats == 0) return VS_OK;
   const Q8Args a = to_args(*q8);
+  // the VJP rows live in the ctx's scratch until the optimizer kernel has read them
+  VS_TRY(vs_ensure(ctx, ctx->vjp_rows, ((size_t)frame->v + 1) * VJP_ROW * 4));
+  if (frame->v > 0) {
+    vjp_rows_kernel<<<vs::div_up(frame->v, 128), 128, 0, ctx->stream>>>(
+        frame->u, frame->v, (const uint32_t*)frame->global_from_compact.ptr, transforms, sh_coeffs, raw_opacities,
+        v_combined, (float4*)ctx->vjp_rows.ptr); ++ctx->launches;
+  }
   q8_kernel<0><<<vs::div_up(num_splats, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
-      frame->u, num_splats, transforms, sh_coeffs, raw_opacities, nullptr,
-      (const uint32_t*)frame->compact_from_global.ptr, v_combined, nullptr, to_q8(mom_t), to_q8(mom_sh), to_q8(mom_o),
-      a, (const float*)frame->opacities.ptr, visible, (const float*)frame->max_radius.ptr, refine_norm, vis_count,
+      frame->u, num_splats, transforms, sh_coeffs, raw_opacities, (const uint32_t*)frame->compact_from_global.ptr,
+      (const float4*)ctx->vjp_rows.ptr, nullptr, to_q8(mom_t), to_q8(mom_sh), to_q8(mom_o), a,
+      (const float*)frame->opacities.ptr, visible, (const float*)frame->max_radius.ptr, refine_norm, vis_count,
       max_screen, single_rank()); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "step_q8 launch");
 }
@@ -882,7 +904,7 @@ VS_API vs_status vs_adam_q8_dense(vs_ctx* ctx, uint32_t num_splats, int32_t sh_d
   u.sh_degree = sh_degree;
   const Q8Args a = to_args(*q8);
   q8_kernel<1><<<vs::div_up(num_splats, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
-      u, num_splats, transforms, sh_coeffs, raw_opacities, nullptr, nullptr, nullptr, grads, to_q8(mom_t),
+      u, num_splats, transforms, sh_coeffs, raw_opacities, nullptr, nullptr, grads, to_q8(mom_t),
       to_q8(mom_sh), to_q8(mom_o), a, opacities, visible, nullptr, nullptr, nullptr, nullptr, single_rank());
   ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "adam_q8_dense launch");
@@ -924,7 +946,7 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
   const Q8Args a = to_args(*q8);
   const uint32_t me = peers->rank;
   q8_kernel<2><<<vs::div_up(splat_end - splat_begin, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
-      u, splat_end, pa.t[me], pa.sh[me], pa.o[me], nullptr, nullptr, nullptr, nullptr, to_q8(mom_t), to_q8(mom_sh),
+      u, splat_end, pa.t[me], pa.sh[me], pa.o[me], nullptr, nullptr, nullptr, to_q8(mom_t), to_q8(mom_sh),
       to_q8(mom_o), a, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, pa);
   ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "adam_q8_peer launch");

@@ -26,6 +26,7 @@ struct vs_ctx {
   // scratch shared by calls on this ctx (stream-ordered reuse)
   DevBuf sort_keys, sort_vals, sort_hist, scan_sums, misc;
   DevBuf io_stage;  // checkpoint I/O chunks (two halves)
+  DevBuf vjp_rows;  // per-visible-splat VJP rows of the single-view Q8 step
 };
 
 struct vs_frame {
