@@ -1292,9 +1292,10 @@ OR_API int or_vjp_dense(const Camera* cam, const RenderCfg* cfg, uint32_t n, con
 //    step ^ salt); value index i takes the bytes 2 (i % 2) and 2 (i % 2) + 1
 //    of h as b_m, b_v and uniforms u = (b + 1/2) / 256:
 //    m code = floor(m/scale + u1), r code = floor(r/scale + u2);
-//  * scales enter as reciprocals: code = floor(m * (1/scale) + u);
-//  * step = (m1 inv1) * (1 / d), d = max(sqrt(v1) sqrt(inv2) + eps,
-//    |m1 inv1| / 8), with 1 / d taken as 0 for d >= 2^126: the normalized
+//  * scales enter as reciprocals: code = floor(fma(m, 1/scale, u));
+//  * m1 = fma(g, 1 - b1, m0 b1), v1 = fma(g g, 1 - b2, r0 r0 b2),
+//    p1 = fma(-(m1 inv1) (1 / d), lr, p0), d = max(fma(sqrt(v1), sqrt(inv2),
+//    eps), |m1 inv1| / 8), with 1 / d taken as 0 for d >= 2^126: the normalized
 //    update is bounded by 8, the bound the reference's packed geometry codec
 //    imposes (src/bwd/kernels/geo_moments.rs:186,192).
 // grads [count] (dense); lr per column: lr_col[index % row_width] * lr.
@@ -1318,13 +1319,13 @@ OR_API int or_adam_q8(size_t count, uint32_t row_width, float* params, const flo
       const float g = grads[row * grad_stride + grad_offset + col];
       const float m0 = ((float)m_codes[i] - 128.0f) * ms;
       const float r0 = (float)v_codes[i] * vsc;
-      const float m = m0 * b1 + g * (1.0f - b1);
-      const float v = r0 * r0 * b2 + g * g * (1.0f - b2);
+      const float m = fmaf(g, 1.0f - b1, m0 * b1);
+      const float v = fmaf(g * g, 1.0f - b2, r0 * r0 * b2);
       const float r = sqrtf(v);
       const float mh = m * inv1;
-      const float denom = fmaxf(r * sqrt_inv2 + eps, fabsf(mh) * 0.125f);
+      const float denom = fmaxf(fmaf(r, sqrt_inv2, eps), fabsf(mh) * 0.125f);
       const float inv_d = denom < 8.5070592e37f ? 1.0f / denom : 0.0f;
-      params[i] = params[i] - (mh * inv_d) * (lr_col[col] * lr);
+      params[i] = fmaf(-(mh * inv_d), lr_col[col] * lr, params[i]);
       m1[j] = m;
       r1[j] = r;
     }
@@ -1343,8 +1344,8 @@ OR_API int or_adam_q8(size_t count, uint32_t row_width, float* params, const flo
       const float u1 = ((float)(hb & 0xffu) + 0.5f) * (1.0f / 256.0f);
       const float u2 = ((float)((hb >> 8) & 0xffu) + 0.5f) * (1.0f / 256.0f);
       float qm = 0.0f, qr = 0.0f;
-      if (nms > 0.0f) qm = clampf(floorf(m1[j] * inv_ms + u1), -127.0f, 127.0f);
-      if (nvs > 0.0f) qr = clampf(floorf(r1[j] * inv_vs + u2), 0.0f, 255.0f);
+      if (nms > 0.0f) qm = clampf(floorf(fmaf(m1[j], inv_ms, u1)), -127.0f, 127.0f);
+      if (nvs > 0.0f) qr = clampf(floorf(fmaf(r1[j], inv_vs, u2)), 0.0f, 255.0f);
       m_codes[i] = (uint8_t)((int32_t)qm + 128);
       v_codes[i] = (uint8_t)qr;
     }

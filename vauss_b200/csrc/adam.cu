@@ -498,14 +498,14 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
     const float m0 = (__uint_as_float(0x4B000000u | mb) - 8388736.0f) * ms;  // (b - 128) * scale
     const float r0 = (__uint_as_float(0x4B000000u | vb) - 8388608.0f) * vsc;
     const float gg = g[k];
-    const float m = m0 * a.b1 + gg * (1.0f - a.b1);
-    const float v = r0 * r0 * a.b2 + gg * gg * (1.0f - a.b2);
+    const float m = fmaf(gg, 1.0f - a.b1, m0 * a.b1);
+    const float v = fmaf(gg * gg, 1.0f - a.b2, r0 * r0 * a.b2);
     const float r = sqrt_rn(v);
     const float mh = m * a.inv1;
-    const float denom = fmaxf(r * a.sqrt_inv2 + a.eps, fabsf(mh) * 0.125f);
+    const float denom = fmaxf(fmaf(r, a.sqrt_inv2, a.eps), fabsf(mh) * 0.125f);
     // mh / denom as mh times the correctly rounded reciprocal (0 from 2^126 on)
     const float inv_d = denom < 8.5070592e37f ? rcp_rn(denom) : 0.0f;
-    float pn = pv[k] - (mh * inv_d) * lr[k];
+    float pn = fmaf(-(mh * inv_d), lr[k], pv[k]);
     if (KIND == 0) pn = pn + nz[k];
     pv[k] = pn;
     m1[k] = m;
@@ -546,10 +546,10 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
       // (NaN clamps to lo either way); floor of |y| < 2^22 is the low
       // mantissa of y + 1.5 2^23 rounded toward -inf.
       const uint32_t qm = nms > 0.0f
-          ? __float_as_uint(__fadd_rd(clampf(m1[k] * inv_ms + u1, -127.0f, 127.0f), 12582912.0f)) - 0x4B400000u + 128u
+          ? __float_as_uint(__fadd_rd(clampf(fmaf(m1[k], inv_ms, u1), -127.0f, 127.0f), 12582912.0f)) - 0x4B400000u + 128u
           : 128u;
       const uint32_t qr = nvs > 0.0f
-          ? __float_as_uint(__fadd_rd(clampf(r1[k] * inv_vs + u2, 0.0f, 255.0f), 12582912.0f)) - 0x4B400000u
+          ? __float_as_uint(__fadd_rd(clampf(fmaf(r1[k], inv_vs, u2), 0.0f, 255.0f), 12582912.0f)) - 0x4B400000u
           : 0u;
       mo |= qm << (8 * e);
       vo |= qr << (8 * e);

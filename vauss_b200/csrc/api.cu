@@ -151,7 +151,7 @@ VS_API void vs_frame_destroy(vs_frame* f) {
   if (!f) return;
   vs_ctx* ctx = f->ctx;
   cudaSetDevice(ctx->device);
-  DevBuf* bufs[] = {&f->compact_from_global, &f->global_from_compact, &f->depths, &f->tile_counts,
+  DevBuf* bufs[] = {&f->compact_from_global, &f->global_from_compact, &f->depths, &f->tile_counts, &f->tile_masks,
                     &f->projected, &f->depth_order, &f->isect_tile, &f->isect_compact, &f->tile_ranges,
                     &f->tile_used_end, &f->opacities, &f->max_radius, &f->lookback, &f->counters};
   for (DevBuf* b : bufs) vs_release(ctx, *b);
@@ -221,6 +221,7 @@ VS_API vs_status vs_render_project(vs_ctx* ctx, vs_frame* f, const vs_camera* ca
   VS_TRY(vs_ensure(ctx, f->global_from_compact, n1 * 4));
   VS_TRY(vs_ensure(ctx, f->depths, n1 * 4));
   VS_TRY(vs_ensure(ctx, f->tile_counts, n1 * 4));
+  VS_TRY(vs_ensure(ctx, f->tile_masks, n1 * 8));
   VS_TRY(vs_ensure(ctx, f->projected, n1 * vs::PROJ_F4 * 16));
   VS_TRY(vs_ensure(ctx, f->opacities, n1 * 4));
   VS_TRY(vs_ensure(ctx, f->max_radius, n1 * 4));

@@ -26,11 +26,18 @@ __global__ void depth_keys_kernel(const float* __restrict__ depths, uint32_t v, 
   }
 }
 
-// One thread per depth-sorted splat; large boxes are walked by the whole warp
-// (map_gaussians.rs:117-173).  Emission stops at the splat's counted budget
-// and pads any shortfall with the sentinel tile id T (map_gaussians.rs:76-113).
+// One thread per depth-sorted splat takes its box's hit mask from projection
+// (small boxes, up to BIG_BOX tiles); the warp then writes the contiguous
+// output range of its 32 splats together, lane l taking positions p = p0 + l:
+// the owning splat is found by a binary search over the lanes' start offsets
+// and the entry is the (p - start)-th hit of its mask, so every store
+// instruction covers 32 consecutive entries.  Large boxes are walked by the
+// whole warp afterwards (map_gaussians.rs:117-173).  Emission stops at the
+// splat's counted budget and pads any shortfall with the sentinel tile id T
+// (map_gaussians.rs:76-113).
 __global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v, const uint32_t* __restrict__ order,
                                                          const uint32_t* __restrict__ cum,
+                                                         const uint2* __restrict__ tile_masks,
                                                          const float4* __restrict__ projected,
                                                          uint32_t* __restrict__ tile_keys,
                                                          uint32_t* __restrict__ compact_vals) {
@@ -42,10 +49,15 @@ __global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v,
   float px = 0.f, py = 0.f, pt = 0.f;
   S2 conic = {0.f, 0.f, 0.f};
   TileBox b = {0, 0, 0, 0};
+  uint2 e = make_uint2(0u, 0u);  // small box: hit mask | width << 16; large: bit 31
   if (active) {
     c = order[i];
     start = i ? cum[i - 1] : 0u;
     budget = cum[i] - start;
+    e = tile_masks[c];
+  }
+  const bool big = active && (e.x & 0x80000000u);
+  if (big) {
     const float4 r0 = projected[(size_t)c * PROJ_F4];
     const float4 r1 = projected[(size_t)c * PROJ_F4 + 1];
     px = r0.x; py = r0.y;
@@ -57,22 +69,40 @@ __global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v,
     bw = b.x1 - b.x0;
     nb = (b.y1 - b.y0) * bw;
   }
-  if (active && nb <= BIG_BOX) {
-    uint32_t slot = 0;
-    for (uint32_t k = 0; k < nb && slot < budget; ++k) {
-      const uint32_t tx = k % bw + b.x0, ty = k / bw + b.y0;
-      if (tile_hit(tx, ty, px, py, conic, pt)) {
-        tile_keys[start + slot] = tx + ty * u.tbw;
-        compact_vals[start + slot] = c;
-        ++slot;
+  {
+    // [s0, s1): the warp's output range; inactive lanes start at s1
+    const uint32_t s1 = __reduce_max_sync(0xffffffffu, active ? start + budget : 0u);
+    const uint32_t my_start = active ? start : s1;
+    const uint32_t s0 = __shfl_sync(0xffffffffu, my_start, 0);
+    const uint32_t info0 = e.x, info1 = e.y;
+    for (uint32_t p0 = s0; p0 < s1; p0 += 32) {
+      const uint32_t p = p0 + lane;
+      uint32_t owner = 0, ostart = s0;
+#pragma unroll
+      for (uint32_t step = 16; step > 0; step >>= 1) {
+        const uint32_t cand = owner + step;
+        const uint32_t sc = __shfl_sync(0xffffffffu, my_start, cand);
+        if (sc <= p) {
+          owner = cand;
+          ostart = sc;
+        }
+      }
+      const uint32_t oi0 = __shfl_sync(0xffffffffu, info0, owner);
+      const uint32_t oi1 = __shfl_sync(0xffffffffu, info1, owner);
+      const uint32_t oc = __shfl_sync(0xffffffffu, c, owner);
+      if (p < s1 && !(oi0 & 0x80000000u)) {
+        const uint32_t k = p - ostart, m = oi0 & 0xffffu;
+        uint32_t key = T;
+        if (k < (uint32_t)__popc(m)) {
+          const uint32_t bit = __fns(m, 0u, (int)k + 1), obw = (oi0 >> 16) & 0x1fu;
+          key = (bit % obw + (oi1 & 0xffffu)) + (bit / obw + (oi1 >> 16)) * u.tbw;
+        }
+        tile_keys[p] = key;
+        compact_vals[p] = oc;
       }
     }
-    for (; slot < budget; ++slot) {
-      tile_keys[start + slot] = T;
-      compact_vals[start + slot] = c;
-    }
   }
-  uint32_t pending = __ballot_sync(0xffffffffu, active && nb > BIG_BOX);
+  uint32_t pending = __ballot_sync(0xffffffffu, big);
   while (pending) {
     const int leader = __ffs(pending) - 1;
     const float lx = __shfl_sync(0xffffffffu, px, leader);
@@ -175,7 +205,8 @@ vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
   uint32_t* tkeys = (uint32_t*)f->isect_tile.ptr;
   uint32_t* tvals = (uint32_t*)f->isect_compact.ptr;
   emit_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>(f->u, v, (const uint32_t*)f->depth_order.ptr, cum,
-                                                        (const float4*)f->projected.ptr, tkeys, tvals); ++ctx->launches;
+                                                        (const uint2*)f->tile_masks.ptr, (const float4*)f->projected.ptr,
+                                                        tkeys, tvals); ++ctx->launches;
   VS_CUDA(ctx, cudaGetLastError());
   const uint32_t tile_bits = 32u - (uint32_t)__builtin_clz(T | 1u);
   uint32_t* sk = (uint32_t*)ctx->sort_keys.ptr;

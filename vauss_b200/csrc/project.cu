@@ -76,15 +76,16 @@ __device__ bool project_one(const float* __restrict__ t, float raw_opac, const f
   return true;
 }
 
-__device__ uint32_t count_box(const TileBox& b, float mx, float my, S2 c, float pt) {
+// Bit i of the result: box tile i (row-major in the box) is hit.
+__device__ uint32_t hit_mask_box(const TileBox& b, float mx, float my, S2 c, float pt) {
   const uint32_t bw = b.x1 - b.x0;
   const uint32_t nb = (b.y1 - b.y0) * bw;
-  uint32_t hits = 0;
+  uint32_t mask = 0;
   for (uint32_t i = 0; i < nb; ++i) {
     const uint32_t tx = i % bw + b.x0, ty = i / bw + b.y0;
-    hits += tile_hit(tx, ty, mx, my, c, pt) ? 1u : 0u;
+    if (tile_hit(tx, ty, mx, my, c, pt)) mask |= 1u << i;
   }
-  return hits;
+  return mask;
 }
 
 // SH colour with the +0.5 offset, NaN scrub and clamp
@@ -168,7 +169,8 @@ __global__ void __launch_bounds__(PROJ_BLOCK, 4) project_kernel(
     Uniforms u, uint32_t n, const float* __restrict__ transforms, const void* __restrict__ sh,
     const float* __restrict__ raw_opac, const float* __restrict__ min_scale, uint32_t* __restrict__ compact_from_global,
     float* __restrict__ opacities, float* __restrict__ max_radius, uint32_t* __restrict__ global_from_compact,
-    float* __restrict__ depths, uint32_t* __restrict__ tile_counts, float4* __restrict__ projected,
+    float* __restrict__ depths, uint32_t* __restrict__ tile_counts, uint2* __restrict__ tile_masks,
+    float4* __restrict__ projected,
     unsigned long long* lookback, uint32_t* counters /* [0] ticket, [1] visible total */,
     unsigned long long* isect_total, uint32_t* err) {
   __shared__ uint32_t s_bid;
@@ -224,7 +226,8 @@ __global__ void __launch_bounds__(PROJ_BLOCK, 4) project_kernel(
   // whole warp, one splat at a time (project_forward.rs:198-247).
   uint32_t nb = 0;
   if (visible) nb = (o.box.y1 - o.box.y0) * (o.box.x1 - o.box.x0);
-  uint32_t hits = (visible && nb <= BIG_BOX) ? count_box(o.box, o.xy_x, o.xy_y, o.conic, o.pt) : 0u;
+  const uint32_t mask = (visible && nb <= BIG_BOX) ? hit_mask_box(o.box, o.xy_x, o.xy_y, o.conic, o.pt) : 0u;
+  uint32_t hits = __popc(mask);
   uint32_t pending = __ballot_sync(0xffffffffu, visible && nb > BIG_BOX);
   while (pending) {
     const int leader = __ffs(pending) - 1;
@@ -301,6 +304,9 @@ __global__ void __launch_bounds__(PROJ_BLOCK, 4) project_kernel(
   global_from_compact[c] = g;
   depths[c] = o.depth;
   tile_counts[c] = hits;
+  // the emission's input: the hit mask of a small box, or a flag for a large one
+  tile_masks[c] = make_uint2(nb <= BIG_BOX ? mask | ((o.box.x1 - o.box.x0) << 16) : 0x80000000u,
+                             o.box.x0 | (o.box.y0 << 16));
   float4* row = projected + (size_t)c * PROJ_F4;
   row[0] = make_float4(o.xy_x, o.xy_y, o.conic.c00, o.conic.c01);
   row[1] = make_float4(o.conic.c11, o.opac, col.x, col.y);
@@ -323,7 +329,7 @@ vs_status launch_project(vs_ctx* ctx, vs_frame* f, const float* transforms, cons
   project_kernel<<<blocks, PROJ_BLOCK, 0, ctx->stream>>>(
       f->u, n, transforms, sh, raw_opac, min_scale, (uint32_t*)f->compact_from_global.ptr, (float*)f->opacities.ptr,
       (float*)f->max_radius.ptr, (uint32_t*)f->global_from_compact.ptr, (float*)f->depths.ptr,
-      (uint32_t*)f->tile_counts.ptr, (float4*)f->projected.ptr, (unsigned long long*)f->lookback.ptr, counters,
+      (uint32_t*)f->tile_counts.ptr, (uint2*)f->tile_masks.ptr, (float4*)f->projected.ptr, (unsigned long long*)f->lookback.ptr, counters,
       isect_total, ctx->d_err); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "project_kernel launch");
 }

@@ -36,7 +36,7 @@ struct vs_frame {
   uint32_t n = 0, v = 0, T = 0;
   uint64_t I = 0;
   bool projected_ok = false, binned = false, rendered = false;
-  DevBuf compact_from_global, global_from_compact, depths, tile_counts, projected, depth_order;
+  DevBuf compact_from_global, global_from_compact, depths, tile_counts, tile_masks, projected, depth_order;
   DevBuf isect_tile, isect_compact, tile_ranges, tile_used_end, opacities, max_radius;
   DevBuf lookback, counters;  // projection compaction state
 };
