@@ -15,7 +15,9 @@
 //
 // The replay evaluates exactly the forward's exponent, alpha and transmittance
 // sequence (raster_sigma, vs_expf, the same comparisons), so every
-// accept/terminate decision matches the forward pass bit for bit.
+// accept/terminate decision matches the forward pass bit for bit.  The
+// gradient sums, whose order already differs from the oracle's (shuffles and
+// atomics), fuse each term's last multiply into the accumulation.
 #include "vs_internal.cuh"
 
 namespace {
@@ -26,6 +28,12 @@ constexpr uint32_t RB_THREADS = 128;
 constexpr uint32_t RB_WARPS = RB_THREADS / 32;
 constexpr uint32_t RB_BATCH = 128;
 constexpr uint32_t NG = 10;
+
+__device__ __forceinline__ float sqrt_approx(float x) {
+  float y;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // Butterfly reduce-scatter of the NG = 10 gradient components over a warp in
 // 12 shuffles (groups of 5 | 3+2 | 2+1 | 1+1 | pair sum).  Afterwards the even
@@ -186,12 +194,12 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
             continue;
           }
           contributes = true;
-          // gradients: the oracle's per-term float steps (the same fmas), summed
-          // in another order
+          // gradients: the oracle's per-term float steps (the same fmas), each
+          // term's last product fused into its accumulation
           const float vis = alpha * st[k];
-          if (bb.z >= 0.0f) g[5] += vis * vr[k];
-          if (bb.w >= 0.0f) g[6] += vis * vg[k];
-          if (cc.x >= 0.0f) g[7] += vis * vb[k];
+          if (bb.z >= 0.0f) g[5] = fmaf(vis, vr[k], g[5]);
+          if (bb.w >= 0.0f) g[6] = fmaf(vis, vg[k], g[6]);
+          if (cc.x >= 0.0f) g[7] = fmaf(vis, vb[k], g[7]);
           const float ra = rcp_rn(1.0f - alpha);  // 1 - alpha in [1e-3, 1]
           const float dot =
               fmaf(fmaf(st[k], cr, -sr[k]), vr[k], fmaf(fmaf(st[k], cg, -sg[k]), vg[k], fmaf(st[k], cb, -sb[k]) * vb[k])) * ra;
@@ -200,14 +208,17 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
           const float vxx = v_sigma * fmaf(c00, dx, c01 * dy);
           const float vxy = v_sigma * fmaf(c01, dx, c11 * dy);
           if (opac * gauss <= 0.999f) {
-            g[2] += 0.5f * v_sigma * dx * dx;
-            g[3] += v_sigma * dx * dy;
-            g[4] += 0.5f * v_sigma * dy * dy;
+            const float hv = 0.5f * v_sigma;
+            g[2] = fmaf(hv * dx, dx, g[2]);
+            g[3] = fmaf(v_sigma * dx, dy, g[3]);
+            g[4] = fmaf(hv * dy, dy, g[4]);
             g[0] += vxx;
             g[1] += vxy;
-            g[8] += v_alpha * gauss;
+            g[8] = fmaf(v_alpha, gauss, g[8]);
             const float ax = vxx * img_w, ay = vxy * img_h;
-            g[9] += sqrt_rn(fmaf(ax, ax, ay * ay)) * rs[k];
+            // the refine weight is a densification statistic: the hardware
+            // square root (a few ulp) is far inside its tolerance
+            g[9] = fmaf(sqrt_approx(fmaf(ax, ax, ay * ay)), rs[k], g[9]);
           }
           sr[k] = fmaf(-vis, cr, sr[k]);
           sg[k] = fmaf(-vis, cg, sg[k]);
