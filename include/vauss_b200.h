@@ -213,7 +213,9 @@ typedef struct vs_q8_cfg {
  * (blocks of 256, fp32 absmax scales, stochastic rounding) on transforms,
  * sh_coeffs (f32) and raw_opacities, plus the refine statistics
  * (refine_norm = max, vis_count += visible, max_screen = max) and the
- * low-opacity mean noise, in one kernel.  stats pointers may be NULL. */
+ * low-opacity mean noise: two kernels (the VJP of the visible splats into
+ * ctx scratch, then the optimizer).  stats pointers may be NULL.  Frames
+ * rendered with a min_scale floor are rejected (VS_ERR_UNSUPPORTED). */
 VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
                             float* transforms, float* sh_coeffs, float* raw_opacities, const float* v_combined,
                             vs_q8_tensor mom_t, vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8,

@@ -219,16 +219,20 @@ __global__ void __launch_bounds__(128) sh_step_kernel(uint32_t count, uint32_t r
 }
 
 // ---- dense VJP ----
-__global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t n, const float* __restrict__ transforms,
+// One thread per visible (projected) splat, in compact order; splats that
+// projection culled have no rasterizer row and no `visible` mark, so their
+// gradient rows, refine sums and view counts stay as they are.
+__global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, const float* __restrict__ transforms,
                                                         const void* __restrict__ sh, const float* __restrict__ raw_opac,
                                                         const float* __restrict__ min_scale,
-                                                        const uint32_t* __restrict__ compact_from_global,
+                                                        const uint32_t* __restrict__ global_from_compact,
                                                         const float* __restrict__ v_combined,
                                                         float* __restrict__ grads, float* __restrict__ refine,
                                                         const float* __restrict__ visible,
                                                         float* __restrict__ vis_accum) {
-  const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
-  if (g >= n) return;
+  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= v) return;
+  const uint32_t g = global_from_compact[c];
   // A row not seen before in this step (vis_accum was 0) is overwritten, so
   // readers gated on vis_accum never see an earlier step's values.
   bool fresh = false;
@@ -237,11 +241,9 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t n, 
     vis_accum[g] = seen + visible[g];
     fresh = seen == 0.0f && visible[g] > 0.0f;
   }
-  const uint32_t row = compact_from_global[g];
-  if (row == 0) return;
   const int nc = (u.sh_degree + 1) * (u.sh_degree + 1);
   const int width = 10 + 3 * nc + 1;
-  const float* rg = v_combined + (size_t)(row - 1) * 10;
+  const float* rg = v_combined + (size_t)c * 10;
   float rr[10];
   bool any = false;
 #pragma unroll
@@ -268,7 +270,7 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t n, 
   sh_basis_all(o.dir.x, o.dir.y, o.dir.z, b);
   for (int k = 0; k < nc; ++k) {
 #pragma unroll
-    for (int c = 0; c < 3; ++c) d[10 + k * 3 + c] = (fresh ? 0.0f : d[10 + k * 3 + c]) + rr[5 + c] * b[k];
+    for (int cc = 0; cc < 3; ++cc) d[10 + k * 3 + cc] = (fresh ? 0.0f : d[10 + k * 3 + cc]) + rr[5 + cc] * b[k];
   }
   d[width - 1] = (fresh ? 0.0f : d[width - 1]) + o.v_raw;
   refine[g] += clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
@@ -883,8 +885,9 @@ VS_API vs_status vs_vjp_dense(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg*
   if (num_splats == 0) return VS_OK;
   vs::Uniforms u = frame->u;
   u.sh_half = cfg->sh_half;
-  vjp_dense_kernel<<<vs::div_up(num_splats, 256), 256, 0, ctx->stream>>>(
-      u, num_splats, transforms, sh_coeffs, raw_opacities, min_scale, (const uint32_t*)frame->compact_from_global.ptr,
+  if (frame->v == 0) return VS_OK;
+  vjp_dense_kernel<<<vs::div_up(frame->v, 256), 256, 0, ctx->stream>>>(
+      u, frame->v, transforms, sh_coeffs, raw_opacities, min_scale, (const uint32_t*)frame->global_from_compact.ptr,
       v_combined, grads, refine, visible, vis_accum); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "vjp_dense launch");
 }

@@ -15,7 +15,6 @@ namespace {
 using namespace vs;
 
 constexpr uint32_t BIN_BLOCK = 256;
-constexpr uint32_t BIG_BOX = 16;
 
 __global__ void depth_keys_kernel(const float* __restrict__ depths, uint32_t v, uint32_t* __restrict__ keys,
                                   uint32_t* __restrict__ ids) {
@@ -27,7 +26,7 @@ __global__ void depth_keys_kernel(const float* __restrict__ depths, uint32_t v, 
 }
 
 // One thread per depth-sorted splat takes its box's hit mask from projection
-// (small boxes, up to BIG_BOX tiles); the warp then writes the contiguous
+// (boxes of up to 16 tiles); the warp then writes the contiguous
 // output range of its 32 splats together, lane l taking positions p = p0 + l:
 // the owning splat is found by a binary search over the lanes' start offsets
 // and the entry is the (p - start)-th hit of its mask, so every store
