@@ -153,8 +153,8 @@ def make_workload(n_splats: int, config: int = 2):
 # capture of this workload (config 2 at 3M splats; profiles/<kernel>_config2_3M.md
 # give the command).  Below the algorithmic bytes for the raster kernels:
 # L2 (126 MB) serves a projected row to the neighbouring tiles that gather it.
-MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 272.8e6, "raster_fwd": 142.5e6, "project": 686.8e6, "loss": 60.8e6,
-                           "optimizer": 2.335e9}
+MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 273.6e6, "raster_fwd": 142.5e6, "project": 700.7e6, "loss": 60.8e6,
+                           "optimizer": 2.352e9 + 474.1e6}
 
 
 def stage_bytes(name: str, n: int, v: int, i: int, p: int, t: int) -> float:
@@ -333,7 +333,7 @@ def run_ours(args):
     roofline = None
     if world == 1 and not multiview:
         restore()
-        stages = profile_stages(trainer, splats, targets, cams, views, dev, reps=3)
+        stages = profile_stages(trainer, splats, targets, cams, views, dev, reps=5)
         peak, which = peaks()
         n, v, i = splats.num_splats, stages.pop("_v"), stages.pop("_i")
         cam0 = cams[views[0]]
@@ -399,8 +399,10 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def profile_stages(trainer, splats, targets, cams, views, dev, reps=3):
-    """Per-stage device times of the single-view step with CUDA events."""
+def profile_stages(trainer, splats, targets, cams, views, dev, reps=5):
+    """Per-stage device times of the single-view step with CUDA events: the
+    median over `reps` steps, so that a host stall between two launches (which
+    the events on the device timeline include) in one step does not count."""
     import torch
     from vauss_b200 import ops
     c = trainer.config
@@ -440,13 +442,13 @@ def profile_stages(trainer, splats, targets, cams, views, dev, reps=3):
         hook("optimizer")
         torch.cuda.synchronize()
         for (a, ea), (b, eb) in zip(evs[:-1], evs[1:]):
-            d = acc.setdefault(b, {"ms": 0.0})
-            d["ms"] += ea.elapsed_time(eb) / reps
+            acc.setdefault(b, []).append(ea.elapsed_time(eb))
         v += out.num_visible / reps
         i += out.num_intersections / reps
-    acc["_v"] = v
-    acc["_i"] = i
-    return acc
+    out = {k: {"ms": float(statistics.median(t))} for k, t in acc.items()}
+    out["_v"] = v
+    out["_i"] = i
+    return out
 
 
 # --------------------------------------------------- CPU baseline (oracle) ----
