@@ -218,10 +218,32 @@ __global__ void __launch_bounds__(128) sh_step_kernel(uint32_t count, uint32_t r
   codes[word] = packed;
 }
 
+// Block-wide compaction: the ids of the threads with `flag` set, in thread
+// order, into list[0 .. return value).  All threads of the block call it.
+template <uint32_t THREADS>
+__device__ __forceinline__ uint32_t compact_block(bool flag, uint32_t* list, uint32_t* warp_cnt) {
+  const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  const uint32_t bal = __ballot_sync(0xffffffffu, flag);
+  if (lane == 0) warp_cnt[warp] = __popc(bal);
+  __syncthreads();
+  uint32_t off = 0, total = 0;
+#pragma unroll
+  for (uint32_t w = 0; w < THREADS / 32; ++w) {
+    const uint32_t cw = warp_cnt[w];
+    off += w < warp ? cw : 0u;
+    total += cw;
+  }
+  if (flag) list[off + __popc(bal & ((1u << lane) - 1u))] = tid;
+  __syncthreads();
+  return total;
+}
+
 // ---- dense VJP ----
 // One thread per visible (projected) splat, in compact order; splats that
 // projection culled have no rasterizer row and no `visible` mark, so their
-// gradient rows, refine sums and view counts stay as they are.
+// gradient rows, refine sums and view counts stay as they are.  The rows with
+// a non-zero rasterizer gradient are compacted per block first, so the VJP
+// runs on whole warps.
 __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, const float* __restrict__ transforms,
                                                         const void* __restrict__ sh, const float* __restrict__ raw_opac,
                                                         const float* __restrict__ min_scale,
@@ -230,32 +252,40 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
                                                         float* __restrict__ grads, float* __restrict__ refine,
                                                         const float* __restrict__ visible,
                                                         float* __restrict__ vis_accum) {
+  __shared__ uint32_t s_list[256];
+  __shared__ uint32_t s_wcnt[8];
+  __shared__ uint8_t s_fresh[256];
   const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= v) return;
-  const uint32_t g = global_from_compact[c];
-  // A row not seen before in this step (vis_accum was 0) is overwritten, so
-  // readers gated on vis_accum never see an earlier step's values.
-  bool fresh = false;
-  if (vis_accum) {
-    const float seen = vis_accum[g];
-    vis_accum[g] = seen + visible[g];
-    fresh = seen == 0.0f && visible[g] > 0.0f;
-  }
   const int nc = (u.sh_degree + 1) * (u.sh_degree + 1);
   const int width = 10 + 3 * nc + 1;
-  const float* rg = v_combined + (size_t)c * 10;
-  float rr[10];
   bool any = false;
+  if (c < v) {
+    const uint32_t g = global_from_compact[c];
+    // A row not seen before in this step (vis_accum was 0) is overwritten, so
+    // readers gated on vis_accum never see an earlier step's values.
+    bool fresh = false;
+    if (vis_accum) {
+      const float seen = vis_accum[g];
+      vis_accum[g] = seen + visible[g];
+      fresh = seen == 0.0f && visible[g] > 0.0f;
+    }
+    const float* rg = v_combined + (size_t)c * 10;
 #pragma unroll
-  for (int k = 0; k < 10; ++k) {
-    rr[k] = rg[k];
-    any = any || rr[k] != 0.0f;
-  }
-  if (!any) {
-    if (fresh)
+    for (int k = 0; k < 10; ++k) any = any || rg[k] != 0.0f;
+    if (!any && fresh)
       for (int k = 0; k < width; ++k) grads[(size_t)g * width + k] = 0.0f;
-    return;
+    s_fresh[threadIdx.x] = fresh ? 1 : 0;
   }
+  const uint32_t total = compact_block<256>(any, s_list, s_wcnt);
+  if (threadIdx.x >= total) return;
+  const uint32_t t = s_list[threadIdx.x];
+  const uint32_t cc = blockIdx.x * blockDim.x + t;
+  const uint32_t g = global_from_compact[cc];
+  const bool fresh = s_fresh[t] != 0;
+  const float* rg = v_combined + (size_t)cc * 10;
+  float rr[10];
+#pragma unroll
+  for (int k = 0; k < 10; ++k) rr[k] = rg[k];
   float tt[10];
 #pragma unroll
   for (int k = 0; k < 10; ++k) tt[k] = transforms[(size_t)g * 10 + k];
@@ -270,7 +300,7 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
   sh_basis_all(o.dir.x, o.dir.y, o.dir.z, b);
   for (int k = 0; k < nc; ++k) {
 #pragma unroll
-    for (int cc = 0; cc < 3; ++cc) d[10 + k * 3 + cc] = (fresh ? 0.0f : d[10 + k * 3 + cc]) + rr[5 + cc] * b[k];
+    for (int q = 0; q < 3; ++q) d[10 + k * 3 + q] = (fresh ? 0.0f : d[10 + k * 3 + q]) + rr[5 + q] * b[k];
   }
   d[width - 1] = (fresh ? 0.0f : d[width - 1]) + o.v_raw;
   refine[g] += clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
@@ -280,45 +310,53 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
 // One row of VJP_ROW floats per visible splat, in compact (projection) order:
 // 0-9 transforms gradient, 10 raw-opacity gradient, 11-13 colour gradient
 // (rasterizer rgb), 14-16 view direction, 17 refine weight, 18 = 1 when the
-// rasterizer row has a non-zero value (else the whole row is 0), 19 unused.
-// Running the VJP here, over the visible rows only and at full occupancy,
-// keeps its dependent gathers and its code out of the optimizer kernel.
+// rasterizer row has a non-zero value, 19 unused.  A row without gradient
+// has only its last float4 (refine, flag) written, as zeros; readers take the
+// rest only when the flag is set.  Running the VJP here, over the compacted
+// rows with a gradient, keeps its dependent gathers and its code out of the
+// optimizer kernel.
 constexpr uint32_t VJP_ROW = 20;
 
 __global__ void __launch_bounds__(128) vjp_rows_kernel(Uniforms u, uint32_t v, const uint32_t* __restrict__ global_from_compact,
                                                        const float* __restrict__ transforms, const float* __restrict__ sh,
                                                        const float* __restrict__ raw_opac,
                                                        const float* __restrict__ v_combined, float4* __restrict__ rows) {
+  __shared__ uint32_t s_list[128];
+  __shared__ uint32_t s_wcnt[4];
   const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= v) return;
-  const float* rg = v_combined + (size_t)c * 10;
-  float rr[10];
   bool active = false;
+  if (c < v) {
+    const float* rg = v_combined + (size_t)c * 10;
 #pragma unroll
-  for (int k = 0; k < 10; ++k) {
-    rr[k] = rg[k];
-    active = active || rr[k] != 0.0f;
+    for (int k = 0; k < 10; ++k) active = active || rg[k] != 0.0f;
+    // a row without gradient: only its flag (and refine) float4 is read
+    if (!active) rows[(size_t)c * (VJP_ROW / 4) + 4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   }
+  // the rows with a gradient, compacted so that the VJP runs on whole warps
+  const uint32_t total = compact_block<128>(active, s_list, s_wcnt);
+  if (threadIdx.x >= total) return;
+  const uint32_t cc = blockIdx.x * blockDim.x + s_list[threadIdx.x];
+  const float* rg = v_combined + (size_t)cc * 10;
+  float rr[10];
+#pragma unroll
+  for (int k = 0; k < 10; ++k) rr[k] = rg[k];
+  const uint32_t g = global_from_compact[cc];
+  float tt[10];
+#pragma unroll
+  for (int k = 0; k < 10; ++k) tt[k] = transforms[(size_t)g * 10 + k];
+  // the Q8 step takes no min_scale floor (its launcher rejects frames with one)
+  const VjpOut r = splat_vjp(tt, raw_opac[g], sh, nullptr, g, rr, u);
   float o[VJP_ROW];
-#pragma unroll
-  for (int k = 0; k < (int)VJP_ROW; ++k) o[k] = 0.0f;
-  if (active) {
-    const uint32_t g = global_from_compact[c];
-    float tt[10];
-#pragma unroll
-    for (int k = 0; k < 10; ++k) tt[k] = transforms[(size_t)g * 10 + k];
-    // the Q8 step takes no min_scale floor (its launcher rejects frames with one)
-    const VjpOut r = splat_vjp(tt, raw_opac[g], sh, nullptr, g, rr, u);
-    o[0] = r.v_mean.x; o[1] = r.v_mean.y; o[2] = r.v_mean.z;
-    o[3] = r.v_q.w; o[4] = r.v_q.x; o[5] = r.v_q.y; o[6] = r.v_q.z;
-    o[7] = r.v_scale.x; o[8] = r.v_scale.y; o[9] = r.v_scale.z;
-    o[10] = r.v_raw;
-    o[11] = rr[5]; o[12] = rr[6]; o[13] = rr[7];
-    o[14] = r.dir.x; o[15] = r.dir.y; o[16] = r.dir.z;
-    o[17] = clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
-    o[18] = 1.0f;
-  }
-  float4* d = rows + (size_t)c * (VJP_ROW / 4);
+  o[0] = r.v_mean.x; o[1] = r.v_mean.y; o[2] = r.v_mean.z;
+  o[3] = r.v_q.w; o[4] = r.v_q.x; o[5] = r.v_q.y; o[6] = r.v_q.z;
+  o[7] = r.v_scale.x; o[8] = r.v_scale.y; o[9] = r.v_scale.z;
+  o[10] = r.v_raw;
+  o[11] = rr[5]; o[12] = rr[6]; o[13] = rr[7];
+  o[14] = r.dir.x; o[15] = r.dir.y; o[16] = r.dir.z;
+  o[17] = clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
+  o[18] = 1.0f;
+  o[19] = 0.0f;
+  float4* d = rows + (size_t)cc * (VJP_ROW / 4);
 #pragma unroll
   for (int k = 0; k < (int)(VJP_ROW / 4); ++k) d[k] = make_float4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
 }
