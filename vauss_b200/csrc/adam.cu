@@ -694,8 +694,9 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
         float refine = 0.0f;
         if (row > 0) {
           const float4* r4 = vjp_rows + (size_t)(row - 1) * (VJP_ROW / 4);
-          const float4 x0 = r4[0], x1 = r4[1], x2 = r4[2], x3 = r4[3], x4 = r4[4];
+          const float4 x4 = r4[4];  // refine, flag: the only part written for a row without gradient
           if (x4.z != 0.0f) {
+            const float4 x0 = r4[0], x1 = r4[1], x2 = r4[2], x3 = r4[3];
             gr[0] = x0.x; gr[1] = x0.y; gr[2] = x0.z; gr[3] = x0.w;
             gr[4] = x1.x; gr[5] = x1.y; gr[6] = x1.z; gr[7] = x1.w;
             gr[8] = x2.x; gr[9] = x2.y; go = x2.z;
