@@ -501,13 +501,16 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
         if (MODE == 1) {
           g[k] = ok ? grow[(size_t)s * width + 10u + col] : 0.0f;
         } else if (MODE == 2) {
+          // every rank's load is issued before the sum, which runs in rank order
+          const uint32_t vm = ok ? sm.vmask[s] : 0u;
+          const size_t off = ((size_t)(t_base / W) + s) * width + 10u + col;
+          float tv[VS_PEER_MAX];
+#pragma unroll
+          for (uint32_t r = 0; r < VS_PEER_MAX; ++r) tv[r] = ((vm >> r) & 1u) ? pa.grads[r][off] : 0.0f;
           float acc = 0.0f;
-          if (ok) {
-            const uint32_t vm = sm.vmask[s];
-            const size_t off = ((size_t)(t_base / W) + s) * width + 10u + col;
-            for (uint32_t r = 0; r < pa.world; ++r)
-              if ((vm >> r) & 1u) acc += pa.grads[r][off];
-          }
+#pragma unroll
+          for (uint32_t r = 0; r < VS_PEER_MAX; ++r)
+            if ((vm >> r) & 1u) acc += tv[r];
           g[k] = acc;
         } else {
           g[k] = ok ? sm.vc[s * 3u + r3] * sm.bas[s * 16u + c3] : 0.0f;
