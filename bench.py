@@ -151,8 +151,11 @@ def make_workload(n_splats: int, config: int = 2):
 
 # DRAM bytes (read + write) per launch of each stage's kernel, from one ncu
 # capture of this workload (config 2 at 3M splats; profiles/<kernel>_config2_3M.md
-# give the command).  Below the algorithmic bytes for the raster kernels:
-# L2 (126 MB) serves a projected row to the neighbouring tiles that gather it.
+# give the command; the optimizer's second term is vjp_rows_kernel from the
+# same capture, taken before that kernel compacted its rows).  Below the
+# algorithmic bytes for the raster kernels: L2 (126 MB) serves a projected row
+# to the neighbouring tiles that gather it.  Only the dominant stage's figure
+# goes into the bench line.
 MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 273.6e6, "raster_fwd": 142.5e6, "project": 700.7e6, "loss": 60.8e6,
                            "optimizer": 2.352e9 + 474.1e6}
 
