@@ -97,9 +97,10 @@ __device__ V3 splat_color(const void* sh, bool half, uint32_t g, int deg, V3 mea
   const int cnt = nc * 3;
   const size_t base = (size_t)g * cnt;
   // All coefficients are loaded before any is used: 16-byte loads when the
-  // row is f32 and a multiple of 16 bytes long (degrees 1 and 3).
+  // row is f32, a multiple of 16 bytes long (degrees 1 and 3) and the array
+  // starts on a 16-byte boundary.
   float cf[48];
-  if (!half && (cnt & 3) == 0) {
+  if (!half && (cnt & 3) == 0 && (reinterpret_cast<uintptr_t>(sh) & 15u) == 0) {
     const float4* p4 = reinterpret_cast<const float4*>((const float*)sh + base);
 #pragma unroll
     for (int q = 0; q < 12; ++q) {

@@ -74,8 +74,24 @@ VSD V3 projection_vjp_pinhole(const M23& J, V3 mc, S3 cov_c, const Uniforms& u, 
 
 // SH view-direction VJP for bands <= 3 (kernels/sh.rs:147-270).
 VSD V3 sh_viewdir_vjp(const void* sh, bool half, size_t base, int deg, V3 v, V3 vc) {
+  // Degree 3 in f32 from a 16-byte aligned array: the 45 coefficients past
+  // the DC term are loaded up front as 16-byte vectors (the row is 192 bytes).
+  float cf[48];
+  const bool vec = !half && deg == 3 && (reinterpret_cast<uintptr_t>(sh) & 15u) == 0;
+  if (vec) {
+    const float4* p4 = reinterpret_cast<const float4*>((const float*)sh + base);
+#pragma unroll
+    for (int q = 0; q < 12; ++q) {
+      const float4 x = p4[q];
+      cf[4 * q] = x.x;
+      cf[4 * q + 1] = x.y;
+      cf[4 * q + 2] = x.z;
+      cf[4 * q + 3] = x.w;
+    }
+  }
   auto sd = [&](int k) -> float {
-    const V3 c = {sh_load(sh, half, base + k), sh_load(sh, half, base + k + 1), sh_load(sh, half, base + k + 2)};
+    const V3 c = vec ? V3{cf[k], cf[k + 1], cf[k + 2]}
+                     : V3{sh_load(sh, half, base + k), sh_load(sh, half, base + k + 1), sh_load(sh, half, base + k + 2)};
     return v3dot(c, vc);
   };
   float gx = 0.0f, gy = 0.0f, gz = 0.0f;
