@@ -157,6 +157,34 @@ def test_abi_rejects_bad_arguments(cuda):
     assert st == 5
 
 
+def test_render_rejects_misaligned_transforms(cuda):
+    """Projection reads each 40-byte transforms row in 8-byte pieces; a
+    transforms array that starts off an 8-byte boundary is refused before any
+    launch."""
+    sp, cams = medium_scene(n=300, sh_degree=3)
+    s = Splats.from_numpy(sp, cuda)
+    t = torch.zeros(300 * 10 + 1, device=cuda)[1:].view(300, 10)  # 4 bytes past an aligned start
+    t.copy_(s.transforms)
+    with pytest.raises(_native.VsError) as e:
+        ops.render(cams[0], ops.render_cfg(3), t, s.sh_coeffs, s.raw_opacities)
+    assert e.value.status == 1 and "8-byte aligned" in str(e.value)
+
+
+def test_render_with_misaligned_sh_matches_aligned(cuda):
+    """SH coefficients are read as 16-byte vectors only from an array on a
+    16-byte boundary; one 4 bytes off renders through scalar loads, bit for bit
+    the same image."""
+    sp, cams = medium_scene(n=3000, sh_degree=3)
+    s = Splats.from_numpy(sp, cuda)
+    sh_off = torch.zeros(3000 * 48 + 1, device=cuda)[1:].view(3000, 16, 3)
+    sh_off.copy_(s.sh_coeffs)
+    cfg = ops.render_cfg(3, mip=True)
+    want = ops.render(cams[0], cfg, s.transforms, s.sh_coeffs, s.raw_opacities).out_img.clone()
+    got = ops.render(cams[0], cfg, s.transforms, sh_off, s.raw_opacities).out_img
+    torch.cuda.synchronize()
+    assert_bits_equal(got.cpu().numpy(), want.cpu().numpy(), "image from a misaligned SH array")
+
+
 def test_q8_rejects_unaligned_arrays(cuda):
     """The Q8 kernels move parameters and codes in 16-byte pieces; a parameter
     array that starts off a 16-byte boundary is refused before any launch."""

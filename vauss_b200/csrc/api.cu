@@ -206,6 +206,9 @@ VS_API vs_status vs_render_project(vs_ctx* ctx, vs_frame* f, const vs_camera* ca
   if (cam->img_w == 0 || cam->img_h == 0) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: zero image size");
   if (cfg->sh_degree < 0 || cfg->sh_degree > 3) return vs_fail(ctx, VS_ERR_UNSUPPORTED, "render_forward: SH degree %d (0..3 supported)", cfg->sh_degree);
   if (num_splats > 0 && (!transforms || !sh_coeffs || !raw_opacities)) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: null splat buffer");
+  // projection reads each 40-byte transforms row in 8-byte pieces
+  if (reinterpret_cast<uintptr_t>(transforms) & 7u)
+    return vs_fail(ctx, VS_ERR_INVALID, "render_forward: transforms must be 8-byte aligned");
   if (cfg->has_min_scale && !min_scale) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: has_min_scale without min_scale");
   if (num_splats > 0xfffffff0u / 10u) return vs_fail(ctx, VS_ERR_CAPACITY, "render_forward: %u splats exceed 32-bit indexing", num_splats);
   VS_TRY(set_device(ctx));
