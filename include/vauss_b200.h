@@ -113,6 +113,7 @@ VS_API vs_status vs_frame_copy(vs_frame* frame, int32_t field, void* dst_device,
  * bwd_info).  Writes out_img [H,W,4] and visible [N] (1.0 where a splat
  * contributed to a pixel, else 0.0); counts_out may be NULL, and so may
  * visible when num_splats is 0 (the image is then the background).
+ * Images are limited to 65535 tiles per side (VS_ERR_UNSUPPORTED beyond).
  * transforms must start on an 8-byte boundary (VS_ERR_INVALID otherwise);
  * f32 SH coefficients on a 16-byte boundary take the vector-load path. */
 VS_API vs_status vs_render_forward(vs_ctx* ctx, vs_frame* frame, const vs_camera* cam, const vs_render_cfg* cfg,

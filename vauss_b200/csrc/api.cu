@@ -204,6 +204,10 @@ VS_API vs_status vs_render_project(vs_ctx* ctx, vs_frame* f, const vs_camera* ca
   if (!ctx) return VS_ERR_INVALID;
   if (!f || f->ctx != ctx || !cam || !cfg) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: missing frame/camera/config");
   if (cam->img_w == 0 || cam->img_h == 0) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: zero image size");
+  // the emission packs tile coordinates into 16 bits
+  if (cam->img_w > 65535u * vs::TILE || cam->img_h > 65535u * vs::TILE)
+    return vs_fail(ctx, VS_ERR_UNSUPPORTED, "render_forward: image %ux%u exceeds 65535 tiles per side", cam->img_w,
+                   cam->img_h);
   if (cfg->sh_degree < 0 || cfg->sh_degree > 3) return vs_fail(ctx, VS_ERR_UNSUPPORTED, "render_forward: SH degree %d (0..3 supported)", cfg->sh_degree);
   if (num_splats > 0 && (!transforms || !sh_coeffs || !raw_opacities)) return vs_fail(ctx, VS_ERR_INVALID, "render_forward: null splat buffer");
   // projection reads each 40-byte transforms row in 8-byte pieces
