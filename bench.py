@@ -1,7 +1,10 @@
 #!/usr/bin/env python
 """Benchmark of the Gaussian-splat training step (fwd + bwd + Adam).
 
-Workload (benchmark configuration 2, "full training iteration at scale"):
+Configurations are numbered as BASELINE.json's ``configs`` list (0-based):
+configs[0] is the tiny CPU-runnable run (a test case, not a bench line).
+
+Default workload, configs[2] ("full training iteration at scale"):
 3,000,000 SH-degree-3 splats (means U[-5,5]^3, log-scales N(-4.5, 0.6),
 opacity logits N(0, 1.5), DC colours U[0,1], higher bands N(0, 0.05)),
 200 pinhole views of 1600x1060 (fx = fy = 1300) on a jittered sphere of
@@ -17,17 +20,32 @@ gradient rows are read over NVLink peer memory by a sharded fused Adam that
 stores the new parameters into every replica (weak scaling: one view per GPU
 per step); value = views/s over the whole job = iterations/s at N = 1.
 
-With --config 3 it runs benchmark configuration 3 instead: 6,000,000 splats
-(configuration-2 distributions) and a fixed global batch of 8 views of
-1920x1080 (fx = fy = 1600) per step, split evenly over 1, 2, 4 or 8 GPUs
-(strong scaling; value = global-batch steps/s).  Every GPU count, one
-included, runs the peer-memory view-parallel trainer.
+After the timed region the same run, from the state the timed region started
+from: the end-to-end leg through the public API (``e2e``), per-stage device
+times (``stages``), at N = 1 one GPU step and one CPU-oracle step compared
+(``parity``; the oracle step is also ``cpu_baseline``), at N > 1 a checksum
+of every rank's replica (``replicas_equal``) and one step through the
+peer-memory exchange against one through an NCCL all-reduce
+(``exchange_check``), and finally configs[3] as a companion leg
+(``config3``: steps/s of the fixed 8-view global batch at this N).
 
-With --config 4 it runs the sort/overlap stress (configuration 4, one GPU):
-10,000,000 large splats, one 3840x2160 view; value = intersections/s through
+--config 3 runs configs[3] as the main line: 6,000,000 splats (configs[2]
+distributions) and a fixed global batch of 8 views of 1920x1080
+(fx = fy = 1600) per step, split evenly over 1, 2, 4 or 8 GPUs (strong
+scaling; value = global-batch steps/s).  Every GPU count, one included, runs
+the peer-memory view-parallel trainer.
+
+--config 1 runs configs[1], the single-view render forward + backward
+microbench (1M splats, 1920x1080), with rooflines for both raster kernels.
+
+--config 4 runs the sort/overlap stress of configs[4] (one GPU): 10,000,000
+large splats, one 3840x2160 view; value = intersections/s through
 intersect + radix sort + tile ranges.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--config 2|3|4]
+--optimizer reference (configs[2], one GPU) steps the reference's optimizer
+storage instead of the 8-bit m+v Adam.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--config 1|2|3|4]
 """
 from __future__ import annotations
 
@@ -57,13 +75,18 @@ def parse():
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--splats", type=int, default=None, help="default: 3M (config 2), 6M (config 3)")
-    p.add_argument("--config", type=int, default=2, choices=[2, 3, 4])
-    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--splats", type=int, default=None, help="default: 1M (configs[1]), 3M (configs[2]), 6M (configs[3]), 10M (configs[4])")
+    p.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4],
+                   help="index into BASELINE.json configs (0-based)")
+    p.add_argument("--optimizer", default="q8", choices=["q8", "reference"],
+                   help="configs[2] on one GPU: the 8-bit m+v Adam, or the reference's optimizer storage")
+    p.add_argument("--no-cpu-baseline", action="store_true", help="skip the oracle step (parity and CPU baseline)")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-check", action="store_true", help="N > 1: skip the peer vs all-reduce exchange check")
+    p.add_argument("--no-config3", action="store_true", help="skip the configs[3] companion leg")
     a = p.parse_args()
     if a.splats is None:
-        a.splats = {2: N_SPLATS, 3: 6_000_000, 4: 10_000_000}[a.config]
+        a.splats = {1: 1_000_000, 2: N_SPLATS, 3: 6_000_000, 4: 10_000_000}[a.config]
     return a
 
 
@@ -150,12 +173,11 @@ def make_workload(n_splats: int, config: int = 2):
 
 
 # DRAM bytes (read + write) per launch of each stage's kernel, from one ncu
-# capture of this workload (config 2 at 3M splats; profiles/<kernel>_config2_3M.md
-# give the command; the optimizer's second term is vjp_rows_kernel from the
-# same capture, taken before that kernel compacted its rows).  Below the
-# algorithmic bytes for the raster kernels: L2 (126 MB) serves a projected row
-# to the neighbouring tiles that gather it.  Only the dominant stage's figure
-# goes into the bench line.
+# capture of this workload (configs[2] at 3M splats; the optimizer's second
+# term is vjp_rows_kernel from the same capture).  Below the algorithmic bytes
+# for the raster kernels: L2 (126 MB) serves a projected row to the
+# neighbouring tiles that gather it.  Only the dominant stage's figure goes
+# into the bench line.
 MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 273.6e6, "raster_fwd": 142.5e6, "project": 700.7e6, "loss": 60.8e6,
                            "optimizer": 2.352e9 + 474.1e6}
 
@@ -175,15 +197,463 @@ def stage_bytes(name: str, n: int, v: int, i: int, p: int, t: int) -> float:
         return i * 52 + p * 32 + v * 80
     if name == "optimizer":  # params r+w 472, m/v codes r+w 236, scales, cfg map 4, stats 24, noise gate 8 per splat
         return n * (472 + 236 + 4 + 24 + 8 + 2 * 59 * 8 / 256) + v * 40
+    if name == "optimizer_reference":
+        # per splat: transforms r+w 80, packed geometry/opacity moment words r+w 88, opacity r+w 8, f16 SH r+w
+        # 192, int8 SH m r+w 96, SH m scales ~3, SH v r+w 8, compact map 4, refine + grad^2 writes 8, stats r+w 24;
+        # per visible splat: v_combined 40, params gathered for the VJP 140, colour/direction row w+r 48
+        return n * (80 + 88 + 8 + 192 + 96 + 3 + 8 + 4 + 8 + 24) + v * (40 + 140 + 48)
     return 0.0
+
+
+def mixed_rel(got, want, floor_frac=1e-3):
+    """Largest |got - want| / max(|want|, floor_frac * max|want|): the tests'
+    mixed absolute/relative error, as one number."""
+    got = np.asarray(got, dtype=np.float64).ravel()
+    want = np.asarray(want, dtype=np.float64).ravel()
+    if want.size == 0:
+        return 0.0
+    scale = max(floor_frac * float(np.abs(want).max()), 1e-30)
+    return float((np.abs(got - want) / np.maximum(np.abs(want), scale)).max())
+
+
+def count_over(got, want, rel=1e-4, floor_frac=1e-3):
+    """Elements beyond the tests' mixed tolerance."""
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    scale = max(floor_frac * float(np.abs(want).max()) if want.size else 0.0, 1e-30)
+    return int((np.abs(got - want) > rel * np.maximum(np.abs(want), scale)).sum())
+
+
+def replica_checksum(splats):
+    """Two order-sensitive int64 checksums per parameter tensor of this
+    rank's replica (sum of the f32 bit patterns, and that sum weighted by the
+    element index mod 65521)."""
+    import torch
+    out = []
+    for x in (splats.transforms, splats.sh_coeffs, splats.raw_opacities):
+        b = x.contiguous().view(-1).view(torch.int32).to(torch.int64)
+        w = torch.arange(b.numel(), device=b.device, dtype=torch.int64) % 65521 + 1
+        out += [int(b.sum().item()), int((b * w).sum().item())]
+        del b, w
+    return out
+
+
+class Leg:
+    """One benchmark workload on this rank: the splats, targets and trainer
+    of configuration 2 (one view per GPU per step) or 3 (a fixed global batch
+    of 8 views split over the GPUs), and the snapshot the timed region
+    starts from."""
+
+    def __init__(self, args, config, n_splats, world, rank, dev):
+        import torch
+        from vauss_b200 import ops, scenes
+        from vauss_b200.trainer import Splats, SplatTrainer, TrainConfig
+        from vauss_b200.view_parallel import ViewParallelTrainer
+        self.args, self.config, self.world, self.rank, self.dev = args, config, world, rank, dev
+        self.multiview = config == 3
+        if self.multiview and 8 % world:
+            raise SystemExit("configuration 3 splits its 8 views over 1, 2, 4 or 8 GPUs")
+        sp, tgt, cams = make_workload(n_splats, config)
+        self.sp, self.cams = sp, cams
+        splats = Splats.from_numpy(sp, dev)
+        tsplats = Splats.from_numpy(tgt, dev)
+        del tgt
+        cfg_t = ops.render_cfg(3, mip=True)
+        if self.multiview:  # this rank's share of the fixed global batch
+            per_rank = 8 // world
+            self.views = [rank * per_rank + k for k in range(per_rank)]
+        else:
+            self.views = [(rank * N_TARGETS + k) % N_VIEWS for k in range(N_TARGETS)]
+        self.targets = []
+        for vi in self.views:
+            out = ops.render(cams[vi], cfg_t, tsplats.transforms, tsplats.sh_coeffs, tsplats.raw_opacities)
+            img = out.out_img[..., :3].clamp(0, 1).cpu().numpy()
+            self.targets.append(torch.from_numpy(scenes.pack_rgba8(img).view(np.int32)).to(dev))
+        del tsplats
+        torch.cuda.synchronize()
+        self.cfg = TrainConfig(optimizer=args.optimizer if not (world > 1 or self.multiview) else "q8")
+        median_scale = float(np.median(np.exp(sp.transforms[:, 7:10])))
+        self.kw = dict(scene_extent=8.0, median_scale=median_scale)
+        self.peer = None
+        if world > 1 or self.multiview:
+            from vauss_b200.peer import PeerGroup, gather_bytes_nccl
+            gather = (lambda b: gather_bytes_nccl(b, dev)) if world > 1 else (lambda b: [b])
+            self.peer = PeerGroup(dev, world, rank, gather)
+            self.trainer = ViewParallelTrainer(self.cfg, dev, peer=self.peer, **self.kw)
+            self.splats = self.trainer.adopt(splats)
+            del splats
+        else:
+            self.trainer = SplatTrainer(self.cfg, dev, **self.kw)
+            self.splats = splats
+
+    def batches(self, k, loader=None):
+        from vauss_b200.trainer import SceneBatch
+        if self.multiview:
+            return ([loader.next_batch() for _ in self.views] if loader else
+                    [SceneBatch(self.targets[j], self.cams[self.views[j]], self.views[j])
+                     for j in range(len(self.views))])
+        vi = k % N_TARGETS
+        return [loader.next_batch() if loader else SceneBatch(self.targets[vi], self.cams[self.views[vi]],
+                                                                 self.views[vi])]
+
+    def step(self, k, loader=None, hook=None):
+        b = self.batches(k, loader)
+        if self.world > 1 or self.multiview:
+            return self.trainer.step_views(b, self.splats, hook=hook)
+        # the reference optimizer hands back new splats (SH in f16 from its first step)
+        self.splats, st = self.trainer.step(b[0], self.splats)
+        return self.splats, st
+
+    def barrier(self):
+        import torch
+        import torch.distributed as dist
+        if self.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def optim_tensors(self):
+        o = self.trainer.optim
+        if "t" in o:
+            return [getattr(o[k], a) for k in ("t", "sh", "o") for a in ("m_codes", "v_codes", "m_scales",
+                                                                           "v_scales")]
+        return [o[k] for k in ("w_t", "w_o", "codes", "scales", "variance")]
+
+    def snapshot(self):
+        import copy
+        s = self.splats
+        tr = self.trainer
+        self.snap = {"p": [x.clone() for x in (s.transforms, s.sh_coeffs, s.raw_opacities)],
+                     "m": [x.clone() for x in self.optim_tensors()],
+                     "time": tr.optim["time"], "step": tr.step_count,
+                     "rng": copy.deepcopy(tr.rng.bit_generator.state)}
+
+    def restore(self):
+        import copy
+        s = self.splats
+        tr = self.trainer
+        for dst, src in zip((s.transforms, s.sh_coeffs, s.raw_opacities), self.snap["p"]):
+            dst.copy_(src)
+        for dst, src in zip(self.optim_tensors(), self.snap["m"]):
+            dst.copy_(src)
+        tr.optim["time"], tr.step_count = self.snap["time"], self.snap["step"]
+        tr.rng.bit_generator.state = copy.deepcopy(self.snap["rng"])
+        self.barrier()
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+        if self.peer is None:
+            return
+        torch.cuda.synchronize(self.dev)
+        if self.world > 1:
+            dist.barrier()  # no rank's kernels touch peer buffers any more
+        self.peer.check()
+        self.peer.close()
+        self.peer = None
+        torch.cuda.synchronize(self.dev)
+        if self.world > 1:
+            dist.barrier()
+
+
+def timed_run(leg, steps, warmup):
+    """Warm-up, snapshot, then `steps` timed steps bracketed by a barrier and
+    a synchronize; returns (max-over-ranks ms, launches per step, clocks,
+    counts of the last warm-up step)."""
+    import torch
+    import torch.distributed as dist
+    from vauss_b200 import ops
+    counts = {}
+    for k in range(warmup):
+        _, st0 = leg.step(k)
+        counts = {"visible": int(st0.num_visible), "intersections": int(st0.num_intersections)}
+    leg.barrier()
+    # The timed region starts from this state; the per-stage profile, the
+    # end-to-end leg and the checks restart from it too, so that all of them
+    # see the same workload (training moves the splats, and the raster work
+    # grows with it).
+    leg.snapshot()
+    ctx = ops.context(leg.dev)
+    launches0 = ctx.launch_count
+    gpu_uuid = str(torch.cuda.get_device_properties(leg.dev).uuid)
+    gpu_id = gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}"
+    stream = torch.cuda.current_stream(leg.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_id) as clk:
+        leg.barrier()
+        clk.mark("start")
+        e0.record(stream)
+        for k in range(steps):
+            leg.step(warmup + k)
+        e1.record(stream)
+        leg.barrier()
+        clk.mark("stop")
+    ms = e0.elapsed_time(e1)
+    launches = (ctx.launch_count - launches0) // max(steps, 1)
+    t = torch.tensor([ms], dtype=torch.float64, device=leg.dev)
+    if leg.world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item()), launches, clk.summary(), counts
+
+
+def e2e_run(leg, steps, warmup):
+    """The same steps through the public API with the ground truth staged from
+    host memory each step (SceneLoader) and the loss read back."""
+    import torch
+    import torch.distributed as dist
+    from vauss_b200 import dataset
+    rgb = [tg.cpu().numpy().view(np.uint8).reshape(tg.shape[0], tg.shape[1], 4)[..., :3].copy()
+           for tg in leg.targets]
+    loader = dataset.SceneLoader(
+        dataset.Scene([dataset.SceneView(img, leg.cams[vi]) for img, vi in zip(rgb, leg.views)]), seed=leg.rank,
+        config=dataset.LoadDatasetConfig(max_scene_batch_cache_size=0), device=leg.dev,
+        hold=len(leg.views) if leg.multiview else 1)
+    loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+    for k in range(warmup):  # untimed: first use of the host-input path
+        _, st = leg.step(k, loader=loader)
+        loss_host.copy_(st.loss, non_blocking=True)
+    leg.restore()
+    stream = torch.cuda.current_stream(leg.dev)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h2d0 = loader.h2d_bytes_total
+    f0.record(stream)
+    for k in range(steps):
+        _, st = leg.step(k, loader=loader)
+        loss_host.copy_(st.loss, non_blocking=True)
+    f1.record(stream)
+    leg.barrier()
+    ems = f0.elapsed_time(f1)
+    h2d_total = loader.h2d_bytes_total - h2d0
+    loader.close()
+    te = torch.tensor([ems], dtype=torch.float64, device=leg.dev)
+    if leg.world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    per = 1 if leg.multiview else leg.world
+    return {"value": per * steps / (float(te.item()) / 1e3), "unit": "steps/s" if leg.multiview else "iters/s",
+            "h2d_bytes_per_step": int(round(h2d_total / max(steps, 1))), "d2h_bytes_per_step": 4,
+            "feed": "SceneLoader (vs_feed): RGB8 views, pinned ring of 4, packed on the GPU, no cache",
+            "api": ("ViewParallelTrainer.step_views (vs_render_forward, vs_loss, vs_rasterize_backward, "
+                    "vs_vjp_dense, vs_peer_barrier, vs_adam_q8_peer)" if leg.world > 1 or leg.multiview else
+                    "SplatTrainer.step (vs_render_forward, vs_loss, vs_rasterize_backward, vs_step_q8)")}
+
+
+def profile_stages_views(leg, reps=5):
+    """Per-stage device times of the view-parallel step (CUDA events on the
+    launching stream): the median over `reps` steps per rank, then the maximum
+    over ranks for every stage."""
+    import torch
+    import torch.distributed as dist
+    stream = torch.cuda.current_stream(leg.dev)
+    acc = {}
+    for r in range(reps):
+        evs = [("start", torch.cuda.Event(enable_timing=True))]
+        evs[0][1].record(stream)
+
+        def hook(name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            evs.append((name, e))
+        leg.step(r, hook=hook)
+        torch.cuda.synchronize()
+        per = {}
+        for (_, ea), (b, eb) in zip(evs[:-1], evs[1:]):
+            per[b] = per.get(b, 0.0) + ea.elapsed_time(eb)  # several views: summed per stage
+        for b, v in per.items():
+            acc.setdefault(b, []).append(v)
+    names = list(acc)
+    med = torch.tensor([statistics.median(acc[k]) for k in names], dtype=torch.float64, device=leg.dev)
+    if leg.world > 1:
+        dist.all_reduce(med, op=dist.ReduceOp.MAX)
+    return {k: {"ms": round(float(v), 4)} for k, v in zip(names, med.tolist())}
+
+
+def replicas_check(leg):
+    """True when every rank's replica has the same checksums as rank 0's."""
+    import torch
+    import torch.distributed as dist
+    mine = torch.tensor(replica_checksum(leg.splats), dtype=torch.int64, device=leg.dev)
+    allc = [torch.empty_like(mine) for _ in range(leg.world)]
+    dist.all_gather(allc, mine)
+    return all(torch.equal(allc[0], c) for c in allc[1:])
+
+
+def exchange_check(leg):
+    """One step from the timed-region snapshot through the peer-memory
+    exchange and one through an NCCL all-reduce of the dense rows followed by
+    the replicated Adam, both from zero moments; returns the largest
+    differences over ranks between the two parameter sets."""
+    import copy
+    import torch
+    import torch.distributed as dist
+    from vauss_b200 import ops
+    from vauss_b200.trainer import Splats
+    from vauss_b200.view_parallel import ViewParallelTrainer
+    from vauss_b200.trainer import SceneBatch
+    leg.restore()
+    tr = leg.trainer
+    saved = tr.optim
+    nc = leg.splats.sh_coeffs.shape[1]
+    m = tr.shard[1] - tr.shard[0]
+    tr.optim = dict(t=ops.Q8Moments(m * 10, leg.dev), sh=ops.Q8Moments(m * nc * 3, leg.dev),
+                    o=ops.Q8Moments(m, leg.dev), time=saved["time"])
+    ref = ViewParallelTrainer(leg.cfg, leg.dev, **leg.kw)  # all-reduce exchange (NCCL)
+    p0 = [x.clone() for x in (leg.splats.transforms, leg.splats.sh_coeffs, leg.splats.raw_opacities)]
+    other = Splats(*[x.clone() for x in p0])
+    ref._init_state(other)
+    ref.optim["time"], ref.step_count = saved["time"], tr.step_count
+    ref.rng.bit_generator.state = copy.deepcopy(tr.rng.bit_generator.state)
+    b = leg.batches(0)
+    tr.step_views(b, leg.splats)
+    ref.step_views(b, other)
+    torch.cuda.synchronize()
+    got = [x.cpu().numpy() for x in (leg.splats.transforms, leg.splats.sh_coeffs, leg.splats.raw_opacities)]
+    want = [x.cpu().numpy() for x in (other.transforms, other.sh_coeffs, other.raw_opacities)]
+    base = [x.cpu().numpy() for x in p0]
+    prm = max(mixed_rel(g, w) for g, w in zip(got, want))
+    upd = max(float(np.abs((g - b0) - (w - b0)).max()) / max(float(np.abs(w - b0).max()), 1e-30)
+              for g, w, b0 in zip(got, want, base))
+    t = torch.tensor([prm, upd], dtype=torch.float64, device=leg.dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    tr.optim = saved
+    del ref, other
+    torch.cuda.empty_cache()
+    leg.restore()
+    return {"params_max_rel": float(t[0]), "update_max_rel": float(t[1]),
+            "what": "one step from the timed-region parameters and zero moments through the peer-memory exchange "
+                    "and through an NCCL all-reduce + replicated Adam; mixed rel over all parameters, and the "
+                    "largest update difference over the largest update"}
+
+
+def parity_leg(leg):
+    """One training step on the GPU and one of the CPU oracle, both from the
+    timed-region snapshot (parameters and 8-bit moments) on the first view:
+    integer outputs compared for equality, floating-point ones as the tests'
+    mixed error.  The oracle step is also the CPU baseline's timed sample."""
+    import oracle
+    import torch
+    from vauss_b200 import ops, scenes
+    leg.restore()
+    tr = leg.trainer
+    c = tr.config
+    dev = leg.dev
+    s = leg.splats
+    n = s.num_splats
+    host = [x.cpu().numpy() for x in (s.transforms, s.sh_coeffs, s.raw_opacities)]
+    o = tr.optim
+    mom_h = {k: [getattr(o[k], a).cpu().numpy() for a in ("m_codes", "v_codes", "m_scales", "v_scales")]
+             for k in ("t", "sh", "o")}
+    t_step = o["time"] + 1
+    lr_t = np.asarray(tr.transforms_lr(), np.float32)
+    lr_dc, lr_rest, lr_o = c.lr_coeffs_dc, c.lr_coeffs_dc / c.lr_coeffs_sh_scale, c.lr_opac
+    noise = (1e-7, 1e-3, 4321)
+    cam, gt = leg.cams[leg.views[0]], leg.targets[0]
+    # ---- GPU: the trainer's kernels with the same arguments ----
+    t, sh, op = (x.clone() for x in (s.transforms, s.sh_coeffs, s.raw_opacities))
+    moms = []
+    for k in ("t", "sh", "o"):
+        q = ops.Q8Moments.__new__(ops.Q8Moments)
+        q.m_codes, q.v_codes, q.m_scales, q.v_scales = (getattr(o[k], a).clone() for a in
+                                                        ("m_codes", "v_codes", "m_scales", "v_scales"))
+        moms.append(q)
+    cfg = ops.render_cfg(3, mip=True)
+    frame = ops.Frame(ops.context(dev))
+    out = ops.render(cam, cfg, t, sh, op, frame=frame)
+    loss = ops.image_loss(out.out_img, gt, c.l1_weight, c.ssim_loss_weight)
+    vc = ops.rasterize_bwd(out.frame, out.out_img, loss.dl_dpred)
+    vc_h = vc.cpu().numpy()
+    q8 = ops.q8_cfg(t_step, lr_t, lr_dc, lr_rest, lr_o, eps=c.adam_epsilon, noise_scale=noise[0],
+                    noise_limit=noise[1], noise_seed=noise[2])
+    ops.step_q8(out.frame, cfg, t, sh, op, vc, *moms, q8, visible=out.visible)
+    torch.cuda.synchronize()
+    g = {"img": out.out_img.cpu().numpy(), "visible": out.visible.cpu().numpy(), "loss": float(loss.loss.item()),
+         "tile": frame.field("isect_tile").cpu().numpy().view(np.uint32),
+         "cid": frame.field("isect_compact").cpu().numpy().view(np.uint32),
+         "ranges": frame.field("tile_ranges").cpu().numpy().view(np.uint32),
+         "used": frame.field("tile_used_end").cpu().numpy().view(np.uint32),
+         "params": [x.cpu().numpy() for x in (t, sh, op)],
+         "codes": [getattr(q, a).cpu().numpy() for q in moms for a in ("m_codes", "v_codes")]}
+    nv, ni = out.num_visible, out.num_intersections
+    del t, sh, op, moms, out, loss, vc, frame
+    torch.cuda.empty_cache()
+    # ---- CPU oracle ----
+    cores = oracle.set_num_threads(os.cpu_count() or 1)
+    gt_h = gt.cpu().numpy().view(np.uint32)
+    t0 = time.perf_counter()
+    cfg_o = oracle.make_cfg(3, mip=True)
+    sset = scenes.SplatSet(*host)
+    ref = oracle.render_forward(cam, cfg_o, sset)
+    lo = oracle.loss_fwd(ref["out_img"], gt_h, c.l1_weight, c.ssim_loss_weight)
+    dl = oracle.loss_bwd(ref["out_img"], gt_h, lo["coeffs"], c.l1_weight, c.ssim_loss_weight)
+    vc_ref = oracle.raster_bwd(cam, (0.0, 0.0, 0.0), ref["proj"], ref["binning_after"], ref["out_img"], dl)
+    grads, _ = oracle.vjp_dense(cam, cfg_o, host[0], host[1], host[2], ref["proj"]["compact_from_global"], vc_ref)
+    b1, b2, inv1, inv2 = ops.adam_coefficients(t_step)
+    width = grads.shape[1]
+    eps = c.adam_epsilon
+    rt = oracle.adam_q8(host[0], grads, width, 0, 10, *[x.copy() for x in mom_h["t"]], lr_t, 1.0, b1, b2, inv1,
+                        inv2, eps, t_step ^ (10 << 24))
+    lr_sh = np.float32([lr_dc] * 3 + [lr_rest] * 45)
+    rs = oracle.adam_q8(host[1].reshape(n, -1), grads, width, 10, 48, *[x.copy() for x in mom_h["sh"]], lr_sh, 1.0,
+                        b1, b2, inv1, inv2, eps, t_step ^ (48 << 24))
+    ro = oracle.adam_q8(host[2], grads, width, width - 1, 1, *[x.copy() for x in mom_h["o"]], np.float32([lr_o]),
+                        1.0, b1, b2, inv1, inv2, eps, t_step ^ (1 << 24))
+    tr_new = oracle.noise_means(rt[0].reshape(n, 10), ref["proj"]["opacities"], ref["visible"], *noise)
+    dt = time.perf_counter() - t0
+    want = [tr_new, rs[0].reshape(host[1].shape), ro[0]]
+    prm = max(mixed_rel(a, b) for a, b in zip(g["params"], want))
+    upd = max(float(np.abs(a - b).max()) / max(float(np.abs(b - h).max()), 1e-30)
+              for a, b, h in zip(g["params"], want, host))
+    codes_want = [rt[1], rt[2], rs[1], rs[2], ro[1], ro[2]]
+    codes_eq = sum(int((a == b).sum()) for a, b in zip(g["codes"], codes_want)) / sum(b.size for b in codes_want)
+    parity = {
+        "counts_equal": bool(nv == ref["proj"]["num_visible"] and ni == ref["proj"]["num_isect"]),
+        "keys_equal": bool(np.array_equal(g["tile"], ref["binning"]["tile_ids"]) and
+                           np.array_equal(g["cid"], ref["binning"]["isect_compact"])),
+        "ranges_equal": bool(np.array_equal(g["ranges"].reshape(-1, 2), ref["tile_offsets_pre"]) and
+                             np.array_equal(g["used"], ref["tile_offsets"][:, 1])),
+        "img_max_rel": mixed_rel(g["img"], ref["out_img"]),
+        "img_px_over_1e-4": count_over(g["img"], ref["out_img"]),
+        "visible_equal": bool(np.array_equal(g["visible"], ref["visible"])),
+        "loss_rel": abs(g["loss"] - lo["loss"]) / max(abs(lo["loss"]), 1e-30),
+        "vcomb_max_rel": mixed_rel(vc_h, vc_ref),
+        "params_max_rel": prm, "update_max_rel": upd, "codes_equal_frac": round(codes_eq, 7),
+        "what": ("one step from the timed-region snapshot on the first view, GPU vs the C++ oracle; floats as "
+                 "max |got-want|/max(|want|, 1e-3 max|want|), update_max_rel = largest parameter-update "
+                 "difference over the largest update")}
+    cpu = {"value": round(1.0 / dt, 5), "unit": "iters/s", "cores": cores, "kind": "port",
+           "sample": "1 full configs[2] step of the C++ oracle (OpenMP) from the timed-region snapshot, the same "
+                     "step the parity check compares"}
+    leg.restore()
+    return parity, cpu
+
+
+def config_line(leg, value, ms_max, steps, warmup, launches, clocks, counts):
+    world, multiview = leg.world, leg.multiview
+    if multiview:
+        workload = dict(workload="configs[3]: 6M SH-3 splats, global batch of 8 views of 1920x1080 split over "
+                                 f"the GPUs ({len(leg.views)} per GPU), L1+0.2 D-SSIM, 8-bit m+v Adam (block 256)",
+                        splats=leg.splats.num_splats, width=1920, height=1080, views_per_step=8)
+    else:
+        workload = dict(workload="configs[2]: 3M SH-3 splats, 1600x1060, 1 view/step/GPU, L1+0.2 D-SSIM, "
+                                 + ("8-bit m+v Adam (block 256)" if leg.cfg.optimizer == "q8" else
+                                    "reference optimizer storage (packed 16/16 geometry moments, f16 SH, "
+                                    "int8 SH m in 128-value blocks)"),
+                        splats=leg.splats.num_splats, width=1600, height=1060, views_per_step=world)
+    return {"metric": ("view-parallel steps/s @6M splats, 8 views of 1920×1080 per step" if multiview else METRIC),
+            "value": round(value, 3), "unit": "steps/s" if multiview else "iters/s", "n_gpus": world,
+            "steps": steps, "warmup": warmup, "ms_per_step": round(ms_max / steps, 4),
+            "higher_is_better": True, "scaling": "strong" if multiview else "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {**workload, "optimizer": leg.cfg.optimizer,
+                       "parallelism": (f"view-parallel x{world}: dense gradient rows read over NVLink peer "
+                                       f"memory by a sharded fused Adam that stores to every replica"
+                                       if world > 1 or multiview else "single GPU"),
+                       "l2": ("inputs larger than L2 (params + moments ~%.1f GB)"
+                              % (leg.splats.num_splats * (236 + 122) / 1e9)), **counts},
+            "gpu_launches": int(launches), "clocks": clocks}
 
 
 def run_ours(args):
     import torch
     import torch.distributed as dist
-    from vauss_b200 import ops, scenes
-    from vauss_b200.trainer import SceneBatch, Splats, SplatTrainer, TrainConfig
-    from vauss_b200.view_parallel import ViewParallelTrainer, views_for_rank
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -195,210 +665,75 @@ def run_ours(args):
     dev = torch.device(f"cuda:{local}")
     torch.cuda.set_device(dev)
 
-    multiview = args.config == 3
-    if multiview and 8 % world:
-        raise SystemExit("config 3 splits its 8 views over 1, 2, 4 or 8 GPUs")
-    sp, tgt, cams = make_workload(args.splats, args.config)
-    splats = Splats.from_numpy(sp, dev)
-    # targets: rendered from the second splat set, quantised to RGBA8
-    tsplats = Splats.from_numpy(tgt, dev)
-    cfg_t = ops.render_cfg(3, mip=True)
-    if multiview:  # this rank's share of the fixed global batch
-        per_rank = 8 // world
-        views = [rank * per_rank + k for k in range(per_rank)]
-    else:
-        views = [(rank * N_TARGETS + k) % N_VIEWS for k in range(N_TARGETS)]
-    targets = []
-    for vi in views:
-        out = ops.render(cams[vi], cfg_t, tsplats.transforms, tsplats.sh_coeffs, tsplats.raw_opacities)
-        img = out.out_img[..., :3].clamp(0, 1).cpu().numpy()
-        targets.append(torch.from_numpy(scenes.pack_rgba8(img).view(np.int32)).to(dev))
-    del tsplats
-    torch.cuda.synchronize()
-
-    cfg = TrainConfig(optimizer="q8")
-    median_scale = float(np.median(np.exp(sp.transforms[:, 7:10])))
-    kw = dict(scene_extent=8.0, median_scale=median_scale)
-    peer = None
-    if world > 1 or multiview:
-        from vauss_b200.peer import PeerGroup, gather_bytes_nccl
-        gather = (lambda b: gather_bytes_nccl(b, dev)) if world > 1 else (lambda b: [b])
-        peer = PeerGroup(dev, world, rank, gather)
-        trainer = ViewParallelTrainer(cfg, dev, peer=peer, **kw)
-        splats = trainer.adopt(splats)
-    else:
-        trainer = SplatTrainer(cfg, dev, **kw)
-
-    def step(k, loader=None):
-        if multiview:
-            batches = ([loader.next_batch() for _ in views] if loader else
-                       [SceneBatch(targets[j], cams[views[j]], views[j]) for j in range(len(views))])
-            return trainer.step_views(batches, splats)
-        vi = k % N_TARGETS
-        b = loader.next_batch() if loader else SceneBatch(targets[vi], cams[views[vi]], views[vi])
-        if world > 1:
-            return trainer.step_views([b], splats)
-        return trainer.step(b, splats)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    counts = {}
-    for k in range(args.warmup):
-        _, st0 = step(k)
-        counts = {"visible": int(st0.num_visible), "intersections": int(st0.num_intersections)}
-    barrier()
-    # The timed region starts from this state; the per-stage profile and the
-    # end-to-end leg restart from it too, so that all three measure the same
-    # workload (training moves the splats, and the raster work grows with it).
-    import copy
-    moments = ("m_codes", "v_codes", "m_scales", "v_scales")
-    snap = {"p": [x.clone() for x in (splats.transforms, splats.sh_coeffs, splats.raw_opacities)],
-            "m": {k: [getattr(trainer.optim[k], a).clone() for a in moments] for k in ("t", "sh", "o")},
-            "time": trainer.optim["time"], "step": trainer.step_count,
-            "rng": copy.deepcopy(trainer.rng.bit_generator.state)}
-
-    def restore():
-        for dst, src in zip((splats.transforms, splats.sh_coeffs, splats.raw_opacities), snap["p"]):
-            dst.copy_(src)
-        for k in ("t", "sh", "o"):
-            for a, src in zip(moments, snap["m"][k]):
-                getattr(trainer.optim[k], a).copy_(src)
-        trainer.optim["time"], trainer.step_count = snap["time"], snap["step"]
-        trainer.rng.bit_generator.state = copy.deepcopy(snap["rng"])
-        barrier()
-    ctx = ops.context(dev)
-    launches0 = ctx.launch_count
-    gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
-    gpu_id = gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}"
-    stream = torch.cuda.current_stream(dev)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(gpu_id) as clk:
-        barrier()
-        clk.mark("start")
-        e0.record(stream)
-        for k in range(args.steps):
-            step(args.warmup + k)
-        e1.record(stream)
-        barrier()
-        clk.mark("stop")
-    ms = e0.elapsed_time(e1)
-    launches = (ctx.launch_count - launches0) // max(args.steps, 1)
-    t = torch.tensor([ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = (1 if multiview else world) * args.steps / (ms_max / 1e3)
-
-    # ---- end to end through the public API: host GT in, loss out ----
-    e2e = None
+    leg = Leg(args, args.config, args.splats, world, rank, dev)
+    ms_max, launches, clocks, counts = timed_run(leg, args.steps, args.warmup)
+    value = (1 if leg.multiview else world) * args.steps / (ms_max / 1e3)
+    out = config_line(leg, value, ms_max, args.steps, args.warmup, launches, clocks, counts)
     if not args.no_e2e:
-        from vauss_b200 import dataset
-        # the views as decoded RGB host images: the staged loader copies one
-        # (per view of the step) from pinned memory every step and packs it
-        rgb = [tg.cpu().numpy().view(np.uint8).reshape(tg.shape[0], tg.shape[1], 4)[..., :3].copy()
-               for tg in targets]
-        loader = dataset.SceneLoader(
-            dataset.Scene([dataset.SceneView(img, cams[vi]) for img, vi in zip(rgb, views)]), seed=rank,
-            config=dataset.LoadDatasetConfig(max_scene_batch_cache_size=0), device=dev,
-            hold=len(views) if multiview else 1)
-        loss_host = torch.empty((), dtype=torch.float32).pin_memory()
-        for k in range(args.warmup):  # untimed: first use of the host-input path
-            _, st = step(k, loader=loader)
-            loss_host.copy_(st.loss, non_blocking=True)
-        restore()
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        h2d0 = loader.h2d_bytes_total
-        f0.record(stream)
-        for k in range(args.steps):
-            _, st = step(k, loader=loader)
-            loss_host.copy_(st.loss, non_blocking=True)
-        f1.record(stream)
-        barrier()
-        ems = f0.elapsed_time(f1)
-        h2d_total = loader.h2d_bytes_total - h2d0
-        loader.close()
-        te = torch.tensor([ems], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(te, op=dist.ReduceOp.MAX)
-        e2e = {"value": (1 if multiview else world) * args.steps / (float(te.item()) / 1e3),
-               "unit": "steps/s" if multiview else "iters/s",
-               "h2d_bytes_per_step": int(round(h2d_total / max(args.steps, 1))), "d2h_bytes_per_step": 4,
-               "feed": "SceneLoader (vs_feed): RGB8 views, pinned ring of 4, packed on the GPU, no cache",
-               "api": ("ViewParallelTrainer.step_views (vs_render_forward, vs_loss, vs_rasterize_backward, "
-                       "vs_vjp_dense, vs_peer_barrier, vs_adam_q8_peer)" if world > 1 else
-                       "SplatTrainer.step (vs_render_forward, vs_loss, vs_rasterize_backward, vs_step_q8)")}
+        e2e = e2e_run(leg, args.steps, args.warmup)
+        out["e2e"] = {k: (round(v, 3) if isinstance(v, float) else v) for k, v in e2e.items()}
+    if world > 1:
+        out["replicas_equal"] = replicas_check(leg)  # after every timed and end-to-end step
 
     # ---- per-stage device times (CUDA events on the launching stream) ----
-    stages = None
-    roofline = None
-    if world == 1 and not multiview:
-        restore()
-        stages = profile_stages(trainer, splats, targets, cams, views, dev, reps=5)
+    if world == 1 and not leg.multiview:
+        leg.restore()
+        stages = profile_stages(leg.trainer, leg.splats, leg.targets, leg.cams, leg.views, dev, reps=5)
         peak, which = peaks()
-        n, v, i = splats.num_splats, stages.pop("_v"), stages.pop("_i")
-        cam0 = cams[views[0]]
+        n, v, i = leg.splats.num_splats, stages.pop("_v"), stages.pop("_i")
+        cam0 = leg.cams[leg.views[0]]
         p, tcount = cam0.width * cam0.height, cam0.num_tiles
         for name, d in stages.items():
-            b = stage_bytes(name, n, v, i, p, tcount)
+            b = stage_bytes(name if not (name == "optimizer" and leg.cfg.optimizer == "reference")
+                            else "optimizer_reference", n, v, i, p, tcount)
             d["gbs"] = b / (d["ms"] / 1e3) / 1e9
             d["alg_bytes"] = b
         dom = max(stages, key=lambda k: stages[k]["ms"])
         ach = stages[dom]["gbs"]
-        roofline = {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                    "frac": round(ach / peak, 4),
-                    "traffic": (MEASURED_TRAFFIC_CONFIG2.get(dom) if n == N_SPLATS else None), "peak_source": which,
-                    "note": "raster stages are FP32-issue bound; see profiles/ for issue utilisation"}
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not multiview:
-        cpu = cpu_baseline(sp, tgt, cams, views, gt=targets[0].cpu().numpy().view(np.uint32))
-
-    if multiview:
-        workload = dict(workload="config 3: 6M SH-3 splats, global batch of 8 views of 1920x1080 split over the "
-                                 f"GPUs ({len(views)} per GPU), L1+0.2 D-SSIM, 8-bit m+v Adam (block 256)",
-                        splats=splats.num_splats, width=1920, height=1080, views_per_step=8)
+        out["roofline"] = {"bound": "hbm", "kernel": dom, "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                           "frac": round(ach / peak, 4),
+                           "traffic": (MEASURED_TRAFFIC_CONFIG2.get(dom) if n == N_SPLATS else None),
+                           "peak_source": which,
+                           "note": "raster stages are FP32-issue bound; see profiles/ for issue utilisation"}
+        out["stages"] = {k: {"ms": round(d["ms"], 4), "gbs": round(d["gbs"], 1), "frac": round(d["gbs"] / peak, 4)}
+                         for k, d in stages.items()}
     else:
-        workload = dict(workload="config 2: 3M SH-3 splats, 1600x1060, 1 view/step/GPU, L1+0.2 D-SSIM, "
-                                 "8-bit m+v Adam (block 256)", splats=splats.num_splats, width=1600, height=1060,
-                        views_per_step=world)
-    out = {"metric": ("view-parallel steps/s @6M splats, 8 views of 1920×1080 per step" if multiview else METRIC),
-           "value": round(value, 3), "unit": "steps/s" if multiview else "iters/s", "n_gpus": world,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
-           "higher_is_better": True, "scaling": "strong" if multiview else "weak", "vs_baseline": None,
-           "dtype": "f32", "data": "synthetic",
-           "config": {**workload, "optimizer": "q8",
-                      "parallelism": (f"view-parallel x{world}: dense gradient rows read over NVLink peer "
-                                      f"memory by a sharded fused Adam that stores to every replica"
-                                      if world > 1 or multiview else "single GPU"),
-                      "l2": ("inputs larger than L2 (params + moments ~%.1f GB)"
-                             % (splats.num_splats * (236 + 122) / 1e9)), **counts},
-           "gpu_launches": int(launches), "clocks": clk.summary()}
-    if roofline:
-        out["roofline"] = roofline
-    if stages:
-        out["stages"] = {k: {"ms": round(d["ms"], 4), "gbs": round(d["gbs"], 1)} for k, d in stages.items()}
-    if cpu:
+        leg.restore()
+        out["stages"] = profile_stages_views(leg)
+        if world > 1:
+            out["stages_note"] = "per stage the median of 5 steps on each rank, then the maximum over ranks"
+    if world > 1 and not args.no_check:
+        out["exchange_check"] = exchange_check(leg)
+    if rank == 0 and world == 1 and not leg.multiview and not args.no_cpu_baseline and \
+            leg.cfg.optimizer == "q8":
+        parity, cpu = parity_leg(leg)
+        out["parity"] = parity
         out["cpu_baseline"] = cpu
-    if e2e:
-        out["e2e"] = {k: (round(v, 3) if isinstance(v, float) else v) for k, v in e2e.items()}
+    leg.close()
+    del leg
+    torch.cuda.empty_cache()
+
+    # ---- configuration 3 (strong scaling) as a companion of the scaling run ----
+    if args.config == 2 and not args.no_config3 and args.optimizer == "q8":
+        c3 = Leg(args, 3, 6_000_000, world, rank, dev)
+        k3, w3 = max(3, min(args.steps, 10)), 3
+        ms3, _, clk3, cnt3 = timed_run(c3, k3, w3)
+        rec = {"steps_per_s": round(k3 / (ms3 / 1e3), 3), "ms_per_step": round(ms3 / k3, 3), "n_gpus": world,
+               "steps": k3, "warmup": w3, "splats": c3.splats.num_splats, "views_per_step": 8,
+               "views_per_gpu": len(c3.views), "scaling": "strong", "clocks": clk3, **cnt3}
+        if not args.no_e2e:
+            e = e2e_run(c3, k3, w3)
+            rec["e2e"] = {"value": round(e["value"], 3), "unit": e["unit"],
+                          "h2d_bytes_per_step": e["h2d_bytes_per_step"], "d2h_bytes_per_step": 4}
+        if world > 1:
+            rec["replicas_equal"] = replicas_check(c3)
+        c3.close()
+        out["config3"] = rec
     if rank == 0:
         print(json.dumps(out), flush=True)
-    if world == 1 and peer is not None:
-        torch.cuda.synchronize(dev)
-        peer.check()
-        peer.close()
     if world > 1:
         dist.barrier()
         torch.cuda.synchronize(dev)
-        dist.barrier()  # no rank's kernels touch peer buffers any more
-        if peer is not None:
-            peer.check()
-            peer.close()
-        torch.cuda.synchronize(dev)
-        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -417,7 +752,8 @@ def profile_stages(trainer, splats, targets, cams, views, dev, reps=5):
     for r in range(reps):
         vi = r % len(targets)
         cam = cams[views[vi]]
-        cfg = ops.render_cfg(3, mip=True, background=(0.0, 0.0, 0.0))
+        cfg = ops.render_cfg(3, mip=True, sh_half=splats.sh_coeffs.dtype == torch.float16,
+                             background=(0.0, 0.0, 0.0))
         evs = [("start", torch.cuda.Event(enable_timing=True))]
         evs[0][1].record(stream)
 
@@ -436,12 +772,17 @@ def profile_stages(trainer, splats, targets, cams, views, dev, reps=5):
         hook("raster_bwd")
         o = trainer.optim
         o["time"] += 1
-        q8 = ops.q8_cfg(o["time"], trainer.transforms_lr(), c.lr_coeffs_dc, c.lr_coeffs_dc / c.lr_coeffs_sh_scale,
-                        c.lr_opac, eps=c.adam_epsilon, noise_scale=1e-7, noise_limit=1e-3, noise_seed=r)
-        rec = trainer.record
-        ops.step_q8(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, o["t"], o["sh"],
-                    o["o"], q8, visible=out.visible, refine_norm=rec.refine_norm, vis_count=rec.vis_count,
-                    max_screen=rec.max_screen)
+        if c.optimizer == "q8":
+            q8 = ops.q8_cfg(o["time"], trainer.transforms_lr(), c.lr_coeffs_dc,
+                            c.lr_coeffs_dc / c.lr_coeffs_sh_scale, c.lr_opac, eps=c.adam_epsilon, noise_scale=1e-7,
+                            noise_limit=1e-3, noise_seed=r)
+            rec = trainer.record
+            ops.step_q8(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, o["t"],
+                        o["sh"], o["o"], q8, visible=out.visible, refine_norm=rec.refine_norm,
+                        vis_count=rec.vis_count, max_screen=rec.max_screen)
+        else:  # the reference optimizer storage: fused project_update + SH step + stats + noise
+            cfg = ops.render_cfg(3, mip=True, sh_half=True, background=(0.0, 0.0, 0.0))
+            trainer._reference_optimizer_step(out, cfg, splats, vc, trainer.transforms_lr(), 0.0, o["time"], 1e-7, r)
         hook("optimizer")
         torch.cuda.synchronize()
         for (a, ea), (b, eb) in zip(evs[:-1], evs[1:]):
@@ -504,7 +845,7 @@ def cpu_baseline(sp, tgt, cams, views, steps=1, warmup=0, gt=None):
         oracle_step(sp, cam, gt, mom, warmup + k + 1)
     dt = (time.perf_counter() - t0) / steps
     return {"value": round(1.0 / dt, 5), "unit": "iters/s", "cores": cores, "kind": "port",
-            "sample": f"{steps} full config-2 step(s) of the C++ oracle (OpenMP), after {warmup} warm-up"}
+            "sample": f"{steps} full configs[2] step(s) of the C++ oracle (OpenMP), after {warmup} warm-up"}
 
 
 def run_reference(args):
@@ -520,21 +861,158 @@ def run_reference(args):
     steps = max(1, min(args.steps, 2))
     warm = min(args.warmup, 1)
     cpu = cpu_baseline(sp, tgt, cams, views, steps=steps, warmup=warm)
-    cpu["sample"] = (f"{steps} timed full config-2 step(s) (after {warm} warm-up) of the C++ oracle restating the "
+    cpu["sample"] = (f"{steps} timed full configs[2] step(s) (after {warm} warm-up) of the C++ oracle restating the "
                      f"reference kernels; the Rust/CubeCL reference cannot be built in this image")
     out = {"metric": METRIC, "value": cpu["value"], "unit": "iters/s", "n_gpus": world, "steps": steps,
            "warmup": warm, "ms_per_step": round(1e3 / cpu["value"], 2), "higher_is_better": True, "scaling": "weak",
            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-           "config": {"workload": "config 2: 3M SH-3 splats, 1600x1060, 1 view/step, L1+0.2 D-SSIM, 8-bit m+v Adam",
+           "config": {"workload": "configs[2]: 3M SH-3 splats, 1600x1060, 1 view/step/GPU, L1+0.2 D-SSIM, 8-bit m+v Adam (block 256)",
                       "splats": args.splats},
            "cpu_baseline": cpu,
            "e2e": {"value": cpu["value"], "unit": "iters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
 
+def run_microbench(args):
+    """BASELINE.json configs[1], the single-view render forward + backward
+    microbench: 1M SH-3 splats (means U[-3,3]^3, log-scales N(-4.5, 0.6),
+    opacity logits N(0, 1.5)), one 1920x1080 pinhole view at distance 6,
+    fx = fy = 1600, upstream image gradient N(0, 1e-3) per pixel and channel.
+    One step = projection, binning, rasterize forward, rasterize backward;
+    value = steps/s.  Both raster kernels get a roofline entry, and the CPU
+    oracle's forward + backward of the same view is the parity check and the
+    CPU baseline.  One view: under torchrun only rank 0 runs."""
+    import torch
+    import oracle
+    from vauss_b200 import ops, scenes
+    from vauss_b200.trainer import Splats
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    sp, cam = scenes.config_microbench(n=args.splats)
+    n = sp.n
+    splats = Splats.from_numpy(sp, dev)
+    frame = ops.Frame(ops.context(dev))
+    cfg = ops.render_cfg(3, mip=True)
+    img = torch.empty(cam.height, cam.width, 4, device=dev)
+    vis = torch.empty(n, device=dev)
+    vc = torch.empty(n, 10, device=dev)
+    v_host = (np.random.default_rng(11).standard_normal((cam.height, cam.width, 4)) * 1e-3).astype(np.float32)
+    v_out = torch.from_numpy(v_host).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(hook=None, upstream=v_out):
+        out = ops.render_stages(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, frame, img, vis,
+                                hook=hook)
+        r = ops.rasterize_bwd(out.frame, out.out_img, upstream, vc)
+        if hook:
+            hook("raster_bwd")
+        return r
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ctx = ops.context(dev)
+    l0 = ctx.launch_count
+    gpu_uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else f"GPU-{gpu_uuid}") as clk:
+        torch.cuda.synchronize()
+        clk.mark("start")
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        clk.mark("stop")
+    ms = e0.elapsed_time(e1)
+    launches = (ctx.launch_count - l0) // max(args.steps, 1)
+    # per-stage medians
+    acc = {}
+    for _ in range(5):
+        evs = [("start", torch.cuda.Event(enable_timing=True))]
+        evs[0][1].record(stream)
+
+        def hook(name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record(stream)
+            evs.append((name, e))
+        step(hook)
+        torch.cuda.synchronize()
+        for (_, ea), (b, eb) in zip(evs[:-1], evs[1:]):
+            acc.setdefault(b, []).append(ea.elapsed_time(eb))
+    nv, ni = frame.num_visible, frame.num_intersections
+    p, tcount = cam.width * cam.height, cam.num_tiles
+    peak, which = peaks()
+    stages, roof = {}, {}
+    for k, t in acc.items():
+        m = statistics.median(t)
+        b = stage_bytes(k, n, nv, ni, p, tcount)
+        stages[k] = {"ms": round(m, 4), "gbs": round(b / (m / 1e3) / 1e9, 1), "frac": round(b / (m / 1e3) / 1e9 / peak, 4)}
+        if k in ("raster_fwd", "raster_bwd"):
+            roof[k] = {"bound": "hbm", "kernel": k + "_kernel", "achieved": stages[k]["gbs"], "peak": peak,
+                       "unit": "GB/s", "frac": stages[k]["frac"], "traffic": None, "peak_source": which,
+                       "alg_bytes": b}
+    # end to end: the upstream gradient from pinned host memory each step, a scalar of the result read back
+    pinned = torch.from_numpy(v_host).pin_memory()
+    dst = torch.empty_like(v_out)
+    res_host = torch.empty((), dtype=torch.float32).pin_memory()
+    for _ in range(3):
+        dst.copy_(pinned, non_blocking=True)
+        res_host.copy_(step(upstream=dst).sum(), non_blocking=True)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        dst.copy_(pinned, non_blocking=True)
+        res_host.copy_(step(upstream=dst).sum(), non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e = {"value": round(args.steps / (f0.elapsed_time(f1) / 1e3), 3), "unit": "steps/s",
+           "h2d_bytes_per_step": int(v_out.numel() * 4), "d2h_bytes_per_step": 4,
+           "api": "vs_render_project/bin/rasterize + vs_rasterize_backward (ops.render_stages, ops.rasterize_bwd)"}
+    out = {"metric": "single-view render fwd+bwd steps/s @1M splats 1920×1080; raster fwd/bwd HBM GB/s vs peak",
+           "value": round(args.steps / (ms / 1e3), 3), "unit": "steps/s", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+           "scaling": "replicas only", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": "configs[1]: 1M SH-3 splats, one 1920x1080 view at distance 6, fx=fy=1600, "
+                                  "Mip mode, upstream gradient N(0,1e-3)", "splats": n, "visible": nv,
+                      "intersections": ni, "l2": "inputs larger than L2 (params 236 MB, image + gradient 66 MB)"},
+           "gpu_launches": int(launches), "clocks": clk.summary(), "stages": stages,
+           "roofline": roof["raster_bwd"], "roofline_raster": roof, "e2e": e2e}
+    if not args.no_cpu_baseline:
+        cores = oracle.set_num_threads(os.cpu_count() or 1)
+        t0 = time.perf_counter()
+        cfg_o = oracle.make_cfg(3, mip=True)
+        ref = oracle.render_forward(cam, cfg_o, sp)
+        vc_ref = oracle.raster_bwd(cam, (0.0, 0.0, 0.0), ref["proj"], ref["binning_after"], ref["out_img"], v_host)
+        dt = time.perf_counter() - t0
+        step()
+        torch.cuda.synchronize()
+        g_img, g_vc = img.cpu().numpy(), vc[:nv].cpu().numpy()
+        out["parity"] = {
+            "counts_equal": bool(nv == ref["proj"]["num_visible"] and ni == ref["proj"]["num_isect"]),
+            "keys_equal": bool(np.array_equal(frame.field("isect_tile").cpu().numpy().view(np.uint32),
+                                              ref["binning"]["tile_ids"]) and
+                               np.array_equal(frame.field("isect_compact").cpu().numpy().view(np.uint32),
+                                              ref["binning"]["isect_compact"])),
+            "ranges_equal": bool(np.array_equal(frame.field("tile_ranges").cpu().numpy().view(np.uint32).reshape(-1, 2),
+                                                ref["tile_offsets_pre"]) and
+                                 np.array_equal(frame.field("tile_used_end").cpu().numpy().view(np.uint32),
+                                                ref["tile_offsets"][:, 1])),
+            "img_max_rel": mixed_rel(g_img, ref["out_img"]), "img_px_over_1e-4": count_over(g_img, ref["out_img"]),
+            "visible_equal": bool(np.array_equal(vis.cpu().numpy(), ref["visible"])),
+            "vcomb_max_rel": mixed_rel(g_vc, vc_ref), "vcomb_over_1e-4": count_over(g_vc, vc_ref)}
+        out["cpu_baseline"] = {"value": round(1.0 / dt, 5), "unit": "steps/s", "cores": cores, "kind": "port",
+                               "sample": "1 forward + backward of the same view by the C++ oracle (OpenMP)"}
+    print(json.dumps(out), flush=True)
+
+
+
 def run_sort_stress(args):
     """Benchmark configuration 4 (sort/overlap stress): 10M splats with large
-    footprints (log-scales N(-2.5, 0.5), opacity logits N(1, 1), config-2
+    footprints (log-scales N(-2.5, 0.5), opacity logits N(1, 1), configs[2]
     means and SH), one 3840x2160 view, fx = fy = 3000.  Times projection,
     binning (intersection emission, depth and tile radix sorts, tile ranges),
     the forward and the backward under an N(0, 1e-3) upstream gradient.  The
@@ -553,7 +1031,6 @@ def run_sort_stress(args):
                               opac_mu=1.0, opac_sigma=1.0, sh_degree=3)
     cam = look_at((0.0, -3.0, 8.0), (0.0, 0.0, 0.0), 3840, 2160, 3000.0)
     splats = Splats.from_numpy(sp, dev)
-    del sp
     frame = ops.Frame(ops.context(dev))
     cfg = ops.render_cfg(3, mip=True)
     img = torch.empty(cam.height, cam.width, 4, device=dev)
@@ -599,7 +1076,7 @@ def run_sort_stress(args):
            "value": round(isect / (sort_ms / 1e3), 1), "unit": "intersections/s", "n_gpus": 1, "steps": args.steps,
            "warmup": args.warmup, "ms_per_step": round(sum(ms.values()), 3), "higher_is_better": True,
            "scaling": "replicas only", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-           "config": {"workload": "config 4: 10M SH-3 splats, log-scales N(-2.5,0.5), opacity logits N(1,1), one "
+           "config": {"workload": "configs[4]: 10M SH-3 splats, log-scales N(-2.5,0.5), opacity logits N(1,1), one "
                                   "3840x2160 view, fx=fy=3000, project+bin+raster fwd+raster bwd (N(0,1e-3) upstream)",
                       "splats": n, "visible": visible, "intersections": isect,
                       "l2": "inputs larger than L2"},
@@ -608,13 +1085,54 @@ def run_sort_stress(args):
                         "peak": peak, "unit": "GB/s", "frac": round(bin_bytes / (ms["bin"] / 1e3) / 1e9 / peak, 4),
                         "traffic": None, "peak_source": which},
            "clocks": clk.summary()}
+    if not args.no_cpu_baseline:
+        out["checks"] = sort_stress_checks(frame, cam, cfg, sp)
     print(json.dumps(out), flush=True)
+
+
+def sort_stress_checks(frame, cam, cfg, sp):
+    """Checks of the last render at full size: the projection (visible set,
+    per-splat tile counts, depths) against the CPU oracle's bit for bit, and
+    size-independent properties of the binning (keys sorted by (tile, depth),
+    the tile ranges partition the list, every splat emitted exactly its tile
+    count, and the total equals the sum of the counts)."""
+    import torch
+    import oracle
+    oracle.set_num_threads(os.cpu_count() or 1)
+    ref = oracle.project(cam, oracle.make_cfg(3, mip=True), sp.transforms, sp.sh, sp.raw_opac)
+    nv, ni = frame.num_visible, frame.num_intersections
+    res = {"counts_equal": bool(nv == ref["num_visible"] and ni == ref["num_isect"]),
+           "compact_from_global_equal": bool(np.array_equal(
+               frame.field("compact_from_global").cpu().numpy().view(np.uint32), ref["compact_from_global"])),
+           "tile_counts_equal": bool(np.array_equal(frame.field("tile_counts").cpu().numpy().view(np.uint32),
+                                                    ref["tile_counts_compact"])),
+           "depths_equal": bool(np.array_equal(frame.field("depths").cpu().numpy().view(np.uint32),
+                                               ref["depths"].view(np.uint32)))}
+    del ref
+    tiles = frame.field("isect_tile").long()
+    cid = frame.field("isect_compact").long()
+    dbits = frame.field("depths").view(torch.int32).long()[cid]
+    res["keys_sorted"] = bool(((tiles[1:] > tiles[:-1]) | ((tiles[1:] == tiles[:-1]) & (dbits[1:] >= dbits[:-1])))
+                              .all().item())
+    del dbits
+    T = cam.num_tiles
+    hist = torch.bincount(tiles, minlength=T)
+    rng = frame.field("tile_ranges").long().view(-1, 2)
+    starts = torch.cumsum(hist, 0) - hist
+    res["ranges_partition"] = bool(torch.equal(rng[:, 0], starts) and torch.equal(rng[:, 1] - rng[:, 0], hist))
+    per = torch.bincount(cid, minlength=nv)
+    res["emitted_equals_counts"] = bool(torch.equal(per, frame.field("tile_counts").long()))
+    res["total_equals_sum"] = bool(int(frame.field("tile_counts").long().sum().item()) == ni)
+    res["what"] = "projection vs the C++ oracle (bit-exact); binning invariants on the GPU at full size"
+    return res
 
 
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == 1:
+        run_microbench(args)
     elif args.config == 4:
         run_sort_stress(args)
     else:

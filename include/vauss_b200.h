@@ -417,7 +417,8 @@ VS_API vs_status vs_radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* valu
  * up (cudaGetSymbolAddress, which can load the module): make that call before
  * any stream capture on that device.  Nothing in the array has to start at
  * zero.  The array is shared by all calls on a device, so calls that overlap
- * on the GPU (other streams or threads) race; the caller serialises them. */
+ * on the GPU (other streams or threads) race; the caller serialises them.
+ * The calling thread's current CUDA device is the same on return. */
 #define VS_SORT_STATIC_MAX_KEYS (1u << 20)
 VS_API vs_status vs_radix_sort_pairs_static(vs_ctx* ctx, uint32_t* keys, uint32_t* values, uint32_t count,
                                             uint32_t key_bits);

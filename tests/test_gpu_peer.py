@@ -134,3 +134,46 @@ def test_barrier_wait_runs_out_with_an_error(cuda):
     # the context stays usable, and the error word was cleared
     assert _barrier(ctx, [mine], 1, 0, 2) == 0
     assert ctx.lib.vs_ctx_check(ctx.h) == 0
+
+
+def test_peer_adam_after_a_barrier_that_gave_up_touches_nothing(cuda):
+    """A barrier whose wait ran out leaves VS_DERR_WAIT in the device error
+    word; the sharded update launched after it must then neither read the
+    peers' (possibly incomplete) rows nor store into any replica."""
+    world, n, nc = 2, 700, 16
+    width = 10 + nc * 3 + 1
+    rng = np.random.default_rng(31)
+    t0 = rng.standard_normal((n, 10)).astype(np.float32)
+    sh0 = (0.3 * rng.standard_normal((n, nc, 3))).astype(np.float32)
+    o0 = rng.standard_normal(n).astype(np.float32)
+    reps = [[torch.from_numpy(x.copy()).to(cuda) for x in (t0, sh0, o0)] for _ in range(world)]
+    g_dev = [torch.from_numpy((1e-3 * rng.standard_normal((n, width))).astype(np.float32)).to(cuda)
+             for _ in range(world)]
+    v_dev = [torch.ones(n, device=cuda) for _ in range(world)]
+    ps = N.PeerSet()
+    ps.world, ps.rank = world, 0
+    for r in range(world):
+        ps.grads[r], ps.vis[r] = g_dev[r].data_ptr(), v_dev[r].data_ptr()
+        ps.transforms[r], ps.sh_coeffs[r], ps.raw_opacities[r] = (x.data_ptr() for x in reps[r])
+    b, e = ViewParallelTrainer.shard_of(n, world, 0)
+    mom = {k: _q8_host(c, rng) for k, c in (("t", (e - b) * 10), ("sh", (e - b) * nc * 3), ("o", e - b))}
+    dm = {k: _q8_dev(v, cuda) for k, v in mom.items()}
+    q8 = ops.q8_cfg(3, np.float32([1e-3] * 10), 2.5e-3, 2.5e-4, 5e-2)
+    ctx = ops.context(cuda)
+    mine, other = _flags(cuda, 0, 0), _flags(cuda, 0, 0)  # rank 1 never signals
+    assert _barrier(ctx, [mine, other], world, 0, 1) == 0
+    ops.adam_q8_peer(3, n, b, e, ps, dm["t"], dm["sh"], dm["o"], q8, device=cuda)
+    torch.cuda.synchronize()
+    for r in range(world):
+        assert_bits_equal(_np(reps[r][0]), t0, f"transforms replica {r}")
+        assert_bits_equal(_np(reps[r][1]), sh0, f"sh replica {r}")
+        assert_bits_equal(_np(reps[r][2]), o0, f"opacity replica {r}")
+    for k, h in mom.items():
+        assert_bits_equal(_np(dm[k].m_codes), h["mc"], f"{k} m codes")
+        assert_bits_equal(_np(dm[k].v_scales), h["vs"], f"{k} v scales")
+    assert ctx.lib.vs_ctx_check(ctx.h) == 4  # VS_ERR_DEVICE_TIMEOUT, and the word is cleared
+    # with the word clear, the same launch updates the replicas again
+    ops.adam_q8_peer(3, n, b, e, ps, dm["t"], dm["sh"], dm["o"], q8, device=cuda)
+    torch.cuda.synchronize()
+    assert not np.array_equal(_np(reps[1][0])[:e], t0[:e])
+    assert ctx.lib.vs_ctx_check(ctx.h) == 0

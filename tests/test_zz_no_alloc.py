@@ -54,3 +54,25 @@ def test_static_sort_rejects_oversize(cuda):
     assert b"static scratch limit" in ctx.lib.vs_ctx_last_error(ctx.h)
     with pytest.raises(_native.VsError):
         ctx.check(st)
+
+
+def test_static_sort_allocates_nothing(cuda):
+    """The property the entry point exists for: after a first call (which
+    looks the static array up), further calls leave the context's workspace
+    and the device's free memory exactly as they were."""
+    ctx = ops.context(cuda)
+    count = 200_000
+    rng = np.random.default_rng(3)
+    keys = torch.from_numpy(rng.integers(0, 1 << 31, count, dtype=np.uint64).astype(np.uint32).view(np.int32))
+    keys = keys.to(cuda)
+    vals = torch.arange(count, dtype=torch.int32, device=cuda)
+    assert ctx.lib.vs_radix_sort_pairs_static(ctx.h, _ptr(keys), _ptr(vals), count, 32) == 0
+    torch.cuda.synchronize()
+    ws = ctx.workspace_bytes
+    free0 = torch.cuda.mem_get_info(cuda)[0]
+    for _ in range(2):
+        assert ctx.lib.vs_radix_sort_pairs_static(ctx.h, _ptr(keys), _ptr(vals), count, 32) == 0
+    torch.cuda.synchronize()
+    assert ctx.workspace_bytes == ws
+    assert torch.cuda.mem_get_info(cuda)[0] == free0
+    assert torch.cuda.current_device() == cuda.index

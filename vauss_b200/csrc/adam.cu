@@ -383,6 +383,9 @@ struct Q8Args {
 // zero offsets otherwise.
 struct PeerArgs {
   uint32_t world, rank;
+  // the ctx's device error word: a barrier before this launch that gave up
+  // sets VS_DERR_WAIT there, and the update then touches nothing
+  const uint32_t* err;
   uint32_t cta_begin;  // first CTA (256 splats) of the shard
   uint32_t m_off;      // first splat covered by the moment arrays
   const float* grads[VS_PEER_MAX];
@@ -646,6 +649,9 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
   constexpr bool kDense = MODE != 0;
 
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
+  // After a barrier that gave up, the peers' rows may be incomplete and other
+  // ranks may still read this replica: no peer load or store, no update.
+  if (MODE == 2 && (*(volatile const uint32_t*)pa.err & VS_DERR_WAIT)) return;
   const uint32_t base = ((MODE == 2 ? pa.cta_begin : 0u) + blockIdx.x) * Q8_SPLATS;
   if (tid == 0) {
 #pragma unroll
@@ -971,6 +977,7 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
   PeerArgs pa{};
   pa.world = peers->world;
   pa.rank = peers->rank;
+  pa.err = ctx->d_err;
   pa.cta_begin = splat_begin / Q8_SPLATS;
   pa.m_off = splat_begin;
   for (uint32_t r = 0; r < peers->world; ++r) {

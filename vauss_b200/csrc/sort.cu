@@ -236,8 +236,11 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_apply_kernel(uint32_t* __re
 // once, then warp 0 walks back over the status words, 32 at a time, to the
 // nearest inclusive prefix (flag 2), publishes its own inclusive prefix and
 // the chunk writes its values.  Status word: flag in the high half (1 =
-// chunk sum, 2 = inclusive prefix), value in the low half.  Waits are bounded:
-// a walk that gives up sets VS_DERR_WAIT and the chunk writes nothing.
+// chunk sum, 2 = inclusive prefix, 3 = failed), value in the low half.  Waits
+// are bounded: a walk that gives up sets VS_DERR_WAIT, publishes flag 3 and the
+// chunk writes nothing; a walk that meets flag 3 before its nearest inclusive
+// prefix fails the same way, so no later chunk writes values built on a
+// prefix that was never formed.
 constexpr uint32_t SCAN_SPIN_LIMIT = 1u << 22;
 
 __device__ __forceinline__ unsigned long long scan_status_load(unsigned long long* p) {
@@ -288,8 +291,16 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_lookback_kernel(uint32_t* _
         const uint32_t flag = (uint32_t)(st >> 32);
         const uint32_t incl = __ballot_sync(0xffffffffu, flag == 2u);
         const uint32_t pending = __ballot_sync(0xffffffffu, flag == 0u);
+        const uint32_t failed = __ballot_sync(0xffffffffu, flag == 3u);
         const uint32_t first = incl ? (uint32_t)(__ffs(incl) - 1) : 32u;
         const uint32_t needed = first >= 31u ? 0xffffffffu : ((2u << first) - 1u);
+        if (failed & needed) {  // an earlier chunk gave up: its prefix never formed
+          if (lane == 0) {
+            atomicOr(err, VS_DERR_WAIT);
+            s_fail = 1u;
+          }
+          break;
+        }
         if (pending & needed) {
           if (++spins > SCAN_SPIN_LIMIT) {
             if (lane == 0) {
@@ -308,11 +319,13 @@ __global__ void __launch_bounds__(SCAN_THREADS) scan_lookback_kernel(uint32_t* _
         if (first < 32u) break;
         hi -= 32;
       }
-      if (lane == 0) scan_status_store(&status[chunk], (2ull << 32) | (exclusive + total));
+      __syncwarp();
+      if (lane == 0)
+        scan_status_store(&status[chunk], s_fail ? (3ull << 32) : ((2ull << 32) | (exclusive + total)));
     }
     if (lane == 0) {
       s_prefix = exclusive;
-      if (chunk == nchunks - 1 && total_dev) *total_dev = (unsigned long long)exclusive + total;
+      if (chunk == nchunks - 1 && total_dev && !s_fail) *total_dev = (unsigned long long)exclusive + total;
     }
   }
   __syncthreads();
@@ -457,6 +470,15 @@ extern "C" VS_API vs_status vs_radix_sort_pairs_static(vs_ctx* ctx, uint32_t* ke
   if (count > STATIC_MAX_KEYS)
     return vs_fail(ctx, VS_ERR_CAPACITY, "radix_sort_static: %u pairs exceed the static scratch limit of %u", count,
                    STATIC_MAX_KEYS);
+  // the caller's current device is put back on every return
+  int prev_device = -1;
+  VS_TRY(vs_cuda(ctx, cudaGetDevice(&prev_device), "cudaGetDevice"));
+  struct RestoreDevice {
+    int dev, cur;
+    ~RestoreDevice() {
+      if (dev >= 0 && dev != cur) cudaSetDevice(dev);
+    }
+  } restore{prev_device, ctx->device};
   VS_TRY(vs_cuda(ctx, cudaSetDevice(ctx->device), "cudaSetDevice"));
   uint32_t* scratch = nullptr;
   VS_TRY(static_scratch(ctx, &scratch));

@@ -89,11 +89,13 @@ class PeerGroup:
     def barrier(self):
         """Device barrier of all ranks on the current stream."""
         self.epoch += 1
+        self.ctx.bind()  # ordered after the work already queued on the current stream
         self.ctx.check(self.ctx.lib.vs_peer_barrier(self.ctx.h, self._flag_ptrs, self.world, self.rank,
                                                     self.epoch & 0xFFFFFFFF))
 
     def check(self):
         """Raises if a device wait of this rank gave up (synchronises)."""
+        self.ctx.bind()
         self.ctx.check(self.ctx.lib.vs_ctx_check(self.ctx.h))
 
     def close(self):

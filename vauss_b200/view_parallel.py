@@ -115,8 +115,13 @@ class ViewParallelTrainer(SplatTrainer):
         self._resident = t.data_ptr()
         return Splats(t, sh, o)
 
-    def step_views(self, batches: Sequence[SceneBatch], splats: Splats) -> tuple[Splats, TrainStepStats]:
+    def step_views(self, batches: Sequence[SceneBatch], splats: Splats, hook=None) -> tuple[Splats, TrainStepStats]:
+        """One optimizer step over this rank's views.  ``hook(name)``, when
+        given, runs after each stage (render, loss, raster_bwd, vjp_dense per
+        view; then barrier_rows, optimizer, barrier_params or exchange,
+        optimizer), where a benchmark records CUDA events."""
         c = self.config
+        mark = hook or (lambda name: None)
         peer = self.peer
         if peer is not None and self.peer_set is None:
             raise RuntimeError("call adopt(splats) before step_views with a peer group")
@@ -168,18 +173,23 @@ class ViewParallelTrainer(SplatTrainer):
             out = ops.render(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, frame=self.frame,
                              out_img=self._buf("img", (cam.height, cam.width, 4), torch.float32),
                              visible=self._buf("visible", (n,), torch.float32))
+            mark("render")
             if ev is not None:
                 torch.cuda.current_stream(self.device).wait_event(ev)
             loss = ops.image_loss(out.out_img, gt, c.l1_weight, c.ssim_loss_weight)
             losses.append(loss.loss.clone())
+            mark("loss")
             vc = ops.rasterize_bwd(out.frame, out.out_img, loss.dl_dpred,
                                    self._buf("v_combined", (max(n, 1), 10), torch.float32))
+            mark("raster_bwd")
             ops.vjp_dense(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, grads,
                           refine, visible=out.visible, vis_accum=vis)
+            mark("vjp_dense")
             num_visible += out.num_visible
             num_isect += out.num_intersections
         if peer is None:
             self.exchange(self.flat)
+            mark("exchange")
         self.optim["time"] += 1
         time = self.optim["time"]
         o = self.optim
@@ -190,12 +200,16 @@ class ViewParallelTrainer(SplatTrainer):
                         noise_limit=self.median_scale, noise_seed=int(self.rng.integers(0, 2 ** 32)))
         if peer is not None:
             peer.barrier()  # every rank's rows and counts are complete
+            mark("barrier_rows")
             ops.adam_q8_peer(splats.sh_degree, n, self.shard[0], self.shard[1], self.peer_set, o["t"], o["sh"],
                              o["o"], q8, device=self.device)
+            mark("optimizer")
             peer.barrier()  # every replica holds the new parameters
+            mark("barrier_params")
         else:
             ops.adam_q8_dense(splats.sh_degree, splats.transforms, splats.sh_coeffs, splats.raw_opacities, grads,
                               o["t"], o["sh"], o["o"], q8, opacities=None, visible=vis)
+            mark("optimizer")
         loss_total = torch.stack(losses).sum() if losses else torch.zeros((), device=self.device)
         stats = TrainStepStats(loss=loss_total, num_visible=num_visible, num_intersections=num_isect,
                                lr_mean=float(self.transforms_lr()[0]), lr_coeffs=c.lr_coeffs_dc, lr_opac=c.lr_opac)
