@@ -217,10 +217,13 @@ typedef struct vs_q8_cfg {
  * sh_coeffs (f32) and raw_opacities, plus the refine statistics
  * (refine_norm = max, vis_count += visible, max_screen = max) and the
  * low-opacity mean noise: two kernels (the VJP of the visible splats into
- * ctx scratch, then the optimizer).  stats pointers may be NULL.  Frames
- * rendered with a min_scale floor are rejected (VS_ERR_UNSUPPORTED). */
+ * ctx scratch, then the optimizer).  stats pointers may be NULL.  min_scale
+ * is the Mip 3D-filter floor the frame was rendered with (the reference's
+ * project_update min_scale/has_min_scale, src/bwd/project_update.rs:84-110):
+ * required when the render had one, ignored otherwise. */
 VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
-                            float* transforms, float* sh_coeffs, float* raw_opacities, const float* v_combined,
+                            float* transforms, float* sh_coeffs, float* raw_opacities, const float* min_scale,
+                            const float* v_combined,
                             vs_q8_tensor mom_t, vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8,
                             const float* visible, float* refine_norm, float* vis_count, float* max_screen);
 
@@ -323,6 +326,18 @@ VS_API vs_status vs_q8_reset_rows(vs_ctx* ctx, vs_q8_tensor mom, uint32_t row_wi
                                   const int32_t* rows);
 /* raw = logit(clamp(sigmoid(raw) - amount, 1e-12, 1 - 1e-12)) (train.rs:2285-2296). */
 VS_API vs_status vs_opacity_decay(vs_ctx* ctx, uint32_t num_splats, float* raw_opacities, float amount);
+/* Mip-Splatting 3D-filter floor per splat, compute_min_scale
+ * (crates/splat-train/src/train.rs:353-387): min_scale[i] = sqrt(factor) *
+ * min_v |mean_i - centre_v| * inv_focal_v.  view_cams: [V, 4] f32 device rows
+ * (centre x, y, z, 1 / max(focal_px, 1e-6)), 16-byte aligned; factor > 0. */
+VS_API vs_status vs_min_scale(vs_ctx* ctx, uint32_t num_splats, const float* transforms, const float* view_cams,
+                              uint32_t num_views, float factor, float* min_scale);
+/* Folds a floor into the raw parameters in place, Splats::bake_min_scale /
+ * fold_min_scale (crates/splat-train-render/src/gaussian_splats.rs:165-188,
+ * 394-402): log-scales -> log sqrt(s^2 + f^2), opacity scaled by the energy
+ * factor and clamped to [1e-6, 1 - 1e-6]. */
+VS_API vs_status vs_fold_min_scale(vs_ctx* ctx, uint32_t num_splats, float* transforms, float* raw_opacities,
+                                   const float* min_scale);
 
 /* ---- dataset feed: packed RGBA8 ground truth -------------------------------
  * Replaces SceneLoader (crates/splat-train-dataset/src/scene_loader.rs:59-184)

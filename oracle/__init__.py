@@ -331,6 +331,24 @@ def refine_split(transforms, sh, raw_opac, parents, children, screen, split_at_s
     return t, shf.reshape(np.asarray(sh).shape), o
 
 
+def min_scale(transforms, view_cams, factor):
+    """compute_min_scale (train.rs:353-387); view_cams [V, 4] = centre xyz, 1/max(focal, 1e-6)."""
+    t = _f32(transforms)
+    cams = _f32(view_cams)
+    out = np.zeros(t.shape[0], np.float32)
+    lib().or_min_scale(ctypes.c_uint32(t.shape[0]), _p(t, F32P), _p(cams, F32P), ctypes.c_uint32(cams.shape[0]),
+                       ctypes.c_float(factor), _p(out, F32P))
+    return out
+
+
+def fold_min_scale(transforms, raw_opac, min_scale):
+    """fold_min_scale (gaussian_splats.rs:165-188) on copies."""
+    t = _f32(transforms).copy()
+    o = _f32(raw_opac).copy()
+    lib().or_fold_min_scale(ctypes.c_uint32(t.shape[0]), _p(t, F32P), _p(o, F32P), _p(_f32(min_scale), F32P))
+    return t, o
+
+
 def opacity_decay(raw_opac, amount):
     o = _f32(raw_opac).copy()
     lib().or_opacity_decay(ctypes.c_uint32(o.shape[0]), _p(o, F32P), ctypes.c_float(amount))
@@ -365,9 +383,10 @@ def f16_roundtrip(x):
     return h, back
 
 
-def render_forward(cam, cfg, splats, bg=(0.0, 0.0, 0.0)):
-    """Projection + binning + rasterize forward, all on the CPU."""
-    proj = project(cam, cfg, splats.transforms, splats.sh, splats.raw_opac)
+def render_forward(cam, cfg, splats, bg=(0.0, 0.0, 0.0), min_scale=None):
+    """Projection + binning + rasterize forward, all on the CPU (with the Mip
+    3D-filter floor when ``min_scale`` is given and cfg.has_min_scale is set)."""
+    proj = project(cam, cfg, splats.transforms, splats.sh, splats.raw_opac, min_scale)
     binning = bin(cam, proj)
     pre_offsets = binning["tile_offsets"].copy()
     fwd = raster_fwd(cam, bg, proj, binning, splats.n)

@@ -1537,6 +1537,43 @@ OR_API void or_opacity_decay(uint32_t n, float* raw_opac, float amount) {
   }
 }
 
+// Mip-Splatting 3D-filter floor, compute_min_scale (crates/splat-train/src/
+// train.rs:353-387); cams rows are (centre x, y, z, 1 / max(focal, 1e-6)).
+OR_API void or_min_scale(uint32_t n, const float* transforms, const float* cams, uint32_t views, float factor,
+                         float* out) {
+  const float sf = sqrtf(factor);
+#pragma omp parallel for schedule(static)
+  for (int64_t gi = 0; gi < (int64_t)n; ++gi) {
+    const float* t = transforms + gi * 10;
+    float r = INFINITY;
+    for (uint32_t v = 0; v < views; ++v) {
+      const float* c = cams + (size_t)v * 4;
+      const float dx = t[0] - c[0], dy = t[1] - c[1], dz = t[2] - c[2];
+      const float dist = sqrtf((dx * dx + dy * dy) + dz * dz);
+      r = fminf(r, dist * c[3]);
+    }
+    out[gi] = r * sf;
+  }
+}
+
+// fold_min_scale (crates/splat-train-render/src/gaussian_splats.rs:165-188).
+OR_API void or_fold_min_scale(uint32_t n, float* transforms, float* raw_opac, const float* min_scale) {
+  for (uint32_t g = 0; g < n; ++g) {
+    float* t = transforms + (size_t)g * 10;
+    const float f = min_scale[g], f2 = f * f;
+    float diff[3];
+    for (int k = 0; k < 3; ++k) {
+      const float ls = t[7 + k];
+      const float nl = vs_logf(vs_expf(ls * 2.0f) + f2) * 0.5f;
+      diff[k] = ls - nl;
+      t[7 + k] = nl;
+    }
+    const float coef = vs_expf((diff[0] + diff[1]) + diff[2]);
+    const float o = fminf(fmaxf(vs_sigmoid(raw_opac[g]) * coef, 1.0e-6f), 1.0f - 1.0e-6f);
+    raw_opac[g] = vs_logf(o / (1.0f - o));
+  }
+}
+
 // ---- dataset feed: view_to_packed_data (crates/splat-train-dataset/src/
 // scene.rs:113-161) for 8-bit sources.  L / LA widen to RGBA the way
 // DynamicImage::into_rgba8 does (l, l, l[, a]); a missing alpha is 255; with

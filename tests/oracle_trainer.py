@@ -29,6 +29,7 @@ class OracleTrainer(SplatTrainer):
         self.vis = np.zeros(n, np.float32)
         self.screen = np.zeros(n, np.float32)
         self.time = 0
+        self.min_scale = None  # the Mip 3D-filter floor [N] f32, when set
         if config.optimizer == "q8":
             self.mom = {"t": _q8_zero(n * 10), "sh": _q8_zero(sp.sh.size), "o": _q8_zero(n)}
         else:
@@ -49,8 +50,9 @@ class OracleTrainer(SplatTrainer):
         n = sp.n
         half = c.optimizer == "reference" and self.sh_half is not None
         sh_now = self.sh_half.view(np.uint16) if half else sp.sh
-        cfg = oracle.make_cfg(sp.sh_degree, mip=c.render_mode_mip, sh_half=half, bg=bg)
-        r = oracle.render_forward(cam, cfg, SplatSet(sp.transforms, sh_now, sp.raw_opac), bg=bg)
+        ms = self.min_scale
+        cfg = oracle.make_cfg(sp.sh_degree, mip=c.render_mode_mip, sh_half=half, bg=bg, has_min_scale=ms is not None)
+        r = oracle.render_forward(cam, cfg, SplatSet(sp.transforms, sh_now, sp.raw_opac), bg=bg, min_scale=ms)
         lo = oracle.loss_fwd(r["out_img"], gt_packed, c.l1_weight, c.ssim_loss_weight)
         dl = oracle.loss_bwd(r["out_img"], gt_packed, lo["coeffs"], c.l1_weight, c.ssim_loss_weight)
         vc = oracle.raster_bwd(cam, bg, r["proj"], r["binning_after"], r["out_img"], dl)
@@ -63,7 +65,7 @@ class OracleTrainer(SplatTrainer):
         b1, b2, inv1, inv2 = ops.adam_coefficients(time)
         if c.optimizer == "q8":
             grads, refine = oracle.vjp_dense(cam, cfg, sp.transforms, sp.sh, sp.raw_opac,
-                                             r["proj"]["compact_from_global"], vc)
+                                             r["proj"]["compact_from_global"], vc, min_scale=ms)
             if opac_reg:
                 o = (np.float32(1) / (np.float32(1) + oracle.expf(-sp.raw_opac))).astype(np.float32)
                 grads[:, -1] = (grads[:, -1] + np.float32(opac_reg) * o * (np.float32(1) - o)).astype(np.float32)
@@ -83,7 +85,7 @@ class OracleTrainer(SplatTrainer):
         else:
             pu = oracle.project_update(cam, cfg, sp.transforms, sh_now, sp.raw_opac, r["proj"]["compact_from_global"],
                                        vc, self.w_t, lr_t, self.w_o, b1, b2, inv1, inv2, c.adam_epsilon, c.lr_opac,
-                                       opac_reg, time)
+                                       opac_reg, time, min_scale=ms)
             refine = pu["refine"]
             self.w_t, self.w_o = pu["w_t"], pu["w_o"]
             gsq = pu["grad_sq"]

@@ -119,7 +119,7 @@ _SIGS = {
     "vs_sh_step": ([c_vp, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_f32p,
                     ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                     ctypes.c_uint32], ctypes.c_int),
-    "vs_step_q8": ([c_vp, c_vp, ctypes.POINTER(RenderCfg), ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, Q8Tensor,
+    "vs_step_q8": ([c_vp, c_vp, ctypes.POINTER(RenderCfg), ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, Q8Tensor,
                     Q8Tensor, Q8Tensor, ctypes.POINTER(Q8Cfg), c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_vjp_dense": ([c_vp, c_vp, ctypes.POINTER(RenderCfg), ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                       c_vp, c_vp, c_vp], ctypes.c_int),
@@ -140,6 +140,8 @@ _SIGS = {
                          c_vp, c_vp, c_vp, ctypes.c_float, ctypes.c_float, ctypes.c_uint32, c_vp], ctypes.c_int),
     "vs_q8_reset_rows": ([c_vp, Q8Tensor, ctypes.c_uint32, ctypes.c_uint32, c_vp], ctypes.c_int),
     "vs_opacity_decay": ([c_vp, ctypes.c_uint32, c_vp, ctypes.c_float], ctypes.c_int),
+    "vs_min_scale": ([c_vp, ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint32, ctypes.c_float, c_vp], ctypes.c_int),
+    "vs_fold_min_scale": ([c_vp, ctypes.c_uint32, c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_pack_view": ([c_vp, c_vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int32, c_vp,
                       ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
     "vs_feed_create": ([c_vp, ctypes.POINTER(FeedCfg), ctypes.POINTER(c_vp)], ctypes.c_int),

@@ -70,8 +70,13 @@ def ply_header(num_splats: int, sh_degree: int, up_axis=None, render_mode: str =
 
 def ply_rows(splats, device=None) -> np.ndarray:
     """The vertex rows of `splats` as host f32 [N, 14 + 3 rest], encoded on
-    the GPU."""
+    the GPU.  A Mip 3D-filter floor is folded into copies of the scales and
+    opacities first, as the reference's export bakes it
+    (gaussian_splats.rs:390-402)."""
     t, sh, o = splats.transforms, splats.sh_coeffs, splats.raw_opacities
+    if getattr(splats, "min_scale", None) is not None:
+        t, o = t.clone(), o.clone()
+        ops.fold_min_scale(t, o, splats.min_scale)
     dev = t.device if device is None else torch.device(device)
     n, coeffs = t.shape[0], sh.shape[1]
     degree = int(round(coeffs ** 0.5)) - 1
@@ -356,6 +361,7 @@ def save_checkpoint(directory: str, trainer, splats, up_axis=None) -> None:
              "scene_extent": trainer.scene_extent, "median_scale": trainer.median_scale,
              "rng": trainer.rng.bit_generator.state, "train_pixels": trainer.train_pixels,
              "view_centers": None if trainer.view_centers is None else np.asarray(trainer.view_centers).tolist(),
+             "view_cams": None if trainer.view_cams is None else trainer.view_cams.cpu().numpy().tolist(),
              "optimizer": trainer.config.optimizer, "refiner": None}
     if trainer.optim is not None:
         if trainer.config.optimizer != "q8":
@@ -366,6 +372,9 @@ def save_checkpoint(directory: str, trainer, splats, up_axis=None) -> None:
     rec = trainer.record
     extra = {} if rec is None else dict(refine_norm=rec.refine_norm.cpu().numpy(), vis_count=rec.vis_count.cpu().numpy(),
                                         max_screen=rec.max_screen.cpu().numpy())
+    if splats.min_scale is not None:  # the PLY holds the folded splat; keep the raw values and the floor
+        extra.update(raw_log_scales=splats.transforms[:, 7:10].cpu().numpy(),
+                     raw_opacities=splats.raw_opacities.cpu().numpy(), min_scale=splats.min_scale.cpu().numpy())
     np.savez(os.path.join(directory, "record.npz"), raw_rotations=splats.transforms[:, 3:7].cpu().numpy(), **extra)
     r = trainer.refiner
     if r is not None:
@@ -391,6 +400,12 @@ def load_checkpoint(directory: str, device):
     splats, _ = load_ply(os.path.join(directory, "splats.ply"), dev)
     rec = np.load(os.path.join(directory, "record.npz"))
     splats.transforms[:, 3:7] = torch.from_numpy(rec["raw_rotations"]).to(dev)
+    if "min_scale" in rec.files:
+        splats.transforms[:, 7:10] = torch.from_numpy(rec["raw_log_scales"]).to(dev)
+        splats.raw_opacities.copy_(torch.from_numpy(rec["raw_opacities"]).to(dev))
+        splats.min_scale = torch.from_numpy(rec["min_scale"]).to(dev)
+    if state.get("view_cams") is not None:
+        tr.view_cams = torch.tensor(state["view_cams"], dtype=torch.float32, device=dev)
     mom = os.path.join(directory, "moments.q8")
     if os.path.exists(mom):
         tr.optim = load_moments(mom, dev)

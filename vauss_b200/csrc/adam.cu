@@ -320,6 +320,7 @@ constexpr uint32_t VJP_ROW = 20;
 __global__ void __launch_bounds__(128) vjp_rows_kernel(Uniforms u, uint32_t v, const uint32_t* __restrict__ global_from_compact,
                                                        const float* __restrict__ transforms, const float* __restrict__ sh,
                                                        const float* __restrict__ raw_opac,
+                                                       const float* __restrict__ min_scale,
                                                        const float* __restrict__ v_combined, float4* __restrict__ rows) {
   __shared__ uint32_t s_list[128];
   __shared__ uint32_t s_wcnt[4];
@@ -344,8 +345,8 @@ __global__ void __launch_bounds__(128) vjp_rows_kernel(Uniforms u, uint32_t v, c
   float tt[10];
 #pragma unroll
   for (int k = 0; k < 10; ++k) tt[k] = transforms[(size_t)g * 10 + k];
-  // the Q8 step takes no min_scale floor (its launcher rejects frames with one)
-  const VjpOut r = splat_vjp(tt, raw_opac[g], sh, nullptr, g, rr, u);
+  // the Mip 3D-filter floor enters the VJP when the frame was rendered with one
+  const VjpOut r = splat_vjp(tt, raw_opac[g], sh, min_scale, g, rr, u);
   float o[VJP_ROW];
   o[0] = r.v_mean.x; o[1] = r.v_mean.y; o[2] = r.v_mean.z;
   o[3] = r.v_q.w; o[4] = r.v_q.x; o[5] = r.v_q.y; o[6] = r.v_q.z;
@@ -885,15 +886,16 @@ VS_API vs_status vs_sh_step(vs_ctx* ctx, uint32_t num_splats, uint32_t row_width
 }
 
 VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
-                            float* transforms, float* sh_coeffs, float* raw_opacities, const float* v_combined,
+                            float* transforms, float* sh_coeffs, float* raw_opacities, const float* min_scale,
+                            const float* v_combined,
                             vs_q8_tensor mom_t, vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8,
                             const float* visible, float* refine_norm, float* vis_count, float* max_screen) {
   if (!ctx) return VS_ERR_INVALID;
   if (!frame || !frame->rendered || !cfg || !q8) return vs_fail(ctx, VS_ERR_INVALID, "step_q8: missing frame/config");
   if (num_splats != frame->n) return vs_fail(ctx, VS_ERR_INVALID, "step_q8: %u splats, frame has %u", num_splats, frame->n);
   if (cfg->sh_half) return vs_fail(ctx, VS_ERR_UNSUPPORTED, "step_q8: SH coefficients must be f32");
-  if (frame->u.has_min_scale)
-    return vs_fail(ctx, VS_ERR_UNSUPPORTED, "step_q8: frames rendered with a min_scale floor need the dense path");
+  if (frame->u.has_min_scale && !min_scale)
+    return vs_fail(ctx, VS_ERR_INVALID, "step_q8: the frame was rendered with a min_scale floor; pass it");
   if (!transforms || !sh_coeffs || !raw_opacities || (frame->v && !v_combined) || !q8_valid(mom_t) ||
       !q8_valid(mom_sh) || !q8_valid(mom_o))
     return vs_fail(ctx, VS_ERR_INVALID, "step_q8: null buffer");
@@ -910,7 +912,7 @@ VS_API vs_status vs_step_q8(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* c
   if (frame->v > 0) {
     vjp_rows_kernel<<<vs::div_up(frame->v, 128), 128, 0, ctx->stream>>>(
         frame->u, frame->v, (const uint32_t*)frame->global_from_compact.ptr, transforms, sh_coeffs, raw_opacities,
-        v_combined, (float4*)ctx->vjp_rows.ptr); ++ctx->launches;
+        frame->u.has_min_scale ? min_scale : nullptr, v_combined, (float4*)ctx->vjp_rows.ptr); ++ctx->launches;
   }
   q8_kernel<0><<<vs::div_up(num_splats, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
       frame->u, num_splats, transforms, sh_coeffs, raw_opacities, (const uint32_t*)frame->compact_from_global.ptr,

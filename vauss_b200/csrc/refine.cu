@@ -150,6 +150,48 @@ __global__ void opacity_decay_kernel(uint32_t n, float* __restrict__ raw_opac, f
   raw_opac[g] = vs_logf(o / (1.0f - o));
 }
 
+// Mip-Splatting 3D-filter floor (compute_min_scale, crates/splat-train/src/
+// train.rs:353-387): f_i = sqrt(factor) * min over the training views of
+// |mean_i - centre_v| / max(focal_v, 1e-6).  `cams` holds per view the centre
+// and the reciprocal focal length (the host forms 1 / max(focal, 1e-6) in f32);
+// the distance sums the squares in axis order.
+__global__ void min_scale_kernel(uint32_t n, const float* __restrict__ transforms, const float4* __restrict__ cams,
+                                 uint32_t views, float sqrt_factor, float* __restrict__ out) {
+  const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n) return;
+  const float mx = transforms[(size_t)g * 10], my = transforms[(size_t)g * 10 + 1], mz = transforms[(size_t)g * 10 + 2];
+  float r = __int_as_float(0x7f800000);
+  for (uint32_t v = 0; v < views; ++v) {
+    const float4 c = cams[v];
+    const float dx = mx - c.x, dy = my - c.y, dz = mz - c.z;
+    const float dist = sqrtf((dx * dx + dy * dy) + dz * dz);
+    r = fminf(r, dist * c.w);
+  }
+  out[g] = r * sqrt_factor;
+}
+
+// Folds the floor into the raw parameters (fold_min_scale, crates/splat-train-
+// render/src/gaussian_splats.rs:165-188): log-scales become log sqrt(s^2 + f^2),
+// the opacity takes the energy factor exp(sum(log s - new log s)) and is stored
+// back as a logit after clamping to [1e-6, 1 - 1e-6].
+__global__ void fold_min_scale_kernel(uint32_t n, float* __restrict__ transforms, float* __restrict__ raw_opac,
+                                      const float* __restrict__ min_scale) {
+  const uint32_t g = blockIdx.x * blockDim.x + threadIdx.x;
+  if (g >= n) return;
+  float* t = transforms + (size_t)g * 10;
+  const float f = min_scale[g], f2 = f * f;
+  float diff[3];
+  for (int k = 0; k < 3; ++k) {
+    const float ls = t[7 + k];
+    const float nl = vs_logf(vs_expf(ls * 2.0f) + f2) * 0.5f;
+    diff[k] = ls - nl;
+    t[7 + k] = nl;
+  }
+  const float coef = vs_expf((diff[0] + diff[1]) + diff[2]);
+  const float o = clampf(vs_sigmoid(raw_opac[g]) * coef, 1.0e-6f, 1.0f - 1.0e-6f);
+  raw_opac[g] = vs_logf(o / (1.0f - o));
+}
+
 }  // namespace
 
 extern "C" {
@@ -217,6 +259,34 @@ VS_API vs_status vs_opacity_decay(vs_ctx* ctx, uint32_t num_splats, float* raw_o
   opacity_decay_kernel<<<div_up(num_splats, 256), 256, 0, ctx->stream>>>(num_splats, raw_opacities, amount);
   ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "opacity_decay launch");
+}
+
+VS_API vs_status vs_min_scale(vs_ctx* ctx, uint32_t num_splats, const float* transforms, const float* view_cams,
+                              uint32_t num_views, float factor, float* min_scale) {
+  if (!ctx) return VS_ERR_INVALID;
+  if ((num_splats && (!transforms || !min_scale)) || (num_views && !view_cams) || !(factor > 0.0f))
+    return vs_fail(ctx, VS_ERR_INVALID, "min_scale: bad arguments");
+  if (num_views == 0) return vs_fail(ctx, VS_ERR_INVALID, "min_scale: no training views");
+  if (((uintptr_t)view_cams & 15u) != 0) return vs_fail(ctx, VS_ERR_INVALID, "min_scale: view_cams must be 16-byte aligned");
+  if (num_splats == 0) return VS_OK;
+  VS_CUDA(ctx, cudaSetDevice(ctx->device));
+  min_scale_kernel<<<div_up(num_splats, 256), 256, 0, ctx->stream>>>(num_splats, transforms, (const float4*)view_cams,
+                                                                     num_views, sqrtf(factor), min_scale);
+  ++ctx->launches;
+  return vs_cuda(ctx, cudaGetLastError(), "min_scale launch");
+}
+
+VS_API vs_status vs_fold_min_scale(vs_ctx* ctx, uint32_t num_splats, float* transforms, float* raw_opacities,
+                                   const float* min_scale) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (num_splats && (!transforms || !raw_opacities || !min_scale))
+    return vs_fail(ctx, VS_ERR_INVALID, "fold_min_scale: null argument");
+  if (num_splats == 0) return VS_OK;
+  VS_CUDA(ctx, cudaSetDevice(ctx->device));
+  fold_min_scale_kernel<<<div_up(num_splats, 256), 256, 0, ctx->stream>>>(num_splats, transforms, raw_opacities,
+                                                                          min_scale);
+  ++ctx->launches;
+  return vs_cuda(ctx, cudaGetLastError(), "fold_min_scale launch");
 }
 
 }  // extern "C"

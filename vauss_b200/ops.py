@@ -313,11 +313,13 @@ def q8_cfg(time: int, lr_transforms, lr_sh_dc: float, lr_sh_rest: float, lr_opac
 
 def step_q8(frame: Frame, cfg: N.RenderCfg, transforms, sh_coeffs, raw_opacities, v_combined, mom_t: Q8Moments,
             mom_sh: Q8Moments, mom_o: Q8Moments, q8: N.Q8Cfg, visible=None, refine_norm=None, vis_count=None,
-            max_screen=None):
-    """Single-view fused VJP + 8-bit-moment Adam + refine statistics + mean noise (in place)."""
+            max_screen=None, min_scale=None):
+    """Single-view fused VJP + 8-bit-moment Adam + refine statistics + mean noise (in place);
+    ``min_scale`` is the Mip 3D-filter floor the frame was rendered with, if any."""
     ctx = frame.ctx.bind()
     ctx.check(ctx.lib.vs_step_q8(ctx.h, frame.h, ctypes.byref(cfg), transforms.shape[0], _ptr(transforms),
-                                 _ptr(sh_coeffs), _ptr(raw_opacities), _ptr(v_combined), mom_t.c(), mom_sh.c(),
+                                 _ptr(sh_coeffs), _ptr(raw_opacities), _ptr(min_scale), _ptr(v_combined),
+                                 mom_t.c(), mom_sh.c(),
                                  mom_o.c(), ctypes.byref(q8), _ptr(visible), _ptr(refine_norm), _ptr(vis_count),
                                  _ptr(max_screen)))
 
@@ -329,6 +331,27 @@ def vjp_dense(frame: Frame, cfg: N.RenderCfg, transforms, sh_coeffs, raw_opaciti
     ctx.check(ctx.lib.vs_vjp_dense(ctx.h, frame.h, ctypes.byref(cfg), transforms.shape[0], _ptr(transforms),
                                    _ptr(sh_coeffs), _ptr(raw_opacities), _ptr(min_scale), _ptr(v_combined),
                                    _ptr(grads), _ptr(refine), _ptr(visible), _ptr(vis_accum)))
+
+
+def min_scale(transforms: torch.Tensor, view_cams: torch.Tensor, factor: float,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """Mip-Splatting 3D-filter floor per splat (compute_min_scale, crates/splat-train/src/train.rs:353-387);
+    ``view_cams`` [V, 4] f32 rows (centre x, y, z, 1 / max(focal_px, 1e-6))."""
+    ctx = context(transforms.device)
+    n = transforms.shape[0]
+    out = torch.empty(n, dtype=torch.float32, device=transforms.device) if out is None else out
+    cams = view_cams.contiguous()
+    ctx.check(ctx.lib.vs_min_scale(ctx.h, n, _ptr(transforms), _ptr(cams), cams.shape[0], ctypes.c_float(factor),
+                                   _ptr(out)))
+    return out
+
+
+def fold_min_scale(transforms: torch.Tensor, raw_opacities: torch.Tensor, min_scale: torch.Tensor):
+    """Splats::bake_min_scale (gaussian_splats.rs:165-188, 394-402): folds the floor into the
+    log-scales and raw opacities in place."""
+    ctx = context(transforms.device)
+    ctx.check(ctx.lib.vs_fold_min_scale(ctx.h, transforms.shape[0], _ptr(transforms), _ptr(raw_opacities),
+                                        _ptr(min_scale)))
 
 
 def adam_q8_dense(sh_degree: int, transforms, sh_coeffs, raw_opacities, grads, mom_t: Q8Moments,

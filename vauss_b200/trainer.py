@@ -32,6 +32,12 @@ from . import ops
 from .camera import Camera
 
 
+# train.rs:41, 347: the 3D-filter floor stops being refreshed after 90 % of
+# training and applies only to training images of at most 300k pixels
+MIN_SCALE_FREEZE_FRAC = 0.9
+MIP_3D_FILTER_MAX_PIXELS = 300_000
+
+
 @dataclass
 class TrainConfig:
     """Trainer options (crates/splat-train/src/config.rs:7-351 defaults)."""
@@ -60,6 +66,10 @@ class TrainConfig:
     max_budget: bool = False
     split_at_screen_size: float = 0.5
     opac_decay: float = 0.004
+    # Mip-Splatting 3D filter (config.rs:300-306): a per-splat scale floor of
+    # sqrt(factor) pixel sizes at the nearest training camera, set at each
+    # refine while training images have at most 300k pixels; 0 disables it
+    min_scale_factor: float = 0.1
 
     @property
     def l1_weight(self) -> float:
@@ -90,6 +100,9 @@ class Splats:
     transforms: torch.Tensor  # [N, 10] f32
     sh_coeffs: torch.Tensor  # [N, C, 3] f32 (f16 after the first reference-mode SH step)
     raw_opacities: torch.Tensor  # [N] f32
+    # Mip 3D-filter floor [N] f32, folded into scales and opacity at render
+    # (gaussian_splats.rs:331-402); None = no floor
+    min_scale: torch.Tensor | None = None
 
     @property
     def num_splats(self) -> int:
@@ -144,8 +157,32 @@ class SplatTrainer:
         self._buffers = {}
         self._copy_stream = None
         self.refiner = None
-        self.train_pixels = 0  # pixels of one training image (the refine budget limit); 0 = unlimited
+        self.train_pixels = 0  # pixels of all training images (the refine budget limit); 0 = unlimited
         self.view_centers = None  # [V, 3] camera centres (far-share of the refine budget)
+        self.view_cams = None  # [V, 4] f32 device rows (centre, 1 / focal px) for the 3D-filter floor
+
+    def set_view_cams(self, cameras, train_pixels: int | None = None):
+        """The training cameras (SplatTrainer::set_view_cams, train.rs:608-619):
+        their centres and focal lengths set the 3D-filter floor and the refine
+        budget's far share; ``train_pixels`` defaults to the sum of their
+        image sizes."""
+        centers = np.array([c.position for c in cameras], dtype=np.float32).reshape(-1, 3)
+        inv_f = np.array([np.float32(1.0) / np.float32(max(c.fx, 1e-6)) for c in cameras], dtype=np.float32)
+        rows = np.concatenate([centers, inv_f[:, None]], axis=1).astype(np.float32)
+        self.view_centers = centers
+        self.view_cams = torch.from_numpy(rows).to(self.device) if len(cameras) else None
+        self.train_pixels = int(sum(c.width * c.height for c in cameras)) if train_pixels is None else train_pixels
+
+    def floor_applies(self, it: int) -> bool:
+        """train.rs:2040-2047: the floor is refreshed at a refine before 90 % of
+        training, with view cameras, a positive factor and training images of at
+        most 300k pixels."""
+        c = self.config
+        if c.min_scale_factor <= 0 or self.view_cams is None or self.view_cams.shape[0] == 0:
+            return False
+        per_view = self.train_pixels // max(self.view_cams.shape[0], 1)
+        small = self.train_pixels == 0 or per_view <= MIP_3D_FILTER_MAX_PIXELS
+        return it / max(c.total_train_iters, 1) < MIN_SCALE_FREEZE_FRAC and small
 
     # ---- refinement (train.rs:1779-2300; vauss_b200/refine.py) ----
     def should_refine(self, step: int) -> bool:
@@ -161,6 +198,11 @@ class SplatTrainer:
             raise NotImplementedError("refinement is implemented for the 8-bit-moment optimizer")
         if self.optim is None or self.record is None:
             raise RuntimeError("refine needs at least one training step first")
+        # the floor is folded into the parameters first (train.rs:1806), so the
+        # decisions see the splats' real sizes and opacities
+        if splats.min_scale is not None:
+            ops.fold_min_scale(splats.transforms, splats.raw_opacities, splats.min_scale)
+            splats = Splats(splats.transforms, splats.sh_coeffs, splats.raw_opacities)
         if self.refiner is None:
             means = splats.transforms[:, :3].detach().cpu().numpy()
             self.refiner = Refiner(self.config, Bounds.from_means(means), self.rng, self.train_pixels,
@@ -169,6 +211,10 @@ class SplatTrainer:
         n = splats.num_splats
         dev = self.device
         self.record = RefineRecord(torch.zeros(n, device=dev), torch.zeros(n, device=dev), torch.zeros(n, device=dev))
+        # a fresh floor against the new positions (train.rs:2040-2056)
+        if self.floor_applies(it):
+            splats = Splats(splats.transforms, splats.sh_coeffs, splats.raw_opacities,
+                            ops.min_scale(splats.transforms, self.view_cams, self.config.min_scale_factor))
         return splats, stats
 
     # ---- learning rates (train.rs:859-904) ----
@@ -238,10 +284,12 @@ class SplatTrainer:
         n = splats.num_splats
         mode = c.optimizer
         cfg = ops.render_cfg(splats.sh_degree, mip=c.render_mode_mip,
-                             sh_half=splats.sh_coeffs.dtype == torch.float16, background=bg)
+                             sh_half=splats.sh_coeffs.dtype == torch.float16, background=bg,
+                             has_min_scale=splats.min_scale is not None)
         if self.frame is None:
             self.frame = ops.Frame(ops.context(self.device))
-        out = ops.render(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, frame=self.frame,
+        out = ops.render(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities,
+                         min_scale=splats.min_scale, frame=self.frame,
                          out_img=self._buf("img", (cam.height, cam.width, 4), torch.float32),
                          visible=self._buf("visible", (n,), torch.float32))
         if gt_ready is not None:
@@ -263,7 +311,7 @@ class SplatTrainer:
                             noise_limit=self.median_scale, noise_seed=noise_seed)
             ops.step_q8(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, o["t"],
                         o["sh"], o["o"], q8, visible=out.visible, refine_norm=rec.refine_norm,
-                        vis_count=rec.vis_count, max_screen=rec.max_screen)
+                        vis_count=rec.vis_count, max_screen=rec.max_screen, min_scale=splats.min_scale)
         else:
             splats = self._reference_optimizer_step(out, cfg, splats, vc, lr_t, opac_reg, time, noise_scale,
                                                     noise_seed)
@@ -283,10 +331,11 @@ class SplatTrainer:
         gsq = self._buf("grad_sq", (n,), torch.float32)
         ops.project_update(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc,
                            o["w_t"], lr_t, o["w_o"], adam, color_dir, refine, gsq, variance=o["variance"],
-                           first_step=(time == 1))
+                           first_step=(time == 1), min_scale=splats.min_scale)
         # SH coefficients live in f16 from the first SH step on (optim.rs:424-436)
         if splats.sh_coeffs.dtype != torch.float16:
-            splats = Splats(splats.transforms, splats.sh_coeffs.to(torch.float16), splats.raw_opacities)
+            splats = Splats(splats.transforms, splats.sh_coeffs.to(torch.float16), splats.raw_opacities,
+                            splats.min_scale)
         nc = splats.sh_coeffs.shape[1]
         lr_scale = np.repeat(np.float32([1.0] + [1.0 / c.lr_coeffs_sh_scale] * (nc - 1)), 3)
         cfrom = out.frame.field("compact_from_global")

@@ -169,8 +169,10 @@ class ViewParallelTrainer(SplatTrainer):
             ready.append(self._copy_stream.record_event())
         for b, gt, ev in zip(batches, gts, ready):
             cam = b.camera
-            cfg = ops.render_cfg(splats.sh_degree, mip=c.render_mode_mip, background=self.background())
-            out = ops.render(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, frame=self.frame,
+            cfg = ops.render_cfg(splats.sh_degree, mip=c.render_mode_mip, background=self.background(),
+                                 has_min_scale=splats.min_scale is not None)
+            out = ops.render(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities,
+                             min_scale=splats.min_scale, frame=self.frame,
                              out_img=self._buf("img", (cam.height, cam.width, 4), torch.float32),
                              visible=self._buf("visible", (n,), torch.float32))
             mark("render")
@@ -183,7 +185,7 @@ class ViewParallelTrainer(SplatTrainer):
                                    self._buf("v_combined", (max(n, 1), 10), torch.float32))
             mark("raster_bwd")
             ops.vjp_dense(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, grads,
-                          refine, visible=out.visible, vis_accum=vis)
+                          refine, min_scale=splats.min_scale, visible=out.visible, vis_accum=vis)
             mark("vjp_dense")
             num_visible += out.num_visible
             num_isect += out.num_intersections
