@@ -290,46 +290,34 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
                                  uint32_t splat_end, const vs_peer_set* peers, vs_q8_tensor mom_t,
                                  vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8);
 
-/* Owner-side VJP exchange.  Instead of dense gradient rows, each rank
- * writes, per view it rendered this step (up to VS_VIEW_SLOTS), the
- * rasterizer gradient row and visible mark of every splat the view projected
- * straight into the memory of the rank that owns the splat's shard, tagged
- * with the step's epoch (vs_view_scatter: posted stores over NVLink); the
- * owner then computes the projection VJP of every view for its shard from its
- * own memory.  Per view that is 48 bytes per projected splat, against 236
- * bytes per splat for dense rows.  Slot index: rank * VS_VIEW_SLOTS + k. */
+/* Owner-side VJP exchange.  Instead of dense gradient rows, each rank keeps,
+ * per view it rendered this step (up to VS_VIEW_SLOTS), the view's projection
+ * map (VS_FIELD_COMPACT_FROM_GLOBAL), forward visible marks, rasterizer
+ * gradient rows (vs_rasterize_backward) and uniforms (vs_frame_uniforms) in
+ * buffers every rank maps; the rank that owns a shard of the splats then
+ * computes the projection VJP of every view for its shard itself, reading only
+ * 8 bytes per (splat, view) plus the 40-byte rows of the splats a view saw.
+ * Slot index: rank * VS_VIEW_SLOTS + k, k < used[rank]. */
 #define VS_VIEW_SLOTS 8
 #define VS_UNIFORMS_BYTES 256
-typedef struct vs_view_dest {
-  uint32_t world, epoch;                    /* epoch: the same nonzero value on every rank for one step */
-  uint32_t shard_begin[VS_PEER_MAX + 1];    /* owner r holds splats [shard_begin[r], shard_begin[r + 1]) */
-  uint32_t* tag[VS_PEER_MAX];               /* owner r's [shard] epoch tags of this rank's view slot */
-  float* visible[VS_PEER_MAX];              /* owner r's [shard] visible marks */
-  float* v_combined[VS_PEER_MAX];           /* owner r's [shard, 10] rasterizer rows */
-} vs_view_dest;
-/* Scatters one rendered view's rasterizer rows (v_combined [V, 10] of the
- * frame's backward) and visible marks [N] to the shard owners of `dest`. */
-VS_API vs_status vs_view_scatter(vs_ctx* ctx, vs_frame* frame, const float* visible, const float* v_combined,
-                                 const vs_view_dest* dest);
 typedef struct vs_view_set {
-  uint32_t world, epoch;
-  uint32_t used[VS_PEER_MAX];               /* view slots each rank filled this step */
-  const uint32_t* tag[VS_PEER_MAX * VS_VIEW_SLOTS];     /* this owner's [shard] tags per (rank, slot) */
-  const float* visible[VS_PEER_MAX * VS_VIEW_SLOTS];    /* [shard] */
-  const float* v_combined[VS_PEER_MAX * VS_VIEW_SLOTS]; /* [shard, 10] */
-  const void* uniforms[VS_PEER_MAX * VS_VIEW_SLOTS];    /* VS_UNIFORMS_BYTES each (vs_frame_uniforms) */
+  uint32_t world;
+  uint32_t used[VS_PEER_MAX];
+  const uint32_t* compact_from_global[VS_PEER_MAX * VS_VIEW_SLOTS]; /* [N] compact id + 1, 0 = not projected */
+  const float* visible[VS_PEER_MAX * VS_VIEW_SLOTS];                /* [N] forward visible marks */
+  const float* v_combined[VS_PEER_MAX * VS_VIEW_SLOTS];             /* [V, 10] rasterizer gradient rows */
+  const void* uniforms[VS_PEER_MAX * VS_VIEW_SLOTS];                /* VS_UNIFORMS_BYTES each */
 } vs_view_set;
 /* Copies the frame's projection uniforms (camera, image, render mode; at most
  * VS_UNIFORMS_BYTES) into device memory, stream-ordered. */
 VS_API vs_status vs_frame_uniforms(vs_frame* frame, void* dst_device);
 /* Dense gradient rows [splat_end - splat_begin, 10 + 3(d+1)^2 + 1] and view
- * counts [splat_end - splat_begin] of splats [splat_begin, splat_end), this
- * rank's shard: per view slot whose tag carries views->epoch, the projection
- * VJP of the splat, summed per rank in slot order and then over ranks in rank
- * order -- bit for bit the rows the dense path (vs_vjp_dense on each rank,
- * then the rank-order sum of vs_adam_q8_peer) gives.  transforms/sh_coeffs/
- * raw_opacities/min_scale are this rank's replica; rows of splats that no
- * view saw are left as they were. */
+ * counts [splat_end - splat_begin] of splats [splat_begin, splat_end): per
+ * view the projection VJP of the splats it saw, summed per rank in slot order
+ * and then over ranks in rank order -- bit for bit the rows the dense path
+ * (vs_vjp_dense on each rank, then the rank-order sum of vs_adam_q8_peer)
+ * gives.  transforms/sh_coeffs/raw_opacities/min_scale are this rank's replica;
+ * rows of splats that no view saw are left as they were. */
 VS_API vs_status vs_vjp_owner(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, uint32_t splat_begin,
                               uint32_t splat_end, const vs_view_set* views, const float* transforms,
                               const float* sh_coeffs, const float* raw_opacities, const float* min_scale,

@@ -181,15 +181,13 @@ def test_peer_adam_after_a_barrier_that_gave_up_touches_nothing(cuda):
 
 @pytest.mark.parametrize("world,views", [(2, 2), (3, 1), (1, 3)])
 def test_owner_vjp_exchange_matches_dense_exchange(cuda, world, views):
-    """The owner-side exchange (vs_view_scatter writes each view's rasterizer
-    rows and visible marks into the owners' arrays; vs_vjp_owner + 
-    vs_adam_q8_shard: each shard's owner computes the projection VJP of every
-    rank's views) against the dense one (vs_vjp_dense on every rank, then
-    vs_adam_q8_peer): the owner's rows equal the rank-order sums of the dense
-    rows, and both give the same replicas and moments bit for bit.  Ranks are
-    emulated on one device; the rasterizer rows are random, including rows of
-    splats whose visible mark is 0; a second step with a new epoch must ignore
-    the first step's rows."""
+    """The owner-side exchange (vs_vjp_owner + vs_adam_q8_shard: each shard's
+    owner computes the projection VJP of every rank's views from the views'
+    maps, visible marks, rasterizer rows and uniforms) against the dense one
+    (vs_vjp_dense on every rank, then vs_adam_q8_peer): the owner's rows equal
+    the rank-order sums of the dense rows, and both give the same replicas and
+    moments bit for bit.  Ranks are emulated on one device; the rasterizer rows
+    are random, including rows of splats whose visible mark is 0."""
     from vauss_b200.camera import look_at
     from tests.helpers import medium_scene
     sp, _ = medium_scene(seed=70 + world, n=4000)
@@ -198,59 +196,36 @@ def test_owner_vjp_exchange_matches_dense_exchange(cuda, world, views):
     cfg = ops.render_cfg(3, mip=True)
     rng = np.random.default_rng(world * 10 + views)
     t0, sh0, o0 = (torch.from_numpy(x).to(cuda) for x in (sp.transforms, sp.sh, sp.raw_opac))
-    bounds = [ViewParallelTrainer.shard_of(n, world, r) for r in range(world)]
-    cap = (max(e - b for b, e in bounds) + 3) // 4 * 4
-    # parts[o][r][k]: owner o's arrays for view k of rank r: [tag cap][visible cap][rows cap x 10]
-    parts = [[[torch.zeros(cap * 12, device=cuda) for _ in range(views)] for _ in range(world)] for _ in range(world)]
-    keep = []
-
-    def run_step(epoch, cams):
-        vs = N.ViewSet()
-        vs.world, vs.epoch = world, epoch
-        dense_rows, dense_vis = [], []
-        for r in range(world):
-            g_r = torch.zeros(n, width, device=cuda)
-            v_r = torch.zeros(n, device=cuda)
-            refine = torch.zeros(n, device=cuda)
-            for k in range(views):
-                out = ops.render(cams[r][k], cfg, t0, sh0, o0)
-                nv = out.num_visible
-                vc = torch.zeros(max(nv, 1), 10, device=cuda)
-                rows_h = (1e-3 * rng.standard_normal((nv, 10))).astype(np.float32)
-                rows_h[rng.random(nv) < 0.2] = 0.0
-                vc[:nv] = torch.from_numpy(rows_h).to(cuda)
-                ops.vjp_dense(out.frame, cfg, t0, sh0, o0, vc, g_r, refine, visible=out.visible, vis_accum=v_r)
-                d = N.ViewDest()
-                d.world, d.epoch = world, epoch
-                for o in range(world):
-                    d.shard_begin[o] = bounds[o][0]
-                    p = parts[o][r][k].data_ptr()
-                    d.tag[o], d.visible[o], d.v_combined[o] = p, p + 4 * cap, p + 8 * cap
-                d.shard_begin[world] = n
-                ops.view_scatter(out.frame, out.visible, vc, d)
-                uni = torch.zeros(N.UNIFORMS_BYTES // 4, dtype=torch.int32, device=cuda)
-                ops.frame_uniforms(out.frame, uni)
-                vs.uniforms[r * N.VIEW_SLOTS + k] = uni.data_ptr()
-                keep.extend([out, vc, uni])
-            vs.used[r] = views
-            dense_rows.append(g_r)
-            dense_vis.append(v_r)
-        torch.cuda.synchronize()
-        return vs, dense_rows, dense_vis
-
-    def cams_for(seed):
-        rr = np.random.default_rng(seed)
-        out = []
-        for _ in range(world):
-            row = []
-            for _ in range(views):
-                a = rr.uniform(0, 2 * np.pi)
-                row.append(look_at((4.0 * np.cos(a), 4.0 * np.sin(a), rr.uniform(-1, 1)), (0, 0, 0), 250, 170, 220.0))
-            out.append(row)
-        return out
-
-    run_step(1, cams_for(1))  # an earlier step whose rows stay behind in the owners' arrays
-    vs, dense_rows, dense_vis = run_step(2, cams_for(2))
+    vs = N.ViewSet()
+    vs.world = world
+    dense_rows, dense_vis, keep = [], [], []
+    for r in range(world):
+        g_r = torch.zeros(n, width, device=cuda)
+        v_r = torch.zeros(n, device=cuda)
+        refine = torch.zeros(n, device=cuda)
+        for k in range(views):
+            a = rng.uniform(0, 2 * np.pi)
+            cam = look_at((4.0 * np.cos(a), 4.0 * np.sin(a), rng.uniform(-1, 1)), (0, 0, 0), 250, 170, 220.0)
+            out = ops.render(cam, cfg, t0, sh0, o0)
+            nv = out.num_visible
+            vc = torch.zeros(n, 10, device=cuda)
+            rows_h = (1e-3 * rng.standard_normal((nv, 10))).astype(np.float32)
+            rows_h[rng.random(nv) < 0.2] = 0.0
+            vc[:nv] = torch.from_numpy(rows_h).to(cuda)
+            ops.vjp_dense(out.frame, cfg, t0, sh0, o0, vc[:max(nv, 1)], g_r, refine, visible=out.visible,
+                          vis_accum=v_r)
+            cmap = torch.empty(n, dtype=torch.int32, device=cuda)
+            out.frame.copy_field("compact_from_global", cmap)
+            uni = torch.zeros(N.UNIFORMS_BYTES // 4, dtype=torch.int32, device=cuda)
+            ops.frame_uniforms(out.frame, uni)
+            j = r * N.VIEW_SLOTS + k
+            vs.compact_from_global[j], vs.visible[j] = cmap.data_ptr(), out.visible.data_ptr()
+            vs.v_combined[j], vs.uniforms[j] = vc.data_ptr(), uni.data_ptr()
+            keep += [out, vc, cmap, uni]
+        vs.used[r] = views
+        dense_rows.append(g_r)
+        dense_vis.append(v_r)
+    torch.cuda.synchronize()
     lr_t = np.float32([1e-3] * 3 + [2e-3] * 4 + [5e-3] * 3)
     q8 = ops.q8_cfg(3, lr_t, 2.5e-3, 2.5e-4, 5e-2, opac_reg=1e-6, noise_scale=1e-3, noise_limit=0.01, noise_seed=5)
     mom_h = dict(t=_q8_host(n * 10, rng), sh=_q8_host(n * nc * 3, rng), o=_q8_host(n, rng))
@@ -279,14 +254,9 @@ def test_owner_vjp_exchange_matches_dense_exchange(cuda, world, views):
     rep_d, rep_o = replicas(), replicas()
     ps_d, ps_o = peer_set(rep_d, dense_rows, dense_vis), peer_set(rep_o)
     moms_d, moms_o = [], []
-    for o in range(world):
-        b, e = bounds[o]
-        for r in range(world):
-            for k in range(views):
-                p = parts[o][r][k].data_ptr()
-                j = r * N.VIEW_SLOTS + k
-                vs.tag[j], vs.visible[j], vs.v_combined[j] = p, p + 4 * cap, p + 8 * cap
-        ps_d.rank = ps_o.rank = o
+    for r in range(world):
+        b, e = ViewParallelTrainer.shard_of(n, world, r)
+        ps_d.rank = ps_o.rank = r
         md, mo = shard_moms(b, e), shard_moms(b, e)
         ops.adam_q8_peer(3, n, b, e, ps_d, md["t"], md["sh"], md["o"], q8, device=cuda)
         rows = torch.zeros(max(e - b, 1), width, device=cuda)
@@ -301,8 +271,8 @@ def test_owner_vjp_exchange_matches_dense_exchange(cuda, world, views):
             want_vis = (want_vis + _np(v_r)[b:e]).astype(np.float32)
             want = np.where((_np(v_r)[b:e] > 0)[:, None], want + _np(g_r)[b:e], want).astype(np.float32)
         seen = want_vis > 0
-        assert_bits_equal(_np(vis)[:e - b], want_vis, f"view counts of shard {o}")
-        assert_bits_equal(_np(rows)[:e - b][seen], want[seen], f"rows of shard {o}")
+        assert_bits_equal(_np(vis)[:e - b], want_vis, f"view counts of shard {r}")
+        assert_bits_equal(_np(rows)[:e - b][seen], want[seen], f"rows of shard {r}")
         moms_d.append(md)
         moms_o.append(mo)
     for r in range(world):

@@ -69,14 +69,9 @@ VIEW_SLOTS = 8
 UNIFORMS_BYTES = 256
 
 
-class ViewDest(ctypes.Structure):
-    _fields_ = [("world", ctypes.c_uint32), ("epoch", ctypes.c_uint32), ("shard_begin", ctypes.c_uint32 * (PEER_MAX + 1)),
-                ("tag", c_vp * PEER_MAX), ("visible", c_vp * PEER_MAX), ("v_combined", c_vp * PEER_MAX)]
-
-
 class ViewSet(ctypes.Structure):
-    _fields_ = [("world", ctypes.c_uint32), ("epoch", ctypes.c_uint32), ("used", ctypes.c_uint32 * PEER_MAX),
-                ("tag", c_vp * (PEER_MAX * VIEW_SLOTS)), ("visible", c_vp * (PEER_MAX * VIEW_SLOTS)),
+    _fields_ = [("world", ctypes.c_uint32), ("used", ctypes.c_uint32 * PEER_MAX),
+                ("compact_from_global", c_vp * (PEER_MAX * VIEW_SLOTS)), ("visible", c_vp * (PEER_MAX * VIEW_SLOTS)),
                 ("v_combined", c_vp * (PEER_MAX * VIEW_SLOTS)), ("uniforms", c_vp * (PEER_MAX * VIEW_SLOTS))]
 
 
@@ -150,7 +145,6 @@ _SIGS = {
     "vs_adam_q8_peer": ([c_vp, ctypes.c_uint32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint32,
                          ctypes.POINTER(PeerSet), Q8Tensor, Q8Tensor, Q8Tensor, ctypes.POINTER(Q8Cfg)], ctypes.c_int),
     "vs_frame_uniforms": ([c_vp, c_vp], ctypes.c_int),
-    "vs_view_scatter": ([c_vp, c_vp, c_vp, c_vp, ctypes.POINTER(ViewDest)], ctypes.c_int),
     "vs_vjp_owner": ([c_vp, ctypes.c_uint32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(ViewSet),
                       c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_adam_q8_shard": ([c_vp, ctypes.c_uint32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp,

@@ -307,15 +307,10 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
 }
 
 // ---- owner-side VJP of the view-parallel step ----
-// view_scatter_kernel (on the viewer, after the view's backward): one thread
-// per projected splat writes the splat's rasterizer row, visible mark and the
-// step's epoch into the owner's slot arrays (posted stores, over NVLink for
-// other ranks' shards).
-//
-// vjp_owner_kernel: one thread per splat of this rank's shard: every view of
-// every rank whose tag carries the epoch contributes its VJP (computed here
-// from this rank's replica, the view's uniforms and the row the viewer
-// wrote into this rank's memory).  The sums are the dense path's: per
+// One thread per splat of this rank's shard: every view of every rank that
+// projected the splat contributes its VJP (computed here from this rank's
+// replica and the view's uniforms, rasterizer row and visible mark, the last
+// three read from the viewer's memory).  The sums are the dense path's: per
 // rank over its views in slot order, the row restarting from +0 at the first
 // view that marks the splat visible (vs_vjp_dense's fresh row) and views with
 // an all-zero rasterizer row adding nothing; then over the ranks whose view
@@ -325,24 +320,6 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
 constexpr uint32_t OWNER_THREADS = 128;
 constexpr uint32_t OWNER_SLOTS = VS_PEER_MAX * VS_VIEW_SLOTS;
 static_assert(sizeof(Uniforms) <= VS_UNIFORMS_BYTES, "uniforms blob");
-
-__global__ void __launch_bounds__(256) view_scatter_kernel(uint32_t v, const uint32_t* __restrict__ global_from_compact,
-                                                           const float* __restrict__ visible,
-                                                           const float4* __restrict__ v_combined, vs_view_dest dest) {
-  const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= v) return;
-  const uint32_t g = global_from_compact[c];
-  uint32_t r = 0;
-  while (r + 1 < dest.world && g >= dest.shard_begin[r + 1]) ++r;
-  const size_t i = g - dest.shard_begin[r];
-  // rows are 10 floats: two 8-byte and two 16-byte pieces keep the stores aligned
-  const float* src = reinterpret_cast<const float*>(v_combined) + (size_t)c * 10;
-  float* dst = dest.v_combined[r] + i * 10;
-#pragma unroll
-  for (int q = 0; q < 10; q += 2) *reinterpret_cast<float2*>(dst + q) = *reinterpret_cast<const float2*>(src + q);
-  dest.visible[r][i] = visible[g];
-  dest.tag[r][i] = dest.epoch;
-}
 
 __global__ void __launch_bounds__(OWNER_THREADS, 4) vjp_owner_kernel(uint32_t begin, uint32_t end, int nc,
                                                                      vs_view_set views,
@@ -384,9 +361,9 @@ __global__ void __launch_bounds__(OWNER_THREADS, 4) vjp_owner_kernel(uint32_t be
     float vis_r = 0.0f;
     for (uint32_t k = 0; k < views.used[r]; ++k) {
       const uint32_t slot = r * VS_VIEW_SLOTS + k;
-      const size_t li = g - begin;
-      if (views.tag[slot][li] != views.epoch) continue;  // the view did not project the splat
-      const float visf = views.visible[slot][li];
+      const uint32_t c1 = views.compact_from_global[slot][g];
+      if (c1 == 0) continue;
+      const float visf = views.visible[slot][g];
       const bool fresh = vis_r == 0.0f && visf > 0.0f;
       vis_r = vis_r + visf;
       if (fresh) {  // the row restarts here (earlier views of this rank are overwritten)
@@ -394,7 +371,7 @@ __global__ void __launch_bounds__(OWNER_THREADS, 4) vjp_owner_kernel(uint32_t be
         for (int q = 0; q < 11; ++q) geo[q] = 0.0f;
         for (uint32_t i = 0; i < wsh; ++i) s_sh[i][tid] = 0.0f;
       }
-      const float* rg = views.v_combined[slot] + li * 10;
+      const float* rg = views.v_combined[slot] + (size_t)(c1 - 1) * 10;
       float rr[10];
       bool any = false;
 #pragma unroll
@@ -1150,40 +1127,17 @@ VS_API vs_status vs_vjp_owner(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degre
     if (views->used[r] > VS_VIEW_SLOTS) return vs_fail(ctx, VS_ERR_INVALID, "vjp_owner: %u views on rank %u", views->used[r], r);
     for (uint32_t k = 0; k < views->used[r]; ++k) {
       const uint32_t slot = r * VS_VIEW_SLOTS + k;
-      if (!views->tag[slot] || !views->visible[slot] || !views->v_combined[slot] || !views->uniforms[slot] ||
-          ((uintptr_t)views->uniforms[slot] & 3u))
+      if (!views->compact_from_global[slot] || !views->visible[slot] || !views->v_combined[slot] ||
+          !views->uniforms[slot] || ((uintptr_t)views->uniforms[slot] & 3u))
         return vs_fail(ctx, VS_ERR_INVALID, "vjp_owner: view slot %u of rank %u", k, r);
     }
   }
-  if (views->epoch == 0) return vs_fail(ctx, VS_ERR_INVALID, "vjp_owner: epoch 0 (reserved for never written)");
   if (splat_end == splat_begin) return VS_OK;
   const int nc = (sh_degree + 1) * (sh_degree + 1);
   vjp_owner_kernel<<<vs::div_up(splat_end - splat_begin, OWNER_THREADS), OWNER_THREADS, 0, ctx->stream>>>(
       splat_begin, splat_end, nc, *views, transforms, sh_coeffs, raw_opacities, min_scale, rows, vis);
   ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "vjp_owner launch");
-}
-
-VS_API vs_status vs_view_scatter(vs_ctx* ctx, vs_frame* frame, const float* visible, const float* v_combined,
-                                 const vs_view_dest* dest) {
-  if (!ctx) return VS_ERR_INVALID;
-  if (!frame || !frame->projected_ok || !dest || (frame->v && (!visible || !v_combined)))
-    return vs_fail(ctx, VS_ERR_INVALID, "view_scatter: bad arguments");
-  if (dest->world == 0 || dest->world > VS_PEER_MAX || dest->epoch == 0 || dest->shard_begin[0] != 0 ||
-      dest->shard_begin[dest->world] != frame->n)
-    return vs_fail(ctx, VS_ERR_INVALID, "view_scatter: world %u, epoch %u, shards do not cover the %u splats",
-                   dest->world, dest->epoch, frame->n);
-  if ((uintptr_t)v_combined & 7u) return vs_fail(ctx, VS_ERR_INVALID, "view_scatter: v_combined must be 8-byte aligned");
-  for (uint32_t r = 0; r < dest->world; ++r) {
-    if (dest->shard_begin[r] > dest->shard_begin[r + 1] || !dest->tag[r] || !dest->visible[r] || !dest->v_combined[r] ||
-        ((uintptr_t)dest->v_combined[r] & 7u))
-      return vs_fail(ctx, VS_ERR_INVALID, "view_scatter: destination of rank %u", r);
-  }
-  if (frame->v == 0) return VS_OK;
-  view_scatter_kernel<<<vs::div_up(frame->v, 256), 256, 0, ctx->stream>>>(
-      frame->v, (const uint32_t*)frame->global_from_compact.ptr, visible, (const float4*)v_combined, *dest);
-  ++ctx->launches;
-  return vs_cuda(ctx, cudaGetLastError(), "view_scatter launch");
 }
 
 VS_API vs_status vs_adam_q8_shard(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, uint32_t splat_begin,

@@ -389,13 +389,6 @@ def frame_uniforms(frame: Frame, dst: torch.Tensor):
     ctx.check(ctx.lib.vs_frame_uniforms(frame.h, _ptr(dst)))
 
 
-def view_scatter(frame: Frame, visible: torch.Tensor, v_combined: torch.Tensor, dest: N.ViewDest):
-    """Writes one view's rasterizer rows and visible marks, tagged with dest.epoch,
-    into the shard owners' slot arrays (vs_view_scatter)."""
-    ctx = frame.ctx.bind()
-    ctx.check(ctx.lib.vs_view_scatter(ctx.h, frame.h, _ptr(visible), _ptr(v_combined), ctypes.byref(dest)))
-
-
 def vjp_owner(sh_degree: int, num_splats: int, splat_begin: int, splat_end: int, views: N.ViewSet, transforms,
               sh_coeffs, raw_opacities, rows, vis, min_scale=None, device=None):
     """The shard owner's projection VJP over every rank's views of the step

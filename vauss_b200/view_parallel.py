@@ -10,15 +10,13 @@ whole batch; each rank then runs the same deterministic 8-bit-moment Adam, so
 the replicas stay bit-identical.
 
 Two exchanges are available.  With a `PeerGroup` (the GPU path) the
-parameter replicas live in buffers every rank maps over NVLink, and so do, on
-each rank and per (viewing rank, view slot), arrays that receive the
-rasterizer rows of the splats of that rank's shard: after each view's
-backward the viewer writes every projected splat's row, visible mark and the
-step's epoch into its owner's arrays (vs_view_scatter, 48 bytes per projected
-splat), and after a device barrier each rank computes the projection VJP of
-every rank's views for its own shard from its own memory (vs_vjp_owner), runs
-the 8-bit-moment Adam on that shard (vs_adam_q8_shard) and stores the new
-parameters into every replica; a second barrier ends the step.
+parameter replicas and, per view a rank renders, the view's projection map,
+visible marks, rasterizer gradient rows and uniforms live in buffers every rank
+maps over NVLink: after a device barrier each rank computes the projection VJP
+of every rank's views for its own shard of the splats (vs_vjp_owner, reading
+8 bytes per splat and view plus the 40-byte rasterizer rows of the splats a
+view saw), runs the 8-bit-moment Adam on that shard (vs_adam_q8_shard) and
+stores the new parameters into every replica; a second barrier ends the step.
 With one rank, or `owner_vjp=False`, each rank instead writes dense [N, 59]
 rows of its views that the shard owners read (vs_vjp_dense + vs_adam_q8_peer).
 Without a peer group, the dense gradient and the view counts go through one
@@ -81,10 +79,6 @@ class ViewParallelTrainer(SplatTrainer):
         self.flat = None
         self.peer_set = None
         self.view_set = None
-        # tags the owners' row arrays: grows by one per step on every rank and,
-        # unlike step_count, never goes back (a restored state must not match
-        # rows written by a step that was undone)
-        self._epoch = 0
 
     @staticmethod
     def shard_of(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -120,31 +114,19 @@ class ViewParallelTrainer(SplatTrainer):
         if self.owner_vjp:
             if not 1 <= views_per_rank <= N.VIEW_SLOTS:
                 raise ValueError(f"{views_per_rank} views per rank (at most {N.VIEW_SLOTS})")
-            bounds = [self.shard_of(n, g.world, r) for r in range(g.world)]
-            cap = (max(e - b for b, e in bounds) + 3) // 4 * 4  # 16-byte aligned parts
             vs = N.ViewSet()
             vs.world = g.world
-            self._dest, self._uni = [], []
+            self._slots = []
             for k in range(views_per_rank):
-                d = N.ViewDest()
-                d.world = g.world
+                a_cm, a_vis = g.alloc(n, i32), g.alloc(n, f32)
+                a_vc, a_u = g.alloc(n * 10, f32), g.alloc(N.UNIFORMS_BYTES // 4, i32)
                 for r in range(g.world):
-                    d.shard_begin[r] = bounds[r][0]
-                d.shard_begin[g.world] = n
-                # on every owner, per viewing rank: [tag cap][visible cap][rows cap x 10] (tags zeroed: epoch 0)
-                for r in range(g.world):
-                    a = g.alloc(cap * 12, f32, zero=True)
                     j = r * N.VIEW_SLOTS + k
-                    vs.tag[j], vs.visible[j], vs.v_combined[j] = a[g.rank], a[g.rank] + 4 * cap, a[g.rank] + 8 * cap
-                    if r == g.rank:  # this rank's view k goes to every owner's part for (this rank, k)
-                        for o in range(g.world):
-                            d.tag[o], d.visible[o], d.v_combined[o] = a[o], a[o] + 4 * cap, a[o] + 8 * cap
-                a_u = g.alloc(N.UNIFORMS_BYTES // 4, i32)
-                for r in range(g.world):
-                    vs.uniforms[r * N.VIEW_SLOTS + k] = a_u[r]
-                self._dest.append(d)
-                self._uni.append(g.local(a_u, N.UNIFORMS_BYTES // 4, i32))
-            self._slots = self._dest
+                    vs.compact_from_global[j], vs.visible[j] = a_cm[r], a_vis[r]
+                    vs.v_combined[j], vs.uniforms[j] = a_vc[r], a_u[r]
+                self._slots.append(dict(cmap=g.local(a_cm, n, i32), visible=g.local(a_vis, n, f32),
+                                        vc=g.local(a_vc, n * 10, f32).view(n, 10),
+                                        uni=g.local(a_u, N.UNIFORMS_BYTES // 4, i32)))
             self.view_set = vs
             self._rows = torch.zeros(max(m, 1), width, dtype=f32, device=self.device)
             self._row_vis = torch.zeros(max(m, 1), dtype=f32, device=self.device)
@@ -177,7 +159,6 @@ class ViewParallelTrainer(SplatTrainer):
         if self.optim is None:
             self._init_state(splats)
         self.step_count += 1
-        self._epoch = self._epoch % 0xFFFFFFFF + 1  # 1 .. 2^32 - 1: epoch 0 marks rows never written
         n = splats.num_splats
         width = 10 + splats.sh_coeffs.shape[1] * 3 + 1
         owner = self.owner_vjp
@@ -226,11 +207,11 @@ class ViewParallelTrainer(SplatTrainer):
             cam = b.camera
             cfg = ops.render_cfg(splats.sh_degree, mip=c.render_mode_mip, background=self.background(),
                                  has_min_scale=splats.min_scale is not None)
-            slot = len(losses)
+            slot = self._slots[len(losses)] if owner else None
             out = ops.render(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities,
                              min_scale=splats.min_scale, frame=self.frame,
                              out_img=self._buf("img", (cam.height, cam.width, 4), torch.float32),
-                             visible=self._buf("visible", (n,), torch.float32))
+                             visible=slot["visible"] if owner else self._buf("visible", (n,), torch.float32))
             mark("render")
             if ev is not None:
                 torch.cuda.current_stream(self.device).wait_event(ev)
@@ -238,14 +219,11 @@ class ViewParallelTrainer(SplatTrainer):
             losses.append(loss.loss.clone())
             mark("loss")
             vc = ops.rasterize_bwd(out.frame, out.out_img, loss.dl_dpred,
-                                   self._buf("v_combined", (max(n, 1), 10), torch.float32))
+                                   slot["vc"] if owner else self._buf("v_combined", (max(n, 1), 10), torch.float32))
             mark("raster_bwd")
-            if owner:  # the rows go to their owners now; the owners read the view's uniforms later
-                d = self._dest[slot]
-                d.epoch = self._epoch
-                ops.view_scatter(out.frame, out.visible, vc, d)
-                ops.frame_uniforms(out.frame, self._uni[slot])
-                mark("scatter")
+            if owner:  # what the shard owners read: the view's projection map and uniforms
+                out.frame.copy_field("compact_from_global", slot["cmap"])
+                ops.frame_uniforms(out.frame, slot["uni"])
             else:
                 ops.vjp_dense(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, grads,
                               refine, min_scale=splats.min_scale, visible=out.visible, vis_accum=vis)
@@ -266,7 +244,6 @@ class ViewParallelTrainer(SplatTrainer):
         if owner:
             for r in range(peer.world):
                 self.view_set.used[r] = len(batches)
-            self.view_set.epoch = self._epoch
             peer.barrier()  # every rank's views of this step are complete
             mark("barrier_rows")
             b0, b1 = self.shard
