@@ -280,7 +280,7 @@ class Leg:
             gather = (lambda b: gather_bytes_nccl(b, dev)) if world > 1 else (lambda b: [b])
             self.peer = PeerGroup(dev, world, rank, gather)
             self.trainer = ViewParallelTrainer(self.cfg, dev, peer=self.peer, **self.kw)
-            self.splats = self.trainer.adopt(splats, views_per_rank=len(self.views) if self.multiview else 1)
+            self.splats = self.trainer.adopt(splats)
             del splats
         else:
             self.trainer = SplatTrainer(self.cfg, dev, **self.kw)

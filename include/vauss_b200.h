@@ -290,46 +290,6 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
                                  uint32_t splat_end, const vs_peer_set* peers, vs_q8_tensor mom_t,
                                  vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8);
 
-/* Owner-side VJP exchange.  Instead of dense gradient rows, each rank keeps,
- * per view it rendered this step (up to VS_VIEW_SLOTS), the view's projection
- * map (VS_FIELD_COMPACT_FROM_GLOBAL), forward visible marks, rasterizer
- * gradient rows (vs_rasterize_backward) and uniforms (vs_frame_uniforms) in
- * buffers every rank maps; the rank that owns a shard of the splats then
- * computes the projection VJP of every view for its shard itself, reading only
- * 8 bytes per (splat, view) plus the 40-byte rows of the splats a view saw.
- * Slot index: rank * VS_VIEW_SLOTS + k, k < used[rank]. */
-#define VS_VIEW_SLOTS 8
-#define VS_UNIFORMS_BYTES 256
-typedef struct vs_view_set {
-  uint32_t world;
-  uint32_t used[VS_PEER_MAX];
-  const uint32_t* compact_from_global[VS_PEER_MAX * VS_VIEW_SLOTS]; /* [N] compact id + 1, 0 = not projected */
-  const float* visible[VS_PEER_MAX * VS_VIEW_SLOTS];                /* [N] forward visible marks */
-  const float* v_combined[VS_PEER_MAX * VS_VIEW_SLOTS];             /* [V, 10] rasterizer gradient rows */
-  const void* uniforms[VS_PEER_MAX * VS_VIEW_SLOTS];                /* VS_UNIFORMS_BYTES each */
-} vs_view_set;
-/* Copies the frame's projection uniforms (camera, image, render mode; at most
- * VS_UNIFORMS_BYTES) into device memory, stream-ordered. */
-VS_API vs_status vs_frame_uniforms(vs_frame* frame, void* dst_device);
-/* Dense gradient rows [splat_end - splat_begin, 10 + 3(d+1)^2 + 1] and view
- * counts [splat_end - splat_begin] of splats [splat_begin, splat_end): per
- * view the projection VJP of the splats it saw, summed per rank in slot order
- * and then over ranks in rank order -- bit for bit the rows the dense path
- * (vs_vjp_dense on each rank, then the rank-order sum of vs_adam_q8_peer)
- * gives.  transforms/sh_coeffs/raw_opacities/min_scale are this rank's replica;
- * rows of splats that no view saw are left as they were. */
-VS_API vs_status vs_vjp_owner(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, uint32_t splat_begin,
-                              uint32_t splat_end, const vs_view_set* views, const float* transforms,
-                              const float* sh_coeffs, const float* raw_opacities, const float* min_scale,
-                              float* rows, float* vis);
-/* vs_adam_q8_peer with this rank's own rows and view counts for its shard
- * (shard-relative, from vs_vjp_owner) instead of every rank's dense rows;
- * the new parameters go to every replica in `replicas` (its grads/vis unused). */
-VS_API vs_status vs_adam_q8_shard(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, uint32_t splat_begin,
-                                  uint32_t splat_end, const float* rows, const float* vis,
-                                  const vs_peer_set* replicas, vs_q8_tensor mom_t, vs_q8_tensor mom_sh,
-                                  vs_q8_tensor mom_o, const vs_q8_cfg* q8);
-
 /* ---- refinement: densify and prune -----------------------------------------
  * The GPU side of SplatTrainer::refine (crates/splat-train/src/train.rs:
  * 1779-2104, refine_splats :2110-2300); the sampling of parents and the

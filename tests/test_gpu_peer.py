@@ -177,108 +177,3 @@ def test_peer_adam_after_a_barrier_that_gave_up_touches_nothing(cuda):
     torch.cuda.synchronize()
     assert not np.array_equal(_np(reps[1][0])[:e], t0[:e])
     assert ctx.lib.vs_ctx_check(ctx.h) == 0
-
-
-@pytest.mark.parametrize("world,views", [(2, 2), (3, 1), (1, 3)])
-def test_owner_vjp_exchange_matches_dense_exchange(cuda, world, views):
-    """The owner-side exchange (vs_vjp_owner + vs_adam_q8_shard: each shard's
-    owner computes the projection VJP of every rank's views from the views'
-    maps, visible marks, rasterizer rows and uniforms) against the dense one
-    (vs_vjp_dense on every rank, then vs_adam_q8_peer): the owner's rows equal
-    the rank-order sums of the dense rows, and both give the same replicas and
-    moments bit for bit.  Ranks are emulated on one device; the rasterizer rows
-    are random, including rows of splats whose visible mark is 0."""
-    from vauss_b200.camera import look_at
-    from tests.helpers import medium_scene
-    sp, _ = medium_scene(seed=70 + world, n=4000)
-    n, nc = sp.n, sp.sh.shape[1]
-    width = 10 + nc * 3 + 1
-    cfg = ops.render_cfg(3, mip=True)
-    rng = np.random.default_rng(world * 10 + views)
-    t0, sh0, o0 = (torch.from_numpy(x).to(cuda) for x in (sp.transforms, sp.sh, sp.raw_opac))
-    vs = N.ViewSet()
-    vs.world = world
-    dense_rows, dense_vis, keep = [], [], []
-    for r in range(world):
-        g_r = torch.zeros(n, width, device=cuda)
-        v_r = torch.zeros(n, device=cuda)
-        refine = torch.zeros(n, device=cuda)
-        for k in range(views):
-            a = rng.uniform(0, 2 * np.pi)
-            cam = look_at((4.0 * np.cos(a), 4.0 * np.sin(a), rng.uniform(-1, 1)), (0, 0, 0), 250, 170, 220.0)
-            out = ops.render(cam, cfg, t0, sh0, o0)
-            nv = out.num_visible
-            vc = torch.zeros(n, 10, device=cuda)
-            rows_h = (1e-3 * rng.standard_normal((nv, 10))).astype(np.float32)
-            rows_h[rng.random(nv) < 0.2] = 0.0
-            vc[:nv] = torch.from_numpy(rows_h).to(cuda)
-            ops.vjp_dense(out.frame, cfg, t0, sh0, o0, vc[:max(nv, 1)], g_r, refine, visible=out.visible,
-                          vis_accum=v_r)
-            cmap = torch.empty(n, dtype=torch.int32, device=cuda)
-            out.frame.copy_field("compact_from_global", cmap)
-            uni = torch.zeros(N.UNIFORMS_BYTES // 4, dtype=torch.int32, device=cuda)
-            ops.frame_uniforms(out.frame, uni)
-            j = r * N.VIEW_SLOTS + k
-            vs.compact_from_global[j], vs.visible[j] = cmap.data_ptr(), out.visible.data_ptr()
-            vs.v_combined[j], vs.uniforms[j] = vc.data_ptr(), uni.data_ptr()
-            keep += [out, vc, cmap, uni]
-        vs.used[r] = views
-        dense_rows.append(g_r)
-        dense_vis.append(v_r)
-    torch.cuda.synchronize()
-    lr_t = np.float32([1e-3] * 3 + [2e-3] * 4 + [5e-3] * 3)
-    q8 = ops.q8_cfg(3, lr_t, 2.5e-3, 2.5e-4, 5e-2, opac_reg=1e-6, noise_scale=1e-3, noise_limit=0.01, noise_seed=5)
-    mom_h = dict(t=_q8_host(n * 10, rng), sh=_q8_host(n * nc * 3, rng), o=_q8_host(n, rng))
-
-    def replicas():
-        return [[x.clone() for x in (t0, sh0, o0)] for _ in range(world)]
-
-    def peer_set(reps, rows=None, vis=None):
-        ps = N.PeerSet()
-        ps.world = world
-        for r in range(world):
-            ps.transforms[r], ps.sh_coeffs[r], ps.raw_opacities[r] = (x.data_ptr() for x in reps[r])
-            if rows is not None:
-                ps.grads[r], ps.vis[r] = rows[r].data_ptr(), vis[r].data_ptr()
-        return ps
-
-    def shard_moms(b, e):
-        out = {}
-        for key, per in (("t", 10), ("sh", nc * 3), ("o", 1)):
-            h = mom_h[key]
-            out[key] = _q8_dev(dict(mc=h["mc"][b * per:e * per], vc=h["vc"][b * per:e * per],
-                                    ms=h["ms"][b * per // 256:(e * per + 255) // 256],
-                                    vs=h["vs"][b * per // 256:(e * per + 255) // 256]), cuda)
-        return out
-
-    rep_d, rep_o = replicas(), replicas()
-    ps_d, ps_o = peer_set(rep_d, dense_rows, dense_vis), peer_set(rep_o)
-    moms_d, moms_o = [], []
-    for r in range(world):
-        b, e = ViewParallelTrainer.shard_of(n, world, r)
-        ps_d.rank = ps_o.rank = r
-        md, mo = shard_moms(b, e), shard_moms(b, e)
-        ops.adam_q8_peer(3, n, b, e, ps_d, md["t"], md["sh"], md["o"], q8, device=cuda)
-        rows = torch.zeros(max(e - b, 1), width, device=cuda)
-        vis = torch.zeros(max(e - b, 1), device=cuda)
-        ops.vjp_owner(3, n, b, e, vs, t0, sh0, o0, rows, vis, device=cuda)
-        ops.adam_q8_shard(3, n, b, e, rows, vis, ps_o, mo["t"], mo["sh"], mo["o"], q8, device=cuda)
-        torch.cuda.synchronize()
-        # rows: the rank-order sum of the dense rows of the ranks that saw the splat
-        want_vis = np.zeros(e - b, np.float32)
-        want = np.zeros((e - b, width), np.float32)
-        for v_r, g_r in zip(dense_vis, dense_rows):
-            want_vis = (want_vis + _np(v_r)[b:e]).astype(np.float32)
-            want = np.where((_np(v_r)[b:e] > 0)[:, None], want + _np(g_r)[b:e], want).astype(np.float32)
-        seen = want_vis > 0
-        assert_bits_equal(_np(vis)[:e - b], want_vis, f"view counts of shard {r}")
-        assert_bits_equal(_np(rows)[:e - b][seen], want[seen], f"rows of shard {r}")
-        moms_d.append(md)
-        moms_o.append(mo)
-    for r in range(world):
-        for i, name in enumerate(("transforms", "sh", "opacity")):
-            assert_bits_equal(_np(rep_o[r][i]), _np(rep_d[r][i]), f"{name} replica {r}")
-    for md, mo in zip(moms_d, moms_o):
-        for key in ("t", "sh", "o"):
-            assert_bits_equal(_np(mo[key].m_codes), _np(md[key].m_codes), f"{key} m codes")
-            assert_bits_equal(_np(mo[key].v_scales), _np(md[key].v_scales), f"{key} v scales")

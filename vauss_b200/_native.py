@@ -65,16 +65,6 @@ class PeerSet(ctypes.Structure):
                 ("raw_opacities", c_vp * PEER_MAX)]
 
 
-VIEW_SLOTS = 8
-UNIFORMS_BYTES = 256
-
-
-class ViewSet(ctypes.Structure):
-    _fields_ = [("world", ctypes.c_uint32), ("used", ctypes.c_uint32 * PEER_MAX),
-                ("compact_from_global", c_vp * (PEER_MAX * VIEW_SLOTS)), ("visible", c_vp * (PEER_MAX * VIEW_SLOTS)),
-                ("v_combined", c_vp * (PEER_MAX * VIEW_SLOTS)), ("uniforms", c_vp * (PEER_MAX * VIEW_SLOTS))]
-
-
 class RefineCfg(ctypes.Structure):
     _fields_ = [("min_opacity", ctypes.c_float), ("max_bound", ctypes.c_float), ("center", ctypes.c_float * 3),
                 ("split_at_screen_size", ctypes.c_float)]
@@ -144,11 +134,6 @@ _SIGS = {
     "vs_ctx_check": ([c_vp], ctypes.c_int),
     "vs_adam_q8_peer": ([c_vp, ctypes.c_uint32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint32,
                          ctypes.POINTER(PeerSet), Q8Tensor, Q8Tensor, Q8Tensor, ctypes.POINTER(Q8Cfg)], ctypes.c_int),
-    "vs_frame_uniforms": ([c_vp, c_vp], ctypes.c_int),
-    "vs_vjp_owner": ([c_vp, ctypes.c_uint32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(ViewSet),
-                      c_vp, c_vp, c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
-    "vs_adam_q8_shard": ([c_vp, ctypes.c_uint32, ctypes.c_int32, ctypes.c_uint32, ctypes.c_uint32, c_vp, c_vp,
-                          ctypes.POINTER(PeerSet), Q8Tensor, Q8Tensor, Q8Tensor, ctypes.POINTER(Q8Cfg)], ctypes.c_int),
     "vs_refine_table": ([c_vp, ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint32, ctypes.c_int32, c_vp, c_vp, c_vp, c_vp,
                          ctypes.POINTER(RefineCfg), c_vp], ctypes.c_int),
     "vs_refine_split": ([c_vp, ctypes.c_uint32, c_vp, c_vp, ctypes.c_uint32, ctypes.c_int32, c_vp, ctypes.c_uint32,

@@ -306,108 +306,6 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
   refine[g] += clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
 }
 
-// ---- owner-side VJP of the view-parallel step ----
-// One thread per splat of this rank's shard: every view of every rank that
-// projected the splat contributes its VJP (computed here from this rank's
-// replica and the view's uniforms, rasterizer row and visible mark, the last
-// three read from the viewer's memory).  The sums are the dense path's: per
-// rank over its views in slot order, the row restarting from +0 at the first
-// view that marks the splat visible (vs_vjp_dense's fresh row) and views with
-// an all-zero rasterizer row adding nothing; then over the ranks whose view
-// count is non-zero, in rank order from +0 -- so the rows equal, bit for bit,
-// what vs_vjp_dense on every rank followed by the rank-order sum of the
-// sharded Adam gives.  The SH part of a rank's row is built in shared memory.
-constexpr uint32_t OWNER_THREADS = 128;
-constexpr uint32_t OWNER_SLOTS = VS_PEER_MAX * VS_VIEW_SLOTS;
-static_assert(sizeof(Uniforms) <= VS_UNIFORMS_BYTES, "uniforms blob");
-
-__global__ void __launch_bounds__(OWNER_THREADS, 4) vjp_owner_kernel(uint32_t begin, uint32_t end, int nc,
-                                                                     vs_view_set views,
-                                                                     const float* __restrict__ transforms,
-                                                                     const float* __restrict__ sh,
-                                                                     const float* __restrict__ raw_opac,
-                                                                     const float* __restrict__ min_scale,
-                                                                     float* __restrict__ rows,
-                                                                     float* __restrict__ vis_out) {
-  __shared__ Uniforms s_u[OWNER_SLOTS];
-  __shared__ float s_sh[48][OWNER_THREADS];  // this rank's SH row of each thread's splat, component-major
-  const uint32_t tid = threadIdx.x;
-  constexpr uint32_t UW = sizeof(Uniforms) / 4;
-  for (uint32_t r = 0; r < views.world; ++r)
-    for (uint32_t i = tid; i < views.used[r] * UW; i += OWNER_THREADS) {
-      const uint32_t slot = r * VS_VIEW_SLOTS + i / UW;
-      reinterpret_cast<uint32_t*>(&s_u[slot])[i % UW] = reinterpret_cast<const uint32_t*>(views.uniforms[slot])[i % UW];
-    }
-  __syncthreads();
-  const uint32_t g = begin + blockIdx.x * OWNER_THREADS + tid;
-  if (g >= end) return;
-  const uint32_t wsh = 3u * (uint32_t)nc;
-  const size_t width = 10u + wsh + 1u;
-  float tt[10];
-#pragma unroll
-  for (int k = 0; k < 10; ++k) tt[k] = transforms[(size_t)g * 10 + k];
-  const float raw = raw_opac[g];
-  float tot[11];
-#pragma unroll
-  for (int k = 0; k < 11; ++k) tot[k] = 0.0f;
-  float vis_tot = 0.0f;
-  bool have = false;
-  float* d = rows + (size_t)(g - begin) * width;
-  for (uint32_t r = 0; r < views.world; ++r) {
-    float geo[11];
-#pragma unroll
-    for (int k = 0; k < 11; ++k) geo[k] = 0.0f;
-    for (uint32_t i = 0; i < wsh; ++i) s_sh[i][tid] = 0.0f;
-    float vis_r = 0.0f;
-    for (uint32_t k = 0; k < views.used[r]; ++k) {
-      const uint32_t slot = r * VS_VIEW_SLOTS + k;
-      const uint32_t c1 = views.compact_from_global[slot][g];
-      if (c1 == 0) continue;
-      const float visf = views.visible[slot][g];
-      const bool fresh = vis_r == 0.0f && visf > 0.0f;
-      vis_r = vis_r + visf;
-      if (fresh) {  // the row restarts here (earlier views of this rank are overwritten)
-#pragma unroll
-        for (int q = 0; q < 11; ++q) geo[q] = 0.0f;
-        for (uint32_t i = 0; i < wsh; ++i) s_sh[i][tid] = 0.0f;
-      }
-      const float* rg = views.v_combined[slot] + (size_t)(c1 - 1) * 10;
-      float rr[10];
-      bool any = false;
-#pragma unroll
-      for (int q = 0; q < 10; ++q) {
-        rr[q] = rg[q];
-        any = any || rr[q] != 0.0f;
-      }
-      if (!any) continue;
-      const VjpOut o = splat_vjp(tt, raw, sh, min_scale, g, rr, s_u[slot]);
-      const float gv[11] = {o.v_mean.x, o.v_mean.y, o.v_mean.z, o.v_q.w, o.v_q.x, o.v_q.y, o.v_q.z,
-                            o.v_scale.x, o.v_scale.y, o.v_scale.z, o.v_raw};
-#pragma unroll
-      for (int q = 0; q < 11; ++q) geo[q] = geo[q] + gv[q];
-      float b[16];
-      sh_basis_all(o.dir.x, o.dir.y, o.dir.z, b);
-      for (int kk = 0; kk < nc; ++kk) {
-#pragma unroll
-        for (int q = 0; q < 3; ++q) s_sh[kk * 3 + q][tid] = s_sh[kk * 3 + q][tid] + rr[5 + q] * b[kk];
-      }
-    }
-    vis_tot = vis_tot + vis_r;
-    if (vis_r > 0.0f) {
-#pragma unroll
-      for (int q = 0; q < 11; ++q) tot[q] = tot[q] + geo[q];
-      for (uint32_t i = 0; i < wsh; ++i) d[10 + i] = (have ? d[10 + i] : 0.0f) + s_sh[i][tid];
-      have = true;
-    }
-  }
-  if (have) {
-#pragma unroll
-    for (int q = 0; q < 10; ++q) d[q] = tot[q];
-    d[width - 1] = tot[10];
-  }
-  vis_out[g - begin] = vis_tot;
-}
-
 // ---- single-view VJP rows (the first half of the fused Q8 step) ----
 // One row of VJP_ROW floats per visible splat, in compact (projection) order:
 // 0-9 transforms gradient, 10 raw-opacity gradient, 11-13 colour gradient
@@ -486,9 +384,6 @@ struct Q8Args {
 // zero offsets otherwise.
 struct PeerArgs {
   uint32_t world, rank;
-  // gradient row sources summed in order (world for the dense exchange, 1 for
-  // the owner's own rows) and the splat their rows start at
-  uint32_t sources, row_off;
   // the ctx's device error word: a barrier before this launch that gave up
   // sets VS_DERR_WAIT there, and the update then touches nothing
   const uint32_t* err;
@@ -612,7 +507,7 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
         } else if (MODE == 2) {
           // every rank's load is issued before the sum, which runs in rank order
           const uint32_t vm = ok ? sm.vmask[s] : 0u;
-          const size_t off = ((size_t)(t_base / W) + s - pa.row_off) * width + 10u + col;
+          const size_t off = ((size_t)(t_base / W) + s) * width + 10u + col;
           float tv[VS_PEER_MAX];
 #pragma unroll
           for (uint32_t r = 0; r < VS_PEER_MAX; ++r) tv[r] = ((vm >> r) & 1u) ? pa.grads[r][off] : 0.0f;
@@ -785,14 +680,14 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
     if (g < n) {
       if (MODE == 2) {
         uint32_t vm = 0;
-        for (uint32_t r = 0; r < pa.sources; ++r) {
-          const float vr = pa.vis[r][g - pa.row_off];
+        for (uint32_t r = 0; r < pa.world; ++r) {
+          const float vr = pa.vis[r][g];
           if (vr > 0.0f) vm |= 1u << r;
           vis_g += vr;
         }
-        for (uint32_t r = 0; r < pa.sources; ++r) {
+        for (uint32_t r = 0; r < pa.world; ++r) {
           if (!((vm >> r) & 1u)) continue;
-          const float* d = pa.grads[r] + (size_t)(g - pa.row_off) * width;
+          const float* d = pa.grads[r] + (size_t)g * width;
 #pragma unroll
           for (int k = 0; k < 10; ++k) gr[k] += d[k];
           go += d[width - 1];
@@ -1084,8 +979,6 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
   PeerArgs pa{};
   pa.world = peers->world;
   pa.rank = peers->rank;
-  pa.sources = peers->world;
-  pa.row_off = 0;
   pa.err = ctx->d_err;
   pa.cta_begin = splat_begin / Q8_SPLATS;
   pa.m_off = splat_begin;
@@ -1111,79 +1004,6 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
       to_q8(mom_o), a, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, pa);
   ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "adam_q8_peer launch");
-}
-
-VS_API vs_status vs_vjp_owner(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, uint32_t splat_begin,
-                              uint32_t splat_end, const vs_view_set* views, const float* transforms,
-                              const float* sh_coeffs, const float* raw_opacities, const float* min_scale,
-                              float* rows, float* vis) {
-  if (!ctx) return VS_ERR_INVALID;
-  if (!views || !transforms || !sh_coeffs || !raw_opacities || !rows || !vis || sh_degree < 0 || sh_degree > 3)
-    return vs_fail(ctx, VS_ERR_INVALID, "vjp_owner: bad arguments");
-  if (views->world == 0 || views->world > VS_PEER_MAX || splat_begin > splat_end || splat_end > num_splats)
-    return vs_fail(ctx, VS_ERR_INVALID, "vjp_owner: world %u, shard [%u, %u) of %u", views->world, splat_begin,
-                   splat_end, num_splats);
-  for (uint32_t r = 0; r < views->world; ++r) {
-    if (views->used[r] > VS_VIEW_SLOTS) return vs_fail(ctx, VS_ERR_INVALID, "vjp_owner: %u views on rank %u", views->used[r], r);
-    for (uint32_t k = 0; k < views->used[r]; ++k) {
-      const uint32_t slot = r * VS_VIEW_SLOTS + k;
-      if (!views->compact_from_global[slot] || !views->visible[slot] || !views->v_combined[slot] ||
-          !views->uniforms[slot] || ((uintptr_t)views->uniforms[slot] & 3u))
-        return vs_fail(ctx, VS_ERR_INVALID, "vjp_owner: view slot %u of rank %u", k, r);
-    }
-  }
-  if (splat_end == splat_begin) return VS_OK;
-  const int nc = (sh_degree + 1) * (sh_degree + 1);
-  vjp_owner_kernel<<<vs::div_up(splat_end - splat_begin, OWNER_THREADS), OWNER_THREADS, 0, ctx->stream>>>(
-      splat_begin, splat_end, nc, *views, transforms, sh_coeffs, raw_opacities, min_scale, rows, vis);
-  ++ctx->launches;
-  return vs_cuda(ctx, cudaGetLastError(), "vjp_owner launch");
-}
-
-VS_API vs_status vs_adam_q8_shard(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, uint32_t splat_begin,
-                                  uint32_t splat_end, const float* rows, const float* vis,
-                                  const vs_peer_set* replicas, vs_q8_tensor mom_t, vs_q8_tensor mom_sh,
-                                  vs_q8_tensor mom_o, const vs_q8_cfg* q8) {
-  if (!ctx) return VS_ERR_INVALID;
-  if (!q8 || !replicas || !rows || !vis || !q8_valid(mom_t) || !q8_valid(mom_sh) || !q8_valid(mom_o) ||
-      sh_degree < 0 || sh_degree > 3)
-    return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_shard: bad arguments");
-  if (replicas->world == 0 || replicas->world > VS_PEER_MAX || replicas->rank >= replicas->world)
-    return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_shard: world %u rank %u", replicas->world, replicas->rank);
-  if (splat_begin % Q8_SPLATS != 0 || splat_begin > splat_end || splat_end > num_splats)
-    return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_shard: shard [%u, %u) of %u splats", splat_begin, splat_end,
-                   num_splats);
-  const uint64_t count_sh = (uint64_t)num_splats * 3 * (sh_degree + 1) * (sh_degree + 1);
-  if (count_sh >= 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "adam_q8_shard: %llu SH values exceed u32 indexing", (unsigned long long)count_sh);
-  PeerArgs pa{};
-  pa.world = replicas->world;
-  pa.rank = replicas->rank;
-  pa.sources = 1;
-  pa.row_off = splat_begin;
-  pa.err = ctx->d_err;
-  pa.cta_begin = splat_begin / Q8_SPLATS;
-  pa.m_off = splat_begin;
-  pa.grads[0] = rows;
-  pa.vis[0] = vis;
-  for (uint32_t r = 0; r < replicas->world; ++r) {
-    if (!replicas->transforms[r] || !replicas->sh_coeffs[r] || !replicas->raw_opacities[r])
-      return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_shard: null replica of rank %u", r);
-    if (!q8_aligned(replicas->transforms[r], replicas->sh_coeffs[r], replicas->raw_opacities[r], mom_t, mom_sh, mom_o))
-      return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_shard: parameter and code arrays must be 16-byte aligned");
-    pa.t[r] = replicas->transforms[r];
-    pa.sh[r] = replicas->sh_coeffs[r];
-    pa.o[r] = replicas->raw_opacities[r];
-  }
-  if (splat_end == splat_begin) return VS_OK;
-  vs::Uniforms u{};
-  u.sh_degree = sh_degree;
-  const Q8Args a = to_args(*q8);
-  const uint32_t me = replicas->rank;
-  q8_kernel<2><<<vs::div_up(splat_end - splat_begin, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
-      u, splat_end, pa.t[me], pa.sh[me], pa.o[me], nullptr, nullptr, nullptr, to_q8(mom_t), to_q8(mom_sh),
-      to_q8(mom_o), a, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, pa);
-  ++ctx->launches;
-  return vs_cuda(ctx, cudaGetLastError(), "adam_q8_shard launch");
 }
 
 VS_API vs_status vs_gather_stats(vs_ctx* ctx, uint32_t n, float* refine_norm, float* vis_count, float* max_screen,

@@ -158,17 +158,6 @@ VS_API void vs_frame_destroy(vs_frame* f) {
   delete f;
 }
 
-VS_API vs_status vs_frame_uniforms(vs_frame* f, void* dst_device) {
-  if (!f) return VS_ERR_INVALID;
-  if (!f->projected_ok) return vs_fail(f->ctx, VS_ERR_INVALID, "frame_uniforms: frame has not been projected");
-  if (!dst_device) return vs_fail(f->ctx, VS_ERR_INVALID, "frame_uniforms: null destination");
-  static_assert(sizeof(vs::Uniforms) <= VS_UNIFORMS_BYTES, "uniforms blob");
-  VS_TRY(vs_cuda(f->ctx, cudaSetDevice(f->ctx->device), "cudaSetDevice"));
-  // from pageable memory: the copy reads the source before the call returns
-  return vs_cuda(f->ctx, cudaMemcpyAsync(dst_device, &f->u, sizeof(vs::Uniforms), cudaMemcpyHostToDevice,
-                                         f->ctx->stream), "frame_uniforms");
-}
-
 VS_API vs_status vs_frame_counts(const vs_frame* f, vs_render_counts* out) {
   if (!f || !out) return VS_ERR_INVALID;
   out->num_visible = f->v;

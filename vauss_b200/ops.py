@@ -108,16 +108,6 @@ class Frame:
     def num_intersections(self) -> int:
         return int(self.counts.num_intersections)
 
-    def copy_field(self, name: str, dst: torch.Tensor):
-        """Copies one frame buffer into ``dst`` (device, stream-ordered)."""
-        p = ctypes.c_void_p()
-        n = ctypes.c_uint64()
-        fid = N.FIELDS[name]
-        self.ctx.check(self.ctx.lib.vs_frame_buffer(self.h, fid, ctypes.byref(p), ctypes.byref(n)))
-        nbytes = int(n.value) * 4
-        assert dst.numel() * dst.element_size() >= nbytes and dst.is_cuda and dst.is_contiguous()
-        self.ctx.check(self.ctx.lib.vs_frame_copy(self.h, fid, _ptr(dst), ctypes.c_uint64(nbytes)))
-
     def field(self, name: str) -> torch.Tensor:
         """A copy of one frame buffer as a CUDA tensor (u32 fields as int32)."""
         p = ctypes.c_void_p()
@@ -379,33 +369,6 @@ def adam_q8_peer(sh_degree: int, num_splats: int, splat_begin: int, splat_end: i
     ctx = context(device)
     ctx.check(ctx.lib.vs_adam_q8_peer(ctx.h, num_splats, sh_degree, splat_begin, splat_end, ctypes.byref(peers),
                                       mom_t.c(), mom_sh.c(), mom_o.c(), ctypes.byref(q8)))
-
-
-def frame_uniforms(frame: Frame, dst: torch.Tensor):
-    """Copies the frame's projection uniforms into ``dst`` (a device buffer of at least
-    UNIFORMS_BYTES bytes), stream-ordered."""
-    ctx = frame.ctx.bind()
-    assert dst.numel() * dst.element_size() >= N.UNIFORMS_BYTES
-    ctx.check(ctx.lib.vs_frame_uniforms(frame.h, _ptr(dst)))
-
-
-def vjp_owner(sh_degree: int, num_splats: int, splat_begin: int, splat_end: int, views: N.ViewSet, transforms,
-              sh_coeffs, raw_opacities, rows, vis, min_scale=None, device=None):
-    """The shard owner's projection VJP over every rank's views of the step
-    (vs_vjp_owner): dense rows and view counts of splats [begin, end)."""
-    ctx = context(device)
-    ctx.check(ctx.lib.vs_vjp_owner(ctx.h, num_splats, sh_degree, splat_begin, splat_end, ctypes.byref(views),
-                                   _ptr(transforms), _ptr(sh_coeffs), _ptr(raw_opacities), _ptr(min_scale),
-                                   _ptr(rows), _ptr(vis)))
-
-
-def adam_q8_shard(sh_degree: int, num_splats: int, splat_begin: int, splat_end: int, rows, vis, replicas: N.PeerSet,
-                  mom_t: Q8Moments, mom_sh: Q8Moments, mom_o: Q8Moments, q8: N.Q8Cfg, device=None):
-    """Sharded Q8 Adam from this rank's own shard rows (vs_adam_q8_shard); the new
-    parameters go to every replica of ``replicas``."""
-    ctx = context(device)
-    ctx.check(ctx.lib.vs_adam_q8_shard(ctx.h, num_splats, sh_degree, splat_begin, splat_end, _ptr(rows), _ptr(vis),
-                                       ctypes.byref(replicas), mom_t.c(), mom_sh.c(), mom_o.c(), ctypes.byref(q8)))
 
 
 def gather_stats(refine_norm, vis_count, max_screen, refine_weight, visible, radius):

@@ -9,19 +9,15 @@ one all-reduce (sum) over the ranks gives every replica the gradient of the
 whole batch; each rank then runs the same deterministic 8-bit-moment Adam, so
 the replicas stay bit-identical.
 
-Two exchanges are available.  With a `PeerGroup` (the GPU path) the
-parameter replicas and, per view a rank renders, the view's projection map,
-visible marks, rasterizer gradient rows and uniforms live in buffers every rank
-maps over NVLink: after a device barrier each rank computes the projection VJP
-of every rank's views for its own shard of the splats (vs_vjp_owner, reading
-8 bytes per splat and view plus the 40-byte rasterizer rows of the splats a
-view saw), runs the 8-bit-moment Adam on that shard (vs_adam_q8_shard) and
-stores the new parameters into every replica; a second barrier ends the step.
-With one rank, or `owner_vjp=False`, each rank instead writes dense [N, 59]
-rows of its views that the shard owners read (vs_vjp_dense + vs_adam_q8_peer).
-Without a peer group, the dense gradient and the view counts go through one
-flat all-reduce (`exchange`, injectable so the host logic runs with gloo ranks
-on the CPU) and every rank runs the full replicated Adam.
+Two exchanges are available.  With a `PeerGroup` (the GPU path) the ranks'
+gradient rows, view counts and parameter replicas live in buffers every rank
+maps over NVLink: after a device barrier each rank runs the 8-bit-moment Adam
+on its shard of the splats only (vs_adam_q8_peer), summing the rows of the
+ranks that saw each splat straight from their memory and storing the new
+parameters into every replica, and a second barrier ends the step.  Without
+one, the dense gradient and the view counts go through one flat all-reduce
+(`exchange`, injectable so the host logic runs with gloo ranks on the CPU) and
+every rank runs the full replicated Adam.
 """
 from __future__ import annotations
 
@@ -69,16 +65,13 @@ class ViewParallelTrainer(SplatTrainer):
     dense gradient before the replicated Q8 Adam step."""
 
     def __init__(self, config: TrainConfig, device, exchange: Callable[[torch.Tensor], None] = all_reduce_sum,
-                 peer: PeerGroup | None = None, owner_vjp: bool = True, **kw):
+                 peer: PeerGroup | None = None, **kw):
         assert config.optimizer == "q8", "the view-parallel path steps the 8-bit m+v optimizer"
         super().__init__(config, device, **kw)
         self.exchange = exchange
         self.peer = peer
-        # one rank has no NVLink traffic to save, and the dense rows are cheaper there
-        self.owner_vjp = owner_vjp and peer is not None and peer.world > 1
         self.flat = None
         self.peer_set = None
-        self.view_set = None
 
     @staticmethod
     def shard_of(n: int, world: int, rank: int) -> tuple[int, int]:
@@ -87,57 +80,35 @@ class ViewParallelTrainer(SplatTrainer):
         b0, b1 = rank * blocks // world, (rank + 1) * blocks // world
         return b0 * 256, min(b1 * 256, n)
 
-    def adopt(self, splats: Splats, views_per_rank: int = 1) -> Splats:
+    def adopt(self, splats: Splats) -> Splats:
         """With a peer group, copies the splats (identical on every rank) into
         replicas that all ranks map and returns them; step_views must be given
-        the returned splats, with at most `views_per_rank` views per call (the
-        same count on every rank).  Without one, returns `splats` unchanged."""
+        the returned splats.  Without one, returns `splats` unchanged."""
         if self.peer is None:
             return splats
         g, n = self.peer, splats.num_splats
         nc = splats.sh_coeffs.shape[1]
         width = 10 + nc * 3 + 1
-        f32, i32 = torch.float32, torch.int32
+        f32 = torch.float32
         addr_t, addr_sh, addr_o = g.alloc(n * 10, f32), g.alloc(n * nc * 3, f32), g.alloc(n, f32)
+        addr_g = g.alloc(n * width, f32, zero=True)
+        addr_v = g.alloc(n, f32, zero=True)
         t = g.local(addr_t, n * 10, f32).view(n, 10)
         sh = g.local(addr_sh, n * nc * 3, f32).view(n, nc, 3)
         o = g.local(addr_o, n, f32)
         t.copy_(splats.transforms)
         sh.copy_(splats.sh_coeffs.float())
         o.copy_(splats.raw_opacities)
+        self._grads = g.local(addr_g, n * width, f32).view(n, width)
+        self._vis = g.local(addr_v, n, f32)
         ps = N.PeerSet()
         ps.world, ps.rank = g.world, g.rank
         for r in range(g.world):
+            ps.grads[r], ps.vis[r] = addr_g[r], addr_v[r]
             ps.transforms[r], ps.sh_coeffs[r], ps.raw_opacities[r] = addr_t[r], addr_sh[r], addr_o[r]
+        self.peer_set = ps
         self.shard = self.shard_of(n, g.world, g.rank)
         m = self.shard[1] - self.shard[0]
-        if self.owner_vjp:
-            if not 1 <= views_per_rank <= N.VIEW_SLOTS:
-                raise ValueError(f"{views_per_rank} views per rank (at most {N.VIEW_SLOTS})")
-            vs = N.ViewSet()
-            vs.world = g.world
-            self._slots = []
-            for k in range(views_per_rank):
-                a_cm, a_vis = g.alloc(n, i32), g.alloc(n, f32)
-                a_vc, a_u = g.alloc(n * 10, f32), g.alloc(N.UNIFORMS_BYTES // 4, i32)
-                for r in range(g.world):
-                    j = r * N.VIEW_SLOTS + k
-                    vs.compact_from_global[j], vs.visible[j] = a_cm[r], a_vis[r]
-                    vs.v_combined[j], vs.uniforms[j] = a_vc[r], a_u[r]
-                self._slots.append(dict(cmap=g.local(a_cm, n, i32), visible=g.local(a_vis, n, f32),
-                                        vc=g.local(a_vc, n * 10, f32).view(n, 10),
-                                        uni=g.local(a_u, N.UNIFORMS_BYTES // 4, i32)))
-            self.view_set = vs
-            self._rows = torch.zeros(max(m, 1), width, dtype=f32, device=self.device)
-            self._row_vis = torch.zeros(max(m, 1), dtype=f32, device=self.device)
-        else:
-            addr_g = g.alloc(n * width, f32, zero=True)
-            addr_v = g.alloc(n, f32, zero=True)
-            self._grads = g.local(addr_g, n * width, f32).view(n, width)
-            self._vis = g.local(addr_v, n, f32)
-            for r in range(g.world):
-                ps.grads[r], ps.vis[r] = addr_g[r], addr_v[r]
-        self.peer_set = ps
         self.optim = dict(t=ops.Q8Moments(m * 10, self.device), sh=ops.Q8Moments(m * nc * 3, self.device),
                           o=ops.Q8Moments(m, self.device), time=0)
         self.record = None
@@ -161,12 +132,7 @@ class ViewParallelTrainer(SplatTrainer):
         self.step_count += 1
         n = splats.num_splats
         width = 10 + splats.sh_coeffs.shape[1] * 3 + 1
-        owner = self.owner_vjp
-        if owner and len(batches) > len(self._slots):
-            raise ValueError(f"{len(batches)} views in one step; adopt() was given {len(self._slots)} per rank")
-        if owner:
-            grads = vis = None
-        elif peer is not None:
+        if peer is not None:
             # rows are overwritten where vis is 0, so only the counts are cleared
             grads, vis = self._grads, self._vis
             vis.zero_()
@@ -177,10 +143,8 @@ class ViewParallelTrainer(SplatTrainer):
             else:
                 self.flat.zero_()
             grads, vis = layout.views(self.flat)
-        refine = None
-        if not owner:
-            refine = self._buf("refine_dense", (n,), torch.float32)
-            refine.zero_()
+        refine = self._buf("refine_dense", (n,), torch.float32)
+        refine.zero_()
         losses = []
         num_visible = num_isect = 0
         if self.frame is None:
@@ -207,11 +171,10 @@ class ViewParallelTrainer(SplatTrainer):
             cam = b.camera
             cfg = ops.render_cfg(splats.sh_degree, mip=c.render_mode_mip, background=self.background(),
                                  has_min_scale=splats.min_scale is not None)
-            slot = self._slots[len(losses)] if owner else None
             out = ops.render(cam, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities,
                              min_scale=splats.min_scale, frame=self.frame,
                              out_img=self._buf("img", (cam.height, cam.width, 4), torch.float32),
-                             visible=slot["visible"] if owner else self._buf("visible", (n,), torch.float32))
+                             visible=self._buf("visible", (n,), torch.float32))
             mark("render")
             if ev is not None:
                 torch.cuda.current_stream(self.device).wait_event(ev)
@@ -219,15 +182,11 @@ class ViewParallelTrainer(SplatTrainer):
             losses.append(loss.loss.clone())
             mark("loss")
             vc = ops.rasterize_bwd(out.frame, out.out_img, loss.dl_dpred,
-                                   slot["vc"] if owner else self._buf("v_combined", (max(n, 1), 10), torch.float32))
+                                   self._buf("v_combined", (max(n, 1), 10), torch.float32))
             mark("raster_bwd")
-            if owner:  # what the shard owners read: the view's projection map and uniforms
-                out.frame.copy_field("compact_from_global", slot["cmap"])
-                ops.frame_uniforms(out.frame, slot["uni"])
-            else:
-                ops.vjp_dense(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, grads,
-                              refine, min_scale=splats.min_scale, visible=out.visible, vis_accum=vis)
-                mark("vjp_dense")
+            ops.vjp_dense(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, grads,
+                          refine, min_scale=splats.min_scale, visible=out.visible, vis_accum=vis)
+            mark("vjp_dense")
             num_visible += out.num_visible
             num_isect += out.num_intersections
         if peer is None:
@@ -241,22 +200,7 @@ class ViewParallelTrainer(SplatTrainer):
                         opac_reg=opac_reg, eps=c.adam_epsilon,
                         noise_scale=c.mean_noise_weight * self.lr_unit() * self.median_scale,
                         noise_limit=self.median_scale, noise_seed=int(self.rng.integers(0, 2 ** 32)))
-        if owner:
-            for r in range(peer.world):
-                self.view_set.used[r] = len(batches)
-            peer.barrier()  # every rank's views of this step are complete
-            mark("barrier_rows")
-            b0, b1 = self.shard
-            ops.vjp_owner(splats.sh_degree, n, b0, b1, self.view_set, splats.transforms, splats.sh_coeffs,
-                          splats.raw_opacities, self._rows, self._row_vis, min_scale=splats.min_scale,
-                          device=self.device)
-            mark("vjp_owner")
-            ops.adam_q8_shard(splats.sh_degree, n, b0, b1, self._rows, self._row_vis, self.peer_set, o["t"], o["sh"],
-                              o["o"], q8, device=self.device)
-            mark("optimizer")
-            peer.barrier()  # every replica holds the new parameters
-            mark("barrier_params")
-        elif peer is not None:
+        if peer is not None:
             peer.barrier()  # every rank's rows and counts are complete
             mark("barrier_rows")
             ops.adam_q8_peer(splats.sh_degree, n, self.shard[0], self.shard[1], self.peer_set, o["t"], o["sh"],
