@@ -172,14 +172,18 @@ def make_workload(n_splats: int, config: int = 2):
     return sp, tgt, cams
 
 
-# DRAM bytes (read + write) per launch of each stage's kernel, from one ncu
-# capture of this workload (configs[2] at 3M splats; the optimizer's second
-# term is vjp_rows_kernel from the same capture).  Below the algorithmic bytes
-# for the raster kernels: L2 (126 MB) serves a projected row to the
-# neighbouring tiles that gather it.  Only the dominant stage's figure goes
-# into the bench line.
-MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 273.6e6, "raster_fwd": 142.5e6, "project": 700.7e6, "loss": 60.8e6,
-                           "optimizer": 2.352e9 + 474.1e6}
+# DRAM bytes (read + write) per launch of each stage's kernel at configs[2]
+# (3M splats, ~1.74M visible, ~5.77M intersections, 1600x1060), from
+# single-kernel ncu captures of smaller cases scaled by the units each kernel
+# processes: raster kernels from configs[1] (3.60M intersections) scaled by
+# intersections, projection and the Q8 optimizer from a 1M-splat configs[2]
+# scene scaled by splats, the VJP rows by visible splats, the loss (same image
+# size) as captured.  Below the algorithmic bytes for the raster kernels: L2
+# (126 MB) serves a projected row to the neighbouring tiles that gather it.
+# Only the dominant stage's figure goes into the bench line.
+MEASURED_TRAFFIC_CONFIG2 = {"raster_bwd": 140.68e6 * 5.766 / 3.597, "raster_fwd": 53.41e6 * 5.766 / 3.597,
+                            "project": 224.93e6 * 3.0, "loss": 60.38e6,
+                            "optimizer": 744.49e6 * 3.0 + 245.23e6 * 1.744 / 0.5858}
 
 
 def stage_bytes(name: str, n: int, v: int, i: int, p: int, t: int) -> float:
