@@ -67,7 +67,7 @@ def test_sort_above_67m_keys_kat(cuda):
     assert np.array_equal(v, expected)
 
 
-@pytest.mark.parametrize("bits", [1, 5, 8, 13, 16, 24])
+@pytest.mark.parametrize("bits", [1, 5, 8, 9, 13, 16, 17, 18, 24, 26, 27, 28])
 def test_sort_partial_bit_ranges(cuda, bits):
     rng = np.random.default_rng(bits)
     keys = rng.integers(0, 2 ** bits, size=200_001, dtype=np.uint32)

@@ -240,6 +240,8 @@ VS_API vs_status vs_render_project(vs_ctx* ctx, vs_frame* f, const vs_camera* ca
   uint64_t isect;
   memcpy(&isect, (const char*)ctx->h_pinned + 32, 8);
   f->I = isect;
+  f->depth_lo = ~ctx->h_pinned[2];
+  f->depth_hi = ctx->h_pinned[3];
   if (f->v > num_splats) return vs_fail(ctx, VS_ERR_CUDA, "render_forward: visible count %u > %u splats", f->v, num_splats);
   if (f->I >= 0xffffffffull)
     return vs_fail(ctx, VS_ERR_CAPACITY, "render_forward: %llu intersections exceed 32-bit indexing",

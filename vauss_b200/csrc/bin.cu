@@ -6,8 +6,9 @@
 // scan_in_place (kernels/map_gaussians.rs:195-269), map_gaussians_to_intersect
 // (:21-174), the tile sort and get_tile_offsets (src/get_tile_offset.rs:11-52).
 // The resulting order is (tile, depth, compact id) -- a stable sort on the
-// 64-bit key tile << 32 | f32_bits(depth) -- done as a 32-bit depth sort over
-// the V visible splats followed by a stable sort over the tile bits only.
+// 64-bit key tile << 32 | f32_bits(depth) -- done as a depth sort over the V
+// visible splats (over the bits in which their depths differ) followed by a
+// stable sort over the tile bits only.
 #include "vs_internal.cuh"
 
 namespace {
@@ -16,11 +17,13 @@ using namespace vs;
 
 constexpr uint32_t BIN_BLOCK = 256;
 
-__global__ void depth_keys_kernel(const float* __restrict__ depths, uint32_t v, uint32_t* __restrict__ keys,
+// Keys are the depth bits less the smallest visible depth's bits (depth >=
+// 0.01, so the bits order like the depths): the same order in fewer key bits.
+__global__ void depth_keys_kernel(const float* __restrict__ depths, uint32_t v, uint32_t lo, uint32_t* __restrict__ keys,
                                   uint32_t* __restrict__ ids) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < v) {
-    keys[i] = __float_as_uint(depths[i]);  // depth >= 0.01, so the bits are monotone
+    keys[i] = __float_as_uint(depths[i]) - lo;
     ids[i] = i;
   }
 }
@@ -33,13 +36,14 @@ __global__ void depth_keys_kernel(const float* __restrict__ depths, uint32_t v, 
 // instruction covers 32 consecutive entries.  Large boxes are walked by the
 // whole warp afterwards (map_gaussians.rs:117-173).  Emission stops at the
 // splat's counted budget and pads any shortfall with the sentinel tile id T
-// (map_gaussians.rs:76-113).
+// (map_gaussians.rs:76-113); no store goes past the projection's intersection
+// total `total`, whatever the offsets hold.
 __global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v, const uint32_t* __restrict__ order,
                                                          const uint32_t* __restrict__ cum,
                                                          const uint2* __restrict__ tile_masks,
                                                          const float4* __restrict__ projected,
                                                          uint32_t* __restrict__ tile_keys,
-                                                         uint32_t* __restrict__ compact_vals) {
+                                                         uint32_t* __restrict__ compact_vals, uint32_t total) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
   const uint32_t lane = threadIdx.x & 31u;
   const bool active = i < v;
@@ -89,7 +93,7 @@ __global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v,
       const uint32_t oi0 = __shfl_sync(0xffffffffu, info0, owner);
       const uint32_t oi1 = __shfl_sync(0xffffffffu, info1, owner);
       const uint32_t oc = __shfl_sync(0xffffffffu, c, owner);
-      if (p < s1 && !(oi0 & 0x80000000u)) {
+      if (p < s1 && p < total && !(oi0 & 0x80000000u)) {
         const uint32_t k = p - ostart, m = oi0 & 0xffffu;
         uint32_t key = T;
         if (k < (uint32_t)__popc(m)) {
@@ -123,13 +127,13 @@ __global__ void __launch_bounds__(BIN_BLOCK) emit_kernel(Uniforms u, uint32_t v,
       const bool hit = t < ln && tile_hit(tx, ty, lx, ly, lc, lpt);
       const uint32_t mask = __ballot_sync(0xffffffffu, hit);
       const uint32_t slot = emitted + __popc(mask & ((1u << lane) - 1u));
-      if (hit && slot < lbudget) {
+      if (hit && slot < lbudget && lstart + slot < total) {
         tile_keys[lstart + slot] = tx + ty * u.tbw;
         compact_vals[lstart + slot] = lc_id;
       }
       emitted += __popc(mask);
     }
-    for (uint32_t p = min(emitted, lbudget) + lane; p < lbudget; p += 32) {
+    for (uint32_t p = min(emitted, lbudget) + lane; p < lbudget && lstart + p < total; p += 32) {
       tile_keys[lstart + p] = T;
       compact_vals[lstart + p] = lc_id;
     }
@@ -187,15 +191,22 @@ vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
   uint32_t* v0 = (uint32_t*)ctx->sort_vals.ptr;
   uint32_t* v1 = v0 + scratch / 4;
   const uint32_t blocks_v = div_up(v, BIN_BLOCK);
-  // the ids are sorted in the frame's depth_order (an even number of passes
-  // leaves the result there; otherwise it is copied back)
+  if (f->depth_hi < f->depth_lo)
+    return vs_fail(ctx, VS_ERR_CUDA, "render_bin: depth range [%08x, %08x] of %u visible splats", f->depth_lo,
+                   f->depth_hi, v);
+  const uint32_t span = f->depth_hi - f->depth_lo;
+  const uint32_t depth_bits = span ? 32u - (uint32_t)__builtin_clz(span) : 0u;
+  // the ids are sorted into the frame's depth_order: the keys start in the
+  // buffer pair from which the sort's last pass writes there
   uint32_t* order = (uint32_t*)f->depth_order.ptr;
-  depth_keys_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const float*)f->depths.ptr, v, k0, order); ++ctx->launches;
+  const bool odd = radix_sort_passes(depth_bits) & 1u;
+  uint32_t* kin = odd ? k1 : k0;
+  uint32_t* vin = odd ? v1 : order;
+  depth_keys_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const float*)f->depths.ptr, v, f->depth_lo, kin, vin); ++ctx->launches;
   bool alt = false;
-  VS_TRY(radix_sort_pairs(ctx, k0, order, k1, v1, v, 32, &alt));
-  if (alt) VS_CUDA(ctx, cudaMemcpyAsync(order, v1, (size_t)v * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  VS_TRY(radix_sort_pairs(ctx, kin, vin, odd ? k0 : k1, odd ? order : v1, v, depth_bits, &alt));
   // tile counts in depth order, inclusive scan -> emission offsets
-  uint32_t* cum = alt ? k0 : k1;  // free half of the key scratch
+  uint32_t* cum = k1;  // the sorted keys are in k0
   VS_TRY(scan_gather_inclusive_u32(ctx, cum, (const uint32_t*)f->tile_counts.ptr, order, v));
   VS_TRY(vs_ensure(ctx, f->isect_tile, (size_t)(I + 1) * 4));
   VS_TRY(vs_ensure(ctx, f->isect_compact, (size_t)(I + 1) * 4));
@@ -205,7 +216,7 @@ vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
   uint32_t* tvals = (uint32_t*)f->isect_compact.ptr;
   emit_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>(f->u, v, (const uint32_t*)f->depth_order.ptr, cum,
                                                         (const uint2*)f->tile_masks.ptr, (const float4*)f->projected.ptr,
-                                                        tkeys, tvals); ++ctx->launches;
+                                                        tkeys, tvals, (uint32_t)I); ++ctx->launches;
   VS_CUDA(ctx, cudaGetLastError());
   const uint32_t tile_bits = 32u - (uint32_t)__builtin_clz(T | 1u);
   uint32_t* sk = (uint32_t*)ctx->sort_keys.ptr;

@@ -172,17 +172,21 @@ __global__ void __launch_bounds__(PROJ_BLOCK, 4) project_kernel(
     float* __restrict__ opacities, float* __restrict__ max_radius, uint32_t* __restrict__ global_from_compact,
     float* __restrict__ depths, uint32_t* __restrict__ tile_counts, uint2* __restrict__ tile_masks,
     float4* __restrict__ projected,
-    unsigned long long* lookback, uint32_t* counters /* [0] ticket, [1] visible total */,
+    unsigned long long* lookback,
+    uint32_t* counters /* [0] ticket, [1] visible total, [2] ~min and [3] max of the visible depth bits */,
     unsigned long long* isect_total, uint32_t* err) {
   __shared__ uint32_t s_bid;
   __shared__ uint32_t s_warp_cnt[PROJ_BLOCK / 32];
   __shared__ uint32_t s_block_off;
   __shared__ uint32_t s_total;
   __shared__ unsigned long long s_isect;
+  __shared__ uint32_t s_dlo_inv, s_dhi;  // ~min and max of the block's visible depth bits
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   if (tid == 0) {
     s_bid = atomicAdd(&counters[0], 1u);  // in-order block ids: look-back only waits on started blocks
     s_isect = 0ull;
+    s_dlo_inv = 0u;
+    s_dhi = 0u;
   }
   __syncthreads();
   const uint32_t bid = s_bid;
@@ -253,10 +257,23 @@ __global__ void __launch_bounds__(PROJ_BLOCK, 4) project_kernel(
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) hsum += __shfl_xor_sync(0xffffffffu, hsum, off);
   if (lane == 0 && hsum) atomicAdd(&s_isect, hsum);
+  // the depth range of the visible splats sets how many key bits the depth
+  // sort needs (depths are positive, so their bits order like the values)
+  const uint32_t dbits = visible ? __float_as_uint(o.depth) : 0u;
+  const uint32_t whi = __reduce_max_sync(0xffffffffu, dbits);
+  const uint32_t wlo_inv = __reduce_max_sync(0xffffffffu, visible ? ~dbits : 0u);
+  if (lane == 0 && ballot) {
+    atomicMax(&s_dhi, whi);
+    atomicMax(&s_dlo_inv, wlo_inv);
+  }
   __syncthreads();
   if (warp == 0) {
     const uint32_t total = s_total;
     if (lane == 0 && s_isect) atomicAdd(isect_total, s_isect);
+    if (lane == 0 && total) {
+      atomicMax(&counters[3], s_dhi);
+      atomicMax(&counters[2], s_dlo_inv);
+    }
     // Decoupled look-back, a warp at a time: lane l reads the status of block
     // hi - l; the nearest published inclusive prefix ends the walk.  Positions
     // before block 0 read as an inclusive prefix of 0.

@@ -6,13 +6,15 @@
 // count / reduce / scan / scan_add / scatter per pass) and prefix sums
 // (crates/splat-train-scan/src/kernels.rs:30-212).
 //
-// Per 8-bit pass: (1) each block histograms its 2048-key tile into a
-// digit-major table hist[digit][tile]; (2) an exclusive scan of that table
-// gives every (digit, tile) its global output offset; (3) each block ranks its
-// keys stably (every warp ranks a contiguous 256-key slice, equal digits found
-// by one ballot per digit bit,
-// warps are combined through per-digit counts), scatters them into shared
-// memory in digit order and writes contiguous per-digit runs to global memory.
+// Per pass of an 8- or 9-bit digit: (1) each block histograms its 2048-key
+// tile into a digit-major table hist[digit][tile]; (2) an exclusive scan of
+// that table gives every (digit, tile) its global output offset; (3) each
+// block ranks its keys stably (every warp ranks a contiguous 256-key slice,
+// equal digits found by one ballot per digit bit, warps are combined through
+// per-digit counts), scatters them into shared memory in digit order and
+// writes contiguous per-digit runs to global memory.  A sort of b key bits
+// takes ceil(b / 9) passes, the bits split as evenly as possible over them; a
+// stable LSD sort gives the same order whatever the digit widths.
 #include <cuda/atomic>
 #include <mutex>
 
@@ -26,14 +28,17 @@ constexpr uint32_t SORT_THREADS = 256;
 constexpr uint32_t SORT_WARPS = SORT_THREADS / 32;
 constexpr uint32_t ITEMS = 8;  // per thread
 constexpr uint32_t SORT_TILE = SORT_THREADS * ITEMS;  // 2048
-constexpr uint32_t RADIX = 256;
+constexpr uint32_t RADIX = 256;       // 8-bit digits: the table size of the fixed-scratch sort
+constexpr uint32_t MAX_DIGIT_BITS = 9;
 
+template <uint32_t RB>
 __global__ void __launch_bounds__(SORT_THREADS) hist_kernel(const uint32_t* __restrict__ keys, uint32_t count,
                                                             uint32_t shift, uint32_t mask, uint32_t tiles,
                                                             uint32_t* __restrict__ hist) {
-  __shared__ uint32_t s_hist[RADIX];
+  constexpr uint32_t R = 1u << RB;
+  __shared__ uint32_t s_hist[R];
   const uint32_t tid = threadIdx.x;
-  s_hist[tid] = 0;
+  for (uint32_t d = tid; d < R; d += SORT_THREADS) s_hist[d] = 0;
   __syncthreads();
   const uint32_t base = blockIdx.x * SORT_TILE;
 #pragma unroll
@@ -45,22 +50,27 @@ __global__ void __launch_bounds__(SORT_THREADS) hist_kernel(const uint32_t* __re
     if (valid) atomicAdd(&s_hist[(keys[i] >> shift) & mask], 1u);
   }
   __syncthreads();
-  hist[tid * tiles + blockIdx.x] = s_hist[tid];
+  for (uint32_t d = tid; d < R; d += SORT_THREADS) hist[d * tiles + blockIdx.x] = s_hist[d];
 }
 
+template <uint32_t RB>
 __global__ void __launch_bounds__(SORT_THREADS) scatter_kernel(
     const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in, uint32_t* __restrict__ keys_out,
     uint32_t* __restrict__ vals_out, uint32_t count, uint32_t shift, uint32_t mask, uint32_t tiles,
     const uint32_t* __restrict__ offsets /* exclusive-scanned hist, digit-major */) {
-  __shared__ uint32_t s_wcnt[SORT_WARPS][RADIX];  // per-warp digit counts, then per-warp offsets
-  __shared__ uint32_t s_dstart[RADIX];            // block-local start of each digit
-  __shared__ uint32_t s_goff[RADIX];              // global start of each digit for this tile
+  constexpr uint32_t R = 1u << RB;
+  constexpr uint32_t DPT = R / SORT_THREADS;  // digits per thread, consecutive
+  static_assert(DPT >= 1 && DPT * SORT_THREADS == R, "digit ownership");
+  __shared__ uint32_t s_wcnt[SORT_WARPS][R];  // per-warp digit counts, then per-warp offsets
+  __shared__ uint32_t s_dstart[R];            // block-local start of each digit
+  __shared__ uint32_t s_goff[R];              // global start of each digit for this tile
   __shared__ uint32_t s_keys[SORT_TILE];
   __shared__ uint32_t s_vals[SORT_TILE];
   __shared__ uint32_t s_scan[SORT_WARPS];
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
-  for (uint32_t i = tid; i < SORT_WARPS * RADIX; i += SORT_THREADS) (&s_wcnt[0][0])[i] = 0;
-  s_goff[tid] = offsets[tid * tiles + blockIdx.x];
+  for (uint32_t i = tid; i < SORT_WARPS * R; i += SORT_THREADS) (&s_wcnt[0][0])[i] = 0;
+#pragma unroll
+  for (uint32_t j = 0; j < DPT; ++j) s_goff[tid * DPT + j] = offsets[(tid * DPT + j) * tiles + blockIdx.x];
   __syncthreads();
 
   // Warp `warp` owns keys [base + warp*256, base + warp*256 + 256), 32 per round.
@@ -72,22 +82,22 @@ __global__ void __launch_bounds__(SORT_THREADS) scatter_kernel(
     const bool valid = i < count;
     k[r] = valid ? keys_in[i] : 0u;
     v[r] = valid ? vals_in[i] : 0u;
-    d[r] = valid ? ((k[r] >> shift) & mask) : RADIX;
+    d[r] = valid ? ((k[r] >> shift) & mask) : R;
   }
 #pragma unroll
   for (uint32_t r = 0; r < ITEMS; ++r) {
-    // lanes holding the same digit (9 bits: an invalid lane holds 256), by
+    // lanes holding the same digit (RB + 1 bits: an invalid lane holds R), by
     // one ballot per bit -- cheaper on sm_100 than match_any
     uint32_t peers = 0xffffffffu;
 #pragma unroll
-    for (uint32_t b = 0; b < 9; ++b) {
+    for (uint32_t b = 0; b <= RB; ++b) {
       const uint32_t bit = (d[r] >> b) & 1u;
       const uint32_t bal = __ballot_sync(0xffffffffu, bit);
       peers &= bit ? bal : ~bal;
     }
     const uint32_t leader = __ffs(peers) - 1;
     uint32_t before = 0;
-    if (lane == leader && d[r] < RADIX) {
+    if (lane == leader && d[r] < R) {
       before = s_wcnt[warp][d[r]];
       s_wcnt[warp][d[r]] = before + __popc(peers);
     }
@@ -96,13 +106,22 @@ __global__ void __launch_bounds__(SORT_THREADS) scatter_kernel(
     __syncwarp();
   }
   __syncthreads();
-  // thread `tid` owns digit `tid`: exclusive prefix over warps, block total
+  // thread `tid` owns digits tid*DPT .. tid*DPT + DPT-1: exclusive prefix over
+  // warps, block totals
+  uint32_t dtot[DPT];
   uint32_t run = 0;
 #pragma unroll
-  for (uint32_t w = 0; w < SORT_WARPS; ++w) {
-    const uint32_t c = s_wcnt[w][tid];
-    s_wcnt[w][tid] = run;
-    run += c;
+  for (uint32_t j = 0; j < DPT; ++j) {
+    const uint32_t dg = tid * DPT + j;
+    uint32_t acc = 0;
+#pragma unroll
+    for (uint32_t w = 0; w < SORT_WARPS; ++w) {
+      const uint32_t c = s_wcnt[w][dg];
+      s_wcnt[w][dg] = acc;
+      acc += c;
+    }
+    dtot[j] = acc;
+    run += acc;
   }
   // exclusive scan of the digit totals across the block (digit-ordered)
   uint32_t incl = run;
@@ -123,11 +142,16 @@ __global__ void __launch_bounds__(SORT_THREADS) scatter_kernel(
     if (lane < SORT_WARPS) s_scan[lane] = s;
   }
   __syncthreads();
-  s_dstart[tid] = incl - run + (warp ? s_scan[warp - 1] : 0u);
+  uint32_t start = incl - run + (warp ? s_scan[warp - 1] : 0u);
+#pragma unroll
+  for (uint32_t j = 0; j < DPT; ++j) {
+    s_dstart[tid * DPT + j] = start;
+    start += dtot[j];
+  }
   __syncthreads();
 #pragma unroll
   for (uint32_t r = 0; r < ITEMS; ++r) {
-    if (d[r] < RADIX) {
+    if (d[r] < R) {
       const uint32_t pos = s_dstart[d[r]] + s_wcnt[warp][d[r]] + rank[r];
       s_keys[pos] = k[r];
       s_vals[pos] = v[r];
@@ -379,26 +403,40 @@ vs_status scan_gather_inclusive_u32(vs_ctx* ctx, uint32_t* out, const uint32_t* 
   return scan_impl(ctx, out, count, nullptr, true, src, idx);
 }
 
+uint32_t radix_sort_passes(uint32_t key_bits) { return div_up(key_bits, MAX_DIGIT_BITS); }
+
 vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
                            uint32_t count, uint32_t key_bits, bool* result_in_alt) {
   *result_in_alt = false;
   if (count <= 1 || key_bits == 0) return VS_OK;
   const uint32_t tiles = div_up(count, SORT_TILE);
-  const size_t hist_n = (size_t)RADIX * tiles;
+  const uint32_t passes = radix_sort_passes(key_bits);
+  const uint32_t wide = key_bits / passes + (key_bits % passes ? 1u : 0u);  // widest digit
+  const size_t hist_n = ((size_t)1 << wide) * tiles;
   if (hist_n > 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "radix sort: %u keys exceed the histogram", count);
   VS_TRY(vs_ensure(ctx, ctx->sort_hist, hist_n * sizeof(uint32_t)));
   uint32_t* hist = (uint32_t*)ctx->sort_hist.ptr;
   uint32_t *kin = keys, *vin = vals, *kout = keys_alt, *vout = vals_alt;
-  for (uint32_t shift = 0; shift < key_bits; shift += 8) {
-    const uint32_t bits = min(8u, key_bits - shift);
+  uint32_t shift = 0;
+  for (uint32_t p = 0; p < passes; ++p) {
+    // the first key_bits % passes passes take one bit more than the rest
+    const uint32_t bits = key_bits / passes + (p < key_bits % passes ? 1u : 0u);
     const uint32_t mask = (1u << bits) - 1u;
-    hist_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
-    VS_TRY(scan_impl(ctx, hist, (uint32_t)hist_n, nullptr, false));
-    scatter_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist); ++ctx->launches;
+    if (bits > 8) {
+      hist_kernel<9><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
+      VS_TRY(scan_impl(ctx, hist, 512u * tiles, nullptr, false));
+      scatter_kernel<9><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist);
+    } else {
+      hist_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
+      VS_TRY(scan_impl(ctx, hist, 256u * tiles, nullptr, false));
+      scatter_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist);
+    }
+    ++ctx->launches;
     VS_CUDA(ctx, cudaGetLastError());
     uint32_t* t = kin; kin = kout; kout = t;
     t = vin; vin = vout; vout = t;
     *result_in_alt = !*result_in_alt;
+    shift += bits;
   }
   return VS_OK;
 }
@@ -494,9 +532,9 @@ extern "C" VS_API vs_status vs_radix_sort_pairs_static(vs_ctx* ctx, uint32_t* ke
   for (uint32_t shift = 0; shift < key_bits; shift += 8) {
     const uint32_t bits = min(8u, key_bits - shift);
     const uint32_t mask = (1u << bits) - 1u;
-    hist_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
+    hist_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
     scan_exclusive_into(ctx, hist, hist_n, sums);
-    scatter_kernel<<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist); ++ctx->launches;
+    scatter_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist); ++ctx->launches;
     VS_TRY(vs_cuda(ctx, cudaGetLastError(), "radix_sort_static launch"));
     uint32_t* t = kin; kin = kout; kout = t;
     t = vin; vin = vout; vout = t;

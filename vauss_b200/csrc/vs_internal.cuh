@@ -35,6 +35,7 @@ struct vs_frame {
   vs_render_cfg cfg{};
   uint32_t n = 0, v = 0, T = 0;
   uint64_t I = 0;
+  uint32_t depth_lo = 0, depth_hi = 0;  // bit range of the visible splats' depths (projection readback)
   bool projected_ok = false, binned = false, rendered = false;
   DevBuf compact_from_global, global_from_compact, depths, tile_counts, tile_masks, projected, depth_order;
   DevBuf isect_tile, isect_compact, tile_ranges, tile_used_end, opacities, max_radius;
@@ -63,6 +64,10 @@ vs::Uniforms vs_make_uniforms(const vs_camera& c, const vs_render_cfg& cfg);
 // ---- launchers (defined next to their kernels) ----
 vs_status launch_project(vs_ctx* ctx, vs_frame* f, const float* transforms, const void* sh, const float* raw_opac,
                          const float* min_scale);
+// Stable LSD sort over the low key_bits bits in radix_sort_passes(key_bits)
+// passes of at most 9 bits; the result is in keys_alt/vals_alt after an odd
+// number of passes (*result_in_alt), else in keys/vals.
+uint32_t radix_sort_passes(uint32_t key_bits);
 vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
                            uint32_t count, uint32_t key_bits, bool* result_in_alt);
 vs_status scan_inclusive_u32(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev);
