@@ -50,7 +50,8 @@ __global__ void __launch_bounds__(SORT_THREADS) hist_kernel(const uint32_t* __re
     if (valid) atomicAdd(&s_hist[(keys[i] >> shift) & mask], 1u);
   }
   __syncthreads();
-  for (uint32_t d = tid; d < R; d += SORT_THREADS) hist[d * tiles + blockIdx.x] = s_hist[d];
+  // the table holds the pass's mask + 1 digits only
+  for (uint32_t d = tid; d <= mask; d += SORT_THREADS) hist[d * tiles + blockIdx.x] = s_hist[d];
 }
 
 template <uint32_t RB>
@@ -70,7 +71,10 @@ __global__ void __launch_bounds__(SORT_THREADS) scatter_kernel(
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   for (uint32_t i = tid; i < SORT_WARPS * R; i += SORT_THREADS) (&s_wcnt[0][0])[i] = 0;
 #pragma unroll
-  for (uint32_t j = 0; j < DPT; ++j) s_goff[tid * DPT + j] = offsets[(tid * DPT + j) * tiles + blockIdx.x];
+  for (uint32_t j = 0; j < DPT; ++j) {
+    const uint32_t dg = tid * DPT + j;
+    if (dg <= mask) s_goff[dg] = offsets[dg * tiles + blockIdx.x];  // no key holds a larger digit
+  }
   __syncthreads();
 
   // Warp `warp` owns keys [base + warp*256, base + warp*256 + 256), 32 per round.
@@ -422,13 +426,14 @@ vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t
     // the first key_bits % passes passes take one bit more than the rest
     const uint32_t bits = key_bits / passes + (p < key_bits % passes ? 1u : 0u);
     const uint32_t mask = (1u << bits) - 1u;
+    // the table is (mask + 1) x tiles words, within the hist_n allocated above
     if (bits > 8) {
       hist_kernel<9><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
-      VS_TRY(scan_impl(ctx, hist, 512u * tiles, nullptr, false));
+      VS_TRY(scan_impl(ctx, hist, (mask + 1u) * tiles, nullptr, false));
       scatter_kernel<9><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist);
     } else {
       hist_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
-      VS_TRY(scan_impl(ctx, hist, 256u * tiles, nullptr, false));
+      VS_TRY(scan_impl(ctx, hist, (mask + 1u) * tiles, nullptr, false));
       scatter_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist);
     }
     ++ctx->launches;
@@ -522,7 +527,6 @@ extern "C" VS_API vs_status vs_radix_sort_pairs_static(vs_ctx* ctx, uint32_t* ke
   VS_TRY(static_scratch(ctx, &scratch));
   if (count <= 1 || key_bits == 0) return VS_OK;
   const uint32_t tiles = div_up(count, SORT_TILE);
-  const uint32_t hist_n = RADIX * tiles;
   uint32_t* keys_alt = scratch;
   uint32_t* vals_alt = scratch + STATIC_MAX_KEYS;
   uint32_t* hist = scratch + 2 * STATIC_MAX_KEYS;
@@ -533,7 +537,7 @@ extern "C" VS_API vs_status vs_radix_sort_pairs_static(vs_ctx* ctx, uint32_t* ke
     const uint32_t bits = min(8u, key_bits - shift);
     const uint32_t mask = (1u << bits) - 1u;
     hist_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
-    scan_exclusive_into(ctx, hist, hist_n, sums);
+    scan_exclusive_into(ctx, hist, (mask + 1u) * tiles, sums);
     scatter_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist); ++ctx->launches;
     VS_TRY(vs_cuda(ctx, cudaGetLastError(), "radix_sort_static launch"));
     uint32_t* t = kin; kin = kout; kout = t;
