@@ -436,7 +436,8 @@ def e2e_run(leg, steps, warmup):
             "h2d_bytes_per_step": int(round(h2d_total / max(steps, 1))), "d2h_bytes_per_step": 4,
             "feed": "SceneLoader (vs_feed): RGB8 views, pinned ring of 4, packed on the GPU, no cache",
             "api": ("ViewParallelTrainer.step_views (vs_render_forward, vs_loss, vs_rasterize_backward, "
-                    "vs_vjp_dense, vs_peer_barrier, vs_adam_q8_peer)" if leg.world > 1 or leg.multiview else
+                    "vs_vjp_compact with one view per rank or vs_vjp_dense, vs_peer_barrier, vs_adam_q8_peer)"
+                    if leg.world > 1 or leg.multiview else
                     "SplatTrainer.step (vs_render_forward, vs_loss, vs_rasterize_backward, vs_step_q8)")}
 
 

@@ -243,7 +243,13 @@ __device__ __forceinline__ uint32_t compact_block(bool flag, uint32_t* list, uin
 // projection culled have no rasterizer row and no `visible` mark, so their
 // gradient rows, refine sums and view counts stay as they are.  The rows with
 // a non-zero rasterizer gradient are compacted per block first, so the VJP
-// runs on whole warps.
+// runs on whole warps.  kCompact writes VS_COMPACT_ROW floats per splat
+// (transforms gradient, raw-opacity gradient, colour gradient): the view's SH
+// gradient is that colour gradient times the SH basis of the view direction,
+// which the shard owner rebuilds from the camera position (cam_out); every row
+// must be fresh (one view per step), as the owner's sum takes one term per
+// rank.
+template <bool kCompact>
 __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, const float* __restrict__ transforms,
                                                         const void* __restrict__ sh, const float* __restrict__ raw_opac,
                                                         const float* __restrict__ min_scale,
@@ -251,13 +257,20 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
                                                         const float* __restrict__ v_combined,
                                                         float* __restrict__ grads, float* __restrict__ refine,
                                                         const float* __restrict__ visible,
-                                                        float* __restrict__ vis_accum) {
+                                                        float* __restrict__ vis_accum, float* __restrict__ cam_out,
+                                                        uint32_t* __restrict__ err) {
   __shared__ uint32_t s_list[256];
   __shared__ uint32_t s_wcnt[8];
   __shared__ uint8_t s_fresh[256];
   const uint32_t c = blockIdx.x * blockDim.x + threadIdx.x;
   const int nc = (u.sh_degree + 1) * (u.sh_degree + 1);
-  const int width = 10 + 3 * nc + 1;
+  const int width = kCompact ? VS_COMPACT_ROW : 10 + 3 * nc + 1;
+  if (kCompact && c == 0) {
+    cam_out[0] = u.cam[0];
+    cam_out[1] = u.cam[1];
+    cam_out[2] = u.cam[2];
+    cam_out[3] = 0.0f;
+  }
   bool any = false;
   if (c < v) {
     const uint32_t g = global_from_compact[c];
@@ -268,6 +281,7 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
       const float seen = vis_accum[g];
       vis_accum[g] = seen + visible[g];
       fresh = seen == 0.0f && visible[g] > 0.0f;
+      if (kCompact && seen != 0.0f && visible[g] > 0.0f) atomicOr(err, VS_DERR_STATE);
     }
     const float* rg = v_combined + (size_t)c * 10;
 #pragma unroll
@@ -293,16 +307,26 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
   float* d = grads + (size_t)g * width;
   const float gv[10] = {o.v_mean.x, o.v_mean.y, o.v_mean.z, o.v_q.w, o.v_q.x, o.v_q.y, o.v_q.z,
                         o.v_scale.x, o.v_scale.y, o.v_scale.z};
-  // 0 + x (not x) on a fresh row keeps the sign of zero of an accumulation
+  if (kCompact) {
+    // the terms a fresh dense row would hold: 0 + x for the accumulated
+    // parts, the raw colour gradient for the SH part
+    float4* d4 = reinterpret_cast<float4*>(d);
+    d4[0] = make_float4(0.0f + gv[0], 0.0f + gv[1], 0.0f + gv[2], 0.0f + gv[3]);
+    d4[1] = make_float4(0.0f + gv[4], 0.0f + gv[5], 0.0f + gv[6], 0.0f + gv[7]);
+    d4[2] = make_float4(0.0f + gv[8], 0.0f + gv[9], 0.0f + o.v_raw, rr[5]);
+    d4[3] = make_float4(rr[6], rr[7], 0.0f, 0.0f);
+  } else {
+    // 0 + x (not x) on a fresh row keeps the sign of zero of an accumulation
 #pragma unroll
-  for (int k = 0; k < 10; ++k) d[k] = (fresh ? 0.0f : d[k]) + gv[k];
-  float b[16];
-  sh_basis_all(o.dir.x, o.dir.y, o.dir.z, b);
-  for (int k = 0; k < nc; ++k) {
+    for (int k = 0; k < 10; ++k) d[k] = (fresh ? 0.0f : d[k]) + gv[k];
+    float b[16];
+    sh_basis_all(o.dir.x, o.dir.y, o.dir.z, b);
+    for (int k = 0; k < nc; ++k) {
 #pragma unroll
-    for (int q = 0; q < 3; ++q) d[10 + k * 3 + q] = (fresh ? 0.0f : d[10 + k * 3 + q]) + rr[5 + q] * b[k];
+      for (int q = 0; q < 3; ++q) d[10 + k * 3 + q] = (fresh ? 0.0f : d[10 + k * 3 + q]) + rr[5 + q] * b[k];
+    }
+    d[width - 1] = (fresh ? 0.0f : d[width - 1]) + o.v_raw;
   }
-  d[width - 1] = (fresh ? 0.0f : d[width - 1]) + o.v_raw;
   refine[g] += clampf(vs_is_finite(rr[9]) ? rr[9] : 0.0f, 0.0f, 1.0e32f);
 }
 
@@ -389,6 +413,11 @@ struct PeerArgs {
   const uint32_t* err;
   uint32_t cta_begin;  // first CTA (256 splats) of the shard
   uint32_t m_off;      // first splat covered by the moment arrays
+  // gradient row sources: `rows` arrays grads[r] / vis[r] indexed by splat -
+  // row_base (the ranks' dense rows, rows = world and row_base = 0; or one
+  // shard-local array of rows gathered from compact rows)
+  uint32_t rows, row_base;
+  const float* cams[VS_PEER_MAX];  // compact rows: each rank's camera position
   const float* grads[VS_PEER_MAX];
   const float* vis[VS_PEER_MAX];
   float* t[VS_PEER_MAX];
@@ -507,7 +536,7 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
         } else if (MODE == 2) {
           // every rank's load is issued before the sum, which runs in rank order
           const uint32_t vm = ok ? sm.vmask[s] : 0u;
-          const size_t off = ((size_t)(t_base / W) + s) * width + 10u + col;
+          const size_t off = ((size_t)(t_base / W) + s - pa.row_base) * width + 10u + col;
           float tv[VS_PEER_MAX];
 #pragma unroll
           for (uint32_t r = 0; r < VS_PEER_MAX; ++r) tv[r] = ((vm >> r) & 1u) ? pa.grads[r][off] : 0.0f;
@@ -680,14 +709,15 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
     if (g < n) {
       if (MODE == 2) {
         uint32_t vm = 0;
-        for (uint32_t r = 0; r < pa.world; ++r) {
-          const float vr = pa.vis[r][g];
+        const uint32_t gi = g - pa.row_base;
+        for (uint32_t r = 0; r < pa.rows; ++r) {
+          const float vr = pa.vis[r][gi];
           if (vr > 0.0f) vm |= 1u << r;
           vis_g += vr;
         }
-        for (uint32_t r = 0; r < pa.world; ++r) {
+        for (uint32_t r = 0; r < pa.rows; ++r) {
           if (!((vm >> r) & 1u)) continue;
-          const float* d = pa.grads[r] + (size_t)g * width;
+          const float* d = pa.grads[r] + (size_t)gi * width;
 #pragma unroll
           for (int k = 0; k < 10; ++k) gr[k] += d[k];
           go += d[width - 1];
@@ -777,6 +807,72 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
   }
   // Peer stores complete before the barrier that follows this kernel.
   if (MODE == 2) __threadfence_system();
+}
+
+// Compact peer rows -> the shard's dense summed rows, one thread per splat of
+// [begin, end): the view counts of every rank summed in rank order (vis_out),
+// and over the ranks that saw the splat, in rank order, the transforms and
+// opacity gradients summed and the SH gradient rebuilt from each rank's colour
+// gradient and view direction -- direction and basis computed as splat_vjp
+// computes them, from the same mean and camera -- into the dense row layout
+// (transforms | SH | opacity).  Each sum starts at 0 and adds one term per
+// rank, the terms being the values a fresh dense row of that rank holds, so
+// the rows equal the rank-order sums of the dense exchange bit for bit.
+__global__ void __launch_bounds__(256) peer_gather_kernel(uint32_t begin, uint32_t end, int deg,
+                                                          const float* __restrict__ transforms, PeerArgs pa,
+                                                          float* __restrict__ dense, float* __restrict__ vis_out) {
+  // after a barrier that gave up, the peers' rows may be incomplete
+  if (*(volatile const uint32_t*)pa.err & VS_DERR_WAIT) return;
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t g = begin + i;
+  if (g >= end) return;
+  const int nc = (deg + 1) * (deg + 1);
+  const uint32_t width = 10u + 3u * (uint32_t)nc + 1u;
+  uint32_t vm = 0;
+  float vsum = 0.0f;
+  for (uint32_t r = 0; r < pa.world; ++r) {
+    const float vr = pa.vis[r][g];
+    if (vr > 0.0f) vm |= 1u << r;
+    vsum += vr;
+  }
+  vis_out[i] = vsum;
+  if (!vm) return;
+  const V3 mean = {transforms[(size_t)g * 10], transforms[(size_t)g * 10 + 1], transforms[(size_t)g * 10 + 2]};
+  float gr[11], gsh[48];
+#pragma unroll
+  for (int k = 0; k < 11; ++k) gr[k] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 48; ++k) gsh[k] = 0.0f;
+  for (uint32_t r = 0; r < pa.world; ++r) {
+    if (!((vm >> r) & 1u)) continue;
+    const float4* row = reinterpret_cast<const float4*>(pa.grads[r] + (size_t)g * VS_COMPACT_ROW);
+    const float4 x0 = row[0], x1 = row[1], x2 = row[2], x3 = row[3];
+    const float* cp = pa.cams[r];
+    const V3 cam = {cp[0], cp[1], cp[2]};
+    gr[0] += x0.x; gr[1] += x0.y; gr[2] += x0.z; gr[3] += x0.w;
+    gr[4] += x1.x; gr[5] += x1.y; gr[6] += x1.z; gr[7] += x1.w;
+    gr[8] += x2.x; gr[9] += x2.y; gr[10] += x2.z;
+    const float vc[3] = {x2.w, x3.x, x3.y};
+    const V3 uw = v3sub(mean, cam);
+    const float ulen = sqrtf(v3dot(uw, uw));
+    const V3 v = v3scale(uw, 1.0f / ulen);
+    float b[16];
+    sh_basis_all(v.x, v.y, v.z, b);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      if (k < nc) {
+#pragma unroll
+        for (int q = 0; q < 3; ++q) gsh[k * 3 + q] += vc[q] * b[k];
+      }
+    }
+  }
+  float* d = dense + (size_t)i * width;
+#pragma unroll
+  for (int k = 0; k < 10; ++k) d[k] = gr[k];
+#pragma unroll
+  for (int k = 0; k < 48; ++k)
+    if (k < 3 * nc) d[10 + k] = gsh[k];
+  d[width - 1] = gr[10];
 }
 
 PeerArgs single_rank() {
@@ -936,10 +1032,33 @@ VS_API vs_status vs_vjp_dense(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg*
   vs::Uniforms u = frame->u;
   u.sh_half = cfg->sh_half;
   if (frame->v == 0) return VS_OK;
-  vjp_dense_kernel<<<vs::div_up(frame->v, 256), 256, 0, ctx->stream>>>(
+  vjp_dense_kernel<false><<<vs::div_up(frame->v, 256), 256, 0, ctx->stream>>>(
       u, frame->v, transforms, sh_coeffs, raw_opacities, min_scale, (const uint32_t*)frame->global_from_compact.ptr,
-      v_combined, grads, refine, visible, vis_accum); ++ctx->launches;
+      v_combined, grads, refine, visible, vis_accum, nullptr, ctx->d_err); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "vjp_dense launch");
+}
+
+VS_API vs_status vs_vjp_compact(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
+                                const float* transforms, const void* sh_coeffs, const float* raw_opacities,
+                                const float* min_scale, const float* v_combined, float* rows, float* refine,
+                                const float* visible, float* vis_accum, float* cam_out) {
+  if (!ctx) return VS_ERR_INVALID;
+  if (!frame || !frame->rendered || !cfg) return vs_fail(ctx, VS_ERR_INVALID, "vjp_compact: missing frame/config");
+  if (num_splats != frame->n)
+    return vs_fail(ctx, VS_ERR_INVALID, "vjp_compact: %u splats, frame has %u", num_splats, frame->n);
+  if (!transforms || !sh_coeffs || !raw_opacities || !rows || !refine || !visible || !vis_accum || !cam_out ||
+      (frame->v && !v_combined))
+    return vs_fail(ctx, VS_ERR_INVALID, "vjp_compact: null buffer");
+  if ((reinterpret_cast<uintptr_t>(rows) | reinterpret_cast<uintptr_t>(cam_out)) & 15u)
+    return vs_fail(ctx, VS_ERR_INVALID, "vjp_compact: rows and cam_out must be 16-byte aligned");
+  // with no visible splat no rank reads this rank's rows or camera
+  if (num_splats == 0 || frame->v == 0) return VS_OK;
+  vs::Uniforms u = frame->u;
+  u.sh_half = cfg->sh_half;
+  vjp_dense_kernel<true><<<vs::div_up(frame->v, 256), 256, 0, ctx->stream>>>(
+      u, frame->v, transforms, sh_coeffs, raw_opacities, min_scale, (const uint32_t*)frame->global_from_compact.ptr,
+      v_combined, rows, refine, visible, vis_accum, cam_out, ctx->d_err); ++ctx->launches;
+  return vs_cuda(ctx, cudaGetLastError(), "vjp_compact launch");
 }
 
 VS_API vs_status vs_adam_q8_dense(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, float* transforms,
@@ -976,16 +1095,23 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
                    num_splats);
   const uint64_t count_sh = (uint64_t)num_splats * 3 * (sh_degree + 1) * (sh_degree + 1);
   if (count_sh >= 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "adam_q8_peer: %llu SH values exceed u32 indexing", (unsigned long long)count_sh);
+  if (peers->row_format > 1) return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: row format %u", peers->row_format);
+  const bool compact = peers->row_format == 1;
   PeerArgs pa{};
   pa.world = peers->world;
   pa.rank = peers->rank;
   pa.err = ctx->d_err;
   pa.cta_begin = splat_begin / Q8_SPLATS;
   pa.m_off = splat_begin;
+  pa.rows = peers->world;
+  pa.row_base = 0;
   for (uint32_t r = 0; r < peers->world; ++r) {
     if (!peers->grads[r] || !peers->vis[r] || !peers->transforms[r] || !peers->sh_coeffs[r] ||
-        !peers->raw_opacities[r])
+        !peers->raw_opacities[r] || (compact && !peers->cams[r]))
       return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: null buffer of rank %u", r);
+    if (compact && (reinterpret_cast<uintptr_t>(peers->grads[r]) & 15u))
+      return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: compact rows must be 16-byte aligned");
+    pa.cams[r] = compact ? peers->cams[r] : nullptr;
     if (!q8_aligned(peers->transforms[r], peers->sh_coeffs[r], peers->raw_opacities[r], mom_t, mom_sh, mom_o))
       return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: parameter and code arrays must be 16-byte aligned");
     pa.grads[r] = peers->grads[r];
@@ -999,6 +1125,24 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
   u.sh_degree = sh_degree;
   const Q8Args a = to_args(*q8);
   const uint32_t me = peers->rank;
+  if (compact) {
+    // the shard's rows summed over the ranks into the workspace, then read as
+    // the one row source of the update
+    const uint32_t sn = splat_end - splat_begin;
+    const uint32_t width = 10u + 3u * (uint32_t)((sh_degree + 1) * (sh_degree + 1)) + 1u;
+    const size_t row_floats = ((size_t)sn * width + 3) & ~(size_t)3;
+    VS_TRY(vs_ensure(ctx, ctx->peer_rows, (row_floats + sn) * sizeof(float)));
+    float* dense = (float*)ctx->peer_rows.ptr;
+    float* vis_sum = dense + row_floats;
+    peer_gather_kernel<<<vs::div_up(sn, 256), 256, 0, ctx->stream>>>(splat_begin, splat_end, sh_degree, pa.t[me],
+                                                                     pa, dense, vis_sum);
+    ++ctx->launches;
+    VS_CUDA(ctx, cudaGetLastError());
+    pa.rows = 1;
+    pa.row_base = splat_begin;
+    pa.grads[0] = dense;
+    pa.vis[0] = vis_sum;
+  }
   q8_kernel<2><<<vs::div_up(splat_end - splat_begin, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
       u, splat_end, pa.t[me], pa.sh[me], pa.o[me], nullptr, nullptr, nullptr, to_q8(mom_t), to_q8(mom_sh),
       to_q8(mom_o), a, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, pa);

@@ -60,6 +60,8 @@ vs_status vs_check_device_error(vs_ctx* ctx, const char* stage) {
   if (e == 0) return VS_OK;
   VS_CUDA(ctx, cudaMemsetAsync(ctx->d_err, 0, 4, ctx->stream));
   if (e & VS_DERR_WAIT) return vs_fail(ctx, VS_ERR_DEVICE_TIMEOUT, "%s: a bounded device wait gave up", stage);
+  if (e & VS_DERR_STATE)
+    return vs_fail(ctx, VS_ERR_INVALID, "%s: compact gradient rows were written twice for a splat in one step", stage);
   return vs_fail(ctx, VS_ERR_CAPACITY, "%s: device capacity check failed (0x%x)", stage, e);
 }
 
@@ -121,6 +123,7 @@ VS_API void vs_ctx_destroy(vs_ctx* ctx) {
   vs_release(ctx, ctx->misc);
   vs_release(ctx, ctx->io_stage);
   vs_release(ctx, ctx->vjp_rows);
+  vs_release(ctx, ctx->peer_rows);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_pinned) cudaFreeHost(ctx->h_pinned);

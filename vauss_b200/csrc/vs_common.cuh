@@ -364,3 +364,4 @@ __host__ __device__ __forceinline__ uint32_t div_up(uint32_t a, uint32_t b) { re
 #define VS_DERR_WAIT 1u
 #define VS_DERR_CAPACITY 2u
 #define VS_DERR_RANGE 4u
+#define VS_DERR_STATE 8u  // a call's precondition on device state failed (compact rows seen twice)

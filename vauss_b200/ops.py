@@ -333,6 +333,17 @@ def vjp_dense(frame: Frame, cfg: N.RenderCfg, transforms, sh_coeffs, raw_opaciti
                                    _ptr(grads), _ptr(refine), _ptr(visible), _ptr(vis_accum)))
 
 
+def vjp_compact(frame: Frame, cfg: N.RenderCfg, transforms, sh_coeffs, raw_opacities, v_combined, rows, refine,
+                cam_out, min_scale=None, visible=None, vis_accum=None):
+    """One view's compact gradient rows [N, 16] (transforms | raw opacity | colour gradient) and the
+    camera position the VJP used (cam_out [4]), for a rank that renders one view per step; the shard
+    owner rebuilds the SH gradient (adam_q8_peer with PeerSet.row_format = 1)."""
+    ctx = frame.ctx.bind()
+    ctx.check(ctx.lib.vs_vjp_compact(ctx.h, frame.h, ctypes.byref(cfg), transforms.shape[0], _ptr(transforms),
+                                     _ptr(sh_coeffs), _ptr(raw_opacities), _ptr(min_scale), _ptr(v_combined),
+                                     _ptr(rows), _ptr(refine), _ptr(visible), _ptr(vis_accum), _ptr(cam_out)))
+
+
 def min_scale(transforms: torch.Tensor, view_cams: torch.Tensor, factor: float,
               out: torch.Tensor | None = None) -> torch.Tensor:
     """Mip-Splatting 3D-filter floor per splat (compute_min_scale, crates/splat-train/src/train.rs:353-387);

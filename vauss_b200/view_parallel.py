@@ -14,7 +14,11 @@ gradient rows, view counts and parameter replicas live in buffers every rank
 maps over NVLink: after a device barrier each rank runs the 8-bit-moment Adam
 on its shard of the splats only (vs_adam_q8_peer), summing the rows of the
 ranks that saw each splat straight from their memory and storing the new
-parameters into every replica, and a second barrier ends the step.  Without
+parameters into every replica, and a second barrier ends the step.  A rank
+that renders one view per step writes compact rows (vs_vjp_compact: 16
+floats, the SH gradient left as the colour gradient plus the camera position)
+and the owners rebuild the SH gradient, bit for bit as the dense rows hold it;
+with several views per rank the rows are dense.  Without
 one, the dense gradient and the view counts go through one flat all-reduce
 (`exchange`, injectable so the host logic runs with gloo ranks on the CPU) and
 every rank runs the full replicated Adam.
@@ -65,11 +69,12 @@ class ViewParallelTrainer(SplatTrainer):
     dense gradient before the replicated Q8 Adam step."""
 
     def __init__(self, config: TrainConfig, device, exchange: Callable[[torch.Tensor], None] = all_reduce_sum,
-                 peer: PeerGroup | None = None, **kw):
+                 peer: PeerGroup | None = None, compact_rows: bool = True, **kw):
         assert config.optimizer == "q8", "the view-parallel path steps the 8-bit m+v optimizer"
         super().__init__(config, device, **kw)
         self.exchange = exchange
         self.peer = peer
+        self.compact_rows = compact_rows  # with a peer group and one view per rank and step
         self.flat = None
         self.peer_set = None
 
@@ -91,8 +96,9 @@ class ViewParallelTrainer(SplatTrainer):
         width = 10 + nc * 3 + 1
         f32 = torch.float32
         addr_t, addr_sh, addr_o = g.alloc(n * 10, f32), g.alloc(n * nc * 3, f32), g.alloc(n, f32)
-        addr_g = g.alloc(n * width, f32, zero=True)
+        addr_g = g.alloc(n * width, f32, zero=True)  # dense rows, or compact rows of 16 floats
         addr_v = g.alloc(n, f32, zero=True)
+        addr_c = g.alloc(4, f32, zero=True)  # camera position of the rank's view (compact rows)
         t = g.local(addr_t, n * 10, f32).view(n, 10)
         sh = g.local(addr_sh, n * nc * 3, f32).view(n, nc, 3)
         o = g.local(addr_o, n, f32)
@@ -101,10 +107,11 @@ class ViewParallelTrainer(SplatTrainer):
         o.copy_(splats.raw_opacities)
         self._grads = g.local(addr_g, n * width, f32).view(n, width)
         self._vis = g.local(addr_v, n, f32)
+        self._cam = g.local(addr_c, 4, f32)
         ps = N.PeerSet()
         ps.world, ps.rank = g.world, g.rank
         for r in range(g.world):
-            ps.grads[r], ps.vis[r] = addr_g[r], addr_v[r]
+            ps.grads[r], ps.vis[r], ps.cams[r] = addr_g[r], addr_v[r], addr_c[r]
             ps.transforms[r], ps.sh_coeffs[r], ps.raw_opacities[r] = addr_t[r], addr_sh[r], addr_o[r]
         self.peer_set = ps
         self.shard = self.shard_of(n, g.world, g.rank)
@@ -132,6 +139,9 @@ class ViewParallelTrainer(SplatTrainer):
         self.step_count += 1
         n = splats.num_splats
         width = 10 + splats.sh_coeffs.shape[1] * 3 + 1
+        # every rank renders the same number of views per step, so all ranks
+        # agree on the row format
+        compact = peer is not None and self.compact_rows and len(batches) == 1
         if peer is not None:
             # rows are overwritten where vis is 0, so only the counts are cleared
             grads, vis = self._grads, self._vis
@@ -184,8 +194,12 @@ class ViewParallelTrainer(SplatTrainer):
             vc = ops.rasterize_bwd(out.frame, out.out_img, loss.dl_dpred,
                                    self._buf("v_combined", (max(n, 1), 10), torch.float32))
             mark("raster_bwd")
-            ops.vjp_dense(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, grads,
-                          refine, min_scale=splats.min_scale, visible=out.visible, vis_accum=vis)
+            if compact:
+                ops.vjp_compact(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, grads,
+                                refine, self._cam, min_scale=splats.min_scale, visible=out.visible, vis_accum=vis)
+            else:
+                ops.vjp_dense(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, grads,
+                              refine, min_scale=splats.min_scale, visible=out.visible, vis_accum=vis)
             mark("vjp_dense")
             num_visible += out.num_visible
             num_isect += out.num_intersections
@@ -201,6 +215,7 @@ class ViewParallelTrainer(SplatTrainer):
                         noise_scale=c.mean_noise_weight * self.lr_unit() * self.median_scale,
                         noise_limit=self.median_scale, noise_seed=int(self.rng.integers(0, 2 ** 32)))
         if peer is not None:
+            self.peer_set.row_format = 1 if compact else 0
             peer.barrier()  # every rank's rows and counts are complete
             mark("barrier_rows")
             ops.adam_q8_peer(splats.sh_degree, n, self.shard[0], self.shard[1], self.peer_set, o["t"], o["sh"],
