@@ -84,6 +84,9 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-check", action="store_true", help="N > 1: skip the peer vs all-reduce exchange check")
     p.add_argument("--no-config3", action="store_true", help="skip the configs[3] companion leg")
+    p.add_argument("--rows", default="compact", choices=["compact", "dense"],
+                   help="N > 1: gradient rows of the peer exchange with one view per rank (compact 64-byte rows "
+                        "with the SH gradient rebuilt by the owner, or dense rows)")
     a = p.parse_args()
     if a.splats is None:
         a.splats = {1: 1_000_000, 2: N_SPLATS, 3: 6_000_000, 4: 10_000_000}[a.config]
@@ -283,7 +286,8 @@ class Leg:
             from vauss_b200.peer import PeerGroup, gather_bytes_nccl
             gather = (lambda b: gather_bytes_nccl(b, dev)) if world > 1 else (lambda b: [b])
             self.peer = PeerGroup(dev, world, rank, gather)
-            self.trainer = ViewParallelTrainer(self.cfg, dev, peer=self.peer, **self.kw)
+            self.trainer = ViewParallelTrainer(self.cfg, dev, peer=self.peer, compact_rows=args.rows == "compact",
+                                               **self.kw)
             self.splats = self.trainer.adopt(splats)
             del splats
         else:
@@ -516,16 +520,24 @@ def exchange_check(leg):
     prm = max(mixed_rel(g, w) for g, w in zip(got, want))
     upd = max(float(np.abs((g - b0) - (w - b0)).max()) / max(float(np.abs(w - b0).max()), 1e-30)
               for g, w, b0 in zip(got, want, base))
-    t = torch.tensor([prm, upd], dtype=torch.float64, device=leg.dev)
+    # values whose update differs by more than 1e-3 of the largest update
+    over = sum(int((np.abs((g - b0) - (w - b0)) > 1e-3 * max(float(np.abs(w - b0).max()), 1e-30)).sum())
+               for g, w, b0 in zip(got, want, base))
+    total = sum(g.size for g in got)
+    t = torch.tensor([prm, upd, over / total], dtype=torch.float64, device=leg.dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     tr.optim = saved
     del ref, other
     torch.cuda.empty_cache()
     leg.restore()
-    return {"params_max_rel": float(t[0]), "update_max_rel": float(t[1]),
+    return {"params_max_rel": float(t[0]), "update_max_rel": float(t[1]), "update_frac_over_1e-3": float(t[2]),
+            "rows": "compact" if getattr(tr, "compact_rows", False) and len(b) == 1 else "dense",
             "what": "one step from the timed-region parameters and zero moments through the peer-memory exchange "
-                    "and through an NCCL all-reduce + replicated Adam; mixed rel over all parameters, and the "
-                    "largest update difference over the largest update"}
+                    "and through an NCCL all-reduce + replicated Adam; mixed rel over all parameters, the "
+                    "largest update difference over the largest update, and the fraction of values whose update "
+                    "differs by more than 1e-3 of the largest (from zero moments Adam's step is about lr * sign(g), "
+                    "so a near-zero gradient whose rounding differs between the two renders moves one update by "
+                    "up to 2 lr)"}
 
 
 def parity_leg(leg):
