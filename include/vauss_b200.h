@@ -304,11 +304,10 @@ typedef struct vs_peer_set {
  * splat_end) only (splat_begin a multiple of 256), with the gradient of each
  * splat summed in rank order over the ranks whose vis > 0 and the noise gated
  * on the summed vis; the moments (mom_*) hold that shard only, and the new
- * parameters go to every rank's replica.  With row_format 1 the shard's rows
- * are first gathered from the ranks' compact rows into dense summed rows in
- * the ctx's workspace (the SH gradient rebuilt from each rank's colour
- * gradient and camera), with the same sums, bit for bit, as row_format 0 over
- * the dense rows of the same views.  All ranks' gradient rows must be
+ * parameters go to every rank's replica.  With row_format 1 the ranks'
+ * compact rows are summed in shared memory, the SH gradient rebuilt from each
+ * rank's colour gradient and camera, with the same sums, bit for bit, as
+ * row_format 0 over the dense rows of the same views.  All ranks' gradient rows must be
  * complete (vs_peer_barrier) before the call, and no rank may read its
  * replica until every rank's call has finished (a second barrier). */
 VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, uint32_t splat_begin,

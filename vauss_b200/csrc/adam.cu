@@ -13,8 +13,13 @@
 //     each visible splat into a compact row, then Adam on all 59 parameters +
 //     refine statistics + mean noise, one CTA per 256 splats;
 //   q8_kernel<1>  -- the same Adam from an all-reduced dense gradient;
-//   q8_kernel<2>  -- the same Adam for one rank's shard over peer memory;
-//   vjp_dense_kernel -- accumulates one view's dense gradient rows.
+//   q8_kernel<2>  -- the same Adam for one rank's shard over peer memory,
+//     the other ranks' dense rows read and summed from their memory;
+//   q8_kernel<3>  -- the same from compact rows (one view per rank): the SH
+//     gradient rebuilt per rank from its colour gradient and camera into
+//     shared memory;
+//   vjp_dense_kernel -- accumulates one view's dense gradient rows, or writes
+//     its compact rows.
 #include "vjp.cuh"
 #include "vs_internal.cuh"
 
@@ -413,11 +418,7 @@ struct PeerArgs {
   const uint32_t* err;
   uint32_t cta_begin;  // first CTA (256 splats) of the shard
   uint32_t m_off;      // first splat covered by the moment arrays
-  // gradient row sources: `rows` arrays grads[r] / vis[r] indexed by splat -
-  // row_base (the ranks' dense rows, rows = world and row_base = 0; or one
-  // shard-local array of rows gathered from compact rows)
-  uint32_t rows, row_base;
-  const float* cams[VS_PEER_MAX];  // compact rows: each rank's camera position
+  const float* cams[VS_PEER_MAX];  // MODE 3 (compact rows): each rank's camera position
   const float* grads[VS_PEER_MAX];
   const float* vis[VS_PEER_MAX];
   float* t[VS_PEER_MAX];
@@ -471,7 +472,12 @@ struct Q8Shared {
   const float* noise;  // [256][3]
   const float* lr_t;   // [10]
   const uint32_t* vmask;  // [256] ranks whose rows are read (MODE 2)
+  const float* gsh;       // [256][Q8_GSH_STRIDE] summed SH gradients (MODE 3)
 };
+
+// Row stride of the MODE 3 SH gradients in shared memory (odd: a warp that
+// walks the rows of consecutive splats hits distinct banks).
+constexpr uint32_t Q8_GSH_STRIDE = 49;
 
 // One 256-value block of one parameter tensor, by one warp.  `W` is the
 // tensor's row width (values per splat), `KIND` 0 = transforms, 1 = SH,
@@ -486,7 +492,8 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
                                          const Q8Shared& sm, const float* __restrict__ grow, uint32_t width,
                                          const PeerArgs& pa) {
   float* p = tensor + t_base;
-  const size_t mb = MODE == 2 ? t_base - (size_t)pa.m_off * W : t_base;  // offset in the moment arrays
+  constexpr bool kPeer = MODE >= 2;
+  const size_t mb = kPeer ? t_base - (size_t)pa.m_off * W : t_base;  // offset in the moment arrays
   uint8_t* mcp = q.mc + mb;
   uint8_t* vcp = q.vc + mb;
   const size_t blk = mb / 256u + jb;
@@ -536,7 +543,7 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
         } else if (MODE == 2) {
           // every rank's load is issued before the sum, which runs in rank order
           const uint32_t vm = ok ? sm.vmask[s] : 0u;
-          const size_t off = ((size_t)(t_base / W) + s - pa.row_base) * width + 10u + col;
+          const size_t off = ((size_t)(t_base / W) + s) * width + 10u + col;
           float tv[VS_PEER_MAX];
 #pragma unroll
           for (uint32_t r = 0; r < VS_PEER_MAX; ++r) tv[r] = ((vm >> r) & 1u) ? pa.grads[r][off] : 0.0f;
@@ -545,6 +552,8 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
           for (uint32_t r = 0; r < VS_PEER_MAX; ++r)
             if ((vm >> r) & 1u) acc += tv[r];
           g[k] = acc;
+        } else if (MODE == 3) {
+          g[k] = ok ? sm.gsh[s * Q8_GSH_STRIDE + col] : 0.0f;
         } else {
           g[k] = ok ? sm.vc[s * 3u + r3] * sm.bas[s * 16u + c3] : 0.0f;
         }
@@ -631,9 +640,9 @@ __device__ __forceinline__ void q8_block(uint32_t lane, uint32_t jb, uint32_t va
       vo |= qr << (8 * e);
     }
     // MODE 2 stores the parameters into every replica (peers over NVLink)
-    const uint32_t nrep = MODE == 2 ? pa.world : 1u;
+    const uint32_t nrep = kPeer ? pa.world : 1u;
     for (uint32_t r = 0; r < nrep; ++r) {
-      float* pr = MODE == 2 ? (KIND == 0 ? pa.t[r] : (KIND == 1 ? pa.sh[r] : pa.o[r])) + t_base : p;
+      float* pr = kPeer ? (KIND == 0 ? pa.t[r] : (KIND == 1 ? pa.sh[r] : pa.o[r])) + t_base : p;
       if (full) {
         *reinterpret_cast<float4*>(pr + li0) = make_float4(pv[4 * h], pv[4 * h + 1], pv[4 * h + 2], pv[4 * h + 3]);
       } else {
@@ -671,18 +680,22 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
     float* __restrict__ refine_norm, float* __restrict__ vis_count, float* __restrict__ max_screen, PeerArgs pa) {
   __shared__ float s_gt[Q8_SPLATS * 10];
   __shared__ float s_go[Q8_SPLATS];
-  __shared__ float s_vc[Q8_SPLATS * 3];
-  __shared__ float s_bas[Q8_SPLATS * 16];
+  __shared__ float s_vc[MODE == 0 ? Q8_SPLATS * 3 : 1];
+  __shared__ float s_bas[MODE == 0 ? Q8_SPLATS * 16 : 1];
   __shared__ float s_noise[Q8_SPLATS * 3];
   __shared__ uint32_t s_vmask[MODE == 2 ? Q8_SPLATS : 1];
   __shared__ float s_lr[10];
   constexpr bool kDense = MODE != 0;
+  constexpr bool kPeer = MODE >= 2;
+  // MODE 3: the summed SH gradients, [256][Q8_GSH_STRIDE] in dynamic shared memory
+  extern __shared__ __align__(16) float s_dyn[];
+  float* s_gsh = s_dyn;
 
   const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
   // After a barrier that gave up, the peers' rows may be incomplete and other
   // ranks may still read this replica: no peer load or store, no update.
-  if (MODE == 2 && (*(volatile const uint32_t*)pa.err & VS_DERR_WAIT)) return;
-  const uint32_t base = ((MODE == 2 ? pa.cta_begin : 0u) + blockIdx.x) * Q8_SPLATS;
+  if (kPeer && (*(volatile const uint32_t*)pa.err & VS_DERR_WAIT)) return;
+  const uint32_t base = ((kPeer ? pa.cta_begin : 0u) + blockIdx.x) * Q8_SPLATS;
   if (tid == 0) {
 #pragma unroll
     for (int k = 0; k < 10; ++k) s_lr[k] = a.lr_t[k];
@@ -709,20 +722,59 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
     if (g < n) {
       if (MODE == 2) {
         uint32_t vm = 0;
-        const uint32_t gi = g - pa.row_base;
-        for (uint32_t r = 0; r < pa.rows; ++r) {
-          const float vr = pa.vis[r][gi];
+        for (uint32_t r = 0; r < pa.world; ++r) {
+          const float vr = pa.vis[r][g];
           if (vr > 0.0f) vm |= 1u << r;
           vis_g += vr;
         }
-        for (uint32_t r = 0; r < pa.rows; ++r) {
+        for (uint32_t r = 0; r < pa.world; ++r) {
           if (!((vm >> r) & 1u)) continue;
-          const float* d = pa.grads[r] + (size_t)gi * width;
+          const float* d = pa.grads[r] + (size_t)g * width;
 #pragma unroll
           for (int k = 0; k < 10; ++k) gr[k] += d[k];
           go += d[width - 1];
         }
         s_vmask[tid] = vm;
+      } else if (MODE == 3) {
+        // compact rows: the transforms and opacity gradients summed in rank
+        // order, and the SH gradient rebuilt per rank from its colour gradient
+        // and the view direction and basis computed as splat_vjp computes
+        // them (same mean, same camera), each sum from 0 one term per rank:
+        // the sums of the dense exchange, bit for bit
+        float* gs = s_gsh + tid * Q8_GSH_STRIDE;
+        for (uint32_t j = 0; j < wsh; ++j) gs[j] = 0.0f;
+        uint32_t vm = 0;
+        for (uint32_t r = 0; r < pa.world; ++r) {
+          const float vr = pa.vis[r][g];
+          if (vr > 0.0f) vm |= 1u << r;
+          vis_g += vr;
+        }
+        if (vm) {
+          const V3 mean = {transforms[(size_t)g * 10], transforms[(size_t)g * 10 + 1],
+                           transforms[(size_t)g * 10 + 2]};
+          for (uint32_t r = 0; r < pa.world; ++r) {
+            if (!((vm >> r) & 1u)) continue;
+            const float4* row = reinterpret_cast<const float4*>(pa.grads[r] + (size_t)g * VS_COMPACT_ROW);
+            const float4 x0 = row[0], x1 = row[1], x2 = row[2], x3 = row[3];
+            const float* cp = pa.cams[r];
+            const V3 cam = {cp[0], cp[1], cp[2]};
+            gr[0] += x0.x; gr[1] += x0.y; gr[2] += x0.z; gr[3] += x0.w;
+            gr[4] += x1.x; gr[5] += x1.y; gr[6] += x1.z; gr[7] += x1.w;
+            gr[8] += x2.x; gr[9] += x2.y; go += x2.z;
+            const float cv[3] = {x2.w, x3.x, x3.y};
+            const V3 uw = v3sub(mean, cam);
+            const float ulen = sqrtf(v3dot(uw, uw));
+            const V3 dv = v3scale(uw, 1.0f / ulen);
+            sh_basis_all(dv.x, dv.y, dv.z, b);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              if (k < nc) {
+#pragma unroll
+                for (int q = 0; q < 3; ++q) gs[k * 3 + q] = gs[k * 3 + q] + cv[q] * b[k];
+              }
+            }
+          }
+        }
       } else if (kDense) {
         const float* d = grads + (size_t)g * width;
 #pragma unroll
@@ -753,10 +805,10 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
 #pragma unroll
     for (int k = 0; k < 10; ++k) s_gt[tid * 10 + k] = gr[k];
     s_go[tid] = go;
-    s_vc[tid * 3 + 0] = vc[0];
-    s_vc[tid * 3 + 1] = vc[1];
-    s_vc[tid * 3 + 2] = vc[2];
     if (!kDense) {
+      s_vc[tid * 3 + 0] = vc[0];
+      s_vc[tid * 3 + 1] = vc[1];
+      s_vc[tid * 3 + 2] = vc[2];
 #pragma unroll
       for (int k = 0; k < 16; ++k) s_bas[tid * 16 + k] = b[k];
     }
@@ -767,7 +819,7 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
         const float o = 1.0f / (1.0f + vs_expf(-raw_opac[g]));
         s_go[tid] = s_go[tid] + a.opac_reg * o * (1.0f - o);
       }
-      if ((visible || MODE == 2) && a.noise_scale != 0.0f) {
+      if ((visible || kPeer) && a.noise_scale != 0.0f) {
         // without per-view opacities (the multi-view path) the gate uses the
         // unfloored sigmoid opacity, which projection also reports when no
         // min_scale floor is set
@@ -786,7 +838,7 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
   const uint32_t nb_t = div_up(splats_here * 10u, 256u);
   const uint32_t nb_sh = div_up(splats_here * wsh, 256u);
   const uint32_t total_blocks = nb_t + nb_sh + 1u;
-  const Q8Shared sm{s_gt, s_go, s_vc, s_bas, s_noise, s_lr, s_vmask};
+  const Q8Shared sm{s_gt, s_go, s_vc, s_bas, s_noise, s_lr, s_vmask, s_gsh};
   const float* grow = MODE == 1 ? grads + (size_t)base * width : nullptr;
   for (uint32_t job = warp; job < total_blocks; job += Q8_WARPS) {
     if (job < nb_t) {
@@ -806,73 +858,7 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
     }
   }
   // Peer stores complete before the barrier that follows this kernel.
-  if (MODE == 2) __threadfence_system();
-}
-
-// Compact peer rows -> the shard's dense summed rows, one thread per splat of
-// [begin, end): the view counts of every rank summed in rank order (vis_out),
-// and over the ranks that saw the splat, in rank order, the transforms and
-// opacity gradients summed and the SH gradient rebuilt from each rank's colour
-// gradient and view direction -- direction and basis computed as splat_vjp
-// computes them, from the same mean and camera -- into the dense row layout
-// (transforms | SH | opacity).  Each sum starts at 0 and adds one term per
-// rank, the terms being the values a fresh dense row of that rank holds, so
-// the rows equal the rank-order sums of the dense exchange bit for bit.
-__global__ void __launch_bounds__(256) peer_gather_kernel(uint32_t begin, uint32_t end, int deg,
-                                                          const float* __restrict__ transforms, PeerArgs pa,
-                                                          float* __restrict__ dense, float* __restrict__ vis_out) {
-  // after a barrier that gave up, the peers' rows may be incomplete
-  if (*(volatile const uint32_t*)pa.err & VS_DERR_WAIT) return;
-  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  const uint32_t g = begin + i;
-  if (g >= end) return;
-  const int nc = (deg + 1) * (deg + 1);
-  const uint32_t width = 10u + 3u * (uint32_t)nc + 1u;
-  uint32_t vm = 0;
-  float vsum = 0.0f;
-  for (uint32_t r = 0; r < pa.world; ++r) {
-    const float vr = pa.vis[r][g];
-    if (vr > 0.0f) vm |= 1u << r;
-    vsum += vr;
-  }
-  vis_out[i] = vsum;
-  if (!vm) return;
-  const V3 mean = {transforms[(size_t)g * 10], transforms[(size_t)g * 10 + 1], transforms[(size_t)g * 10 + 2]};
-  float gr[11], gsh[48];
-#pragma unroll
-  for (int k = 0; k < 11; ++k) gr[k] = 0.0f;
-#pragma unroll
-  for (int k = 0; k < 48; ++k) gsh[k] = 0.0f;
-  for (uint32_t r = 0; r < pa.world; ++r) {
-    if (!((vm >> r) & 1u)) continue;
-    const float4* row = reinterpret_cast<const float4*>(pa.grads[r] + (size_t)g * VS_COMPACT_ROW);
-    const float4 x0 = row[0], x1 = row[1], x2 = row[2], x3 = row[3];
-    const float* cp = pa.cams[r];
-    const V3 cam = {cp[0], cp[1], cp[2]};
-    gr[0] += x0.x; gr[1] += x0.y; gr[2] += x0.z; gr[3] += x0.w;
-    gr[4] += x1.x; gr[5] += x1.y; gr[6] += x1.z; gr[7] += x1.w;
-    gr[8] += x2.x; gr[9] += x2.y; gr[10] += x2.z;
-    const float vc[3] = {x2.w, x3.x, x3.y};
-    const V3 uw = v3sub(mean, cam);
-    const float ulen = sqrtf(v3dot(uw, uw));
-    const V3 v = v3scale(uw, 1.0f / ulen);
-    float b[16];
-    sh_basis_all(v.x, v.y, v.z, b);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      if (k < nc) {
-#pragma unroll
-        for (int q = 0; q < 3; ++q) gsh[k * 3 + q] += vc[q] * b[k];
-      }
-    }
-  }
-  float* d = dense + (size_t)i * width;
-#pragma unroll
-  for (int k = 0; k < 10; ++k) d[k] = gr[k];
-#pragma unroll
-  for (int k = 0; k < 48; ++k)
-    if (k < 3 * nc) d[10 + k] = gsh[k];
-  d[width - 1] = gr[10];
+  if (kPeer) __threadfence_system();
 }
 
 PeerArgs single_rank() {
@@ -1103,8 +1089,6 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
   pa.err = ctx->d_err;
   pa.cta_begin = splat_begin / Q8_SPLATS;
   pa.m_off = splat_begin;
-  pa.rows = peers->world;
-  pa.row_base = 0;
   for (uint32_t r = 0; r < peers->world; ++r) {
     if (!peers->grads[r] || !peers->vis[r] || !peers->transforms[r] || !peers->sh_coeffs[r] ||
         !peers->raw_opacities[r] || (compact && !peers->cams[r]))
@@ -1126,26 +1110,17 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
   const Q8Args a = to_args(*q8);
   const uint32_t me = peers->rank;
   if (compact) {
-    // the shard's rows summed over the ranks into the workspace, then read as
-    // the one row source of the update
-    const uint32_t sn = splat_end - splat_begin;
-    const uint32_t width = 10u + 3u * (uint32_t)((sh_degree + 1) * (sh_degree + 1)) + 1u;
-    const size_t row_floats = ((size_t)sn * width + 3) & ~(size_t)3;
-    VS_TRY(vs_ensure(ctx, ctx->peer_rows, (row_floats + sn) * sizeof(float)));
-    float* dense = (float*)ctx->peer_rows.ptr;
-    float* vis_sum = dense + row_floats;
-    peer_gather_kernel<<<vs::div_up(sn, 256), 256, 0, ctx->stream>>>(splat_begin, splat_end, sh_degree, pa.t[me],
-                                                                     pa, dense, vis_sum);
-    ++ctx->launches;
-    VS_CUDA(ctx, cudaGetLastError());
-    pa.rows = 1;
-    pa.row_base = splat_begin;
-    pa.grads[0] = dense;
-    pa.vis[0] = vis_sum;
+    // the compact rows are summed, and the SH gradient rebuilt, in shared memory
+    constexpr int kGshBytes = (int)(Q8_SPLATS * Q8_GSH_STRIDE * sizeof(float));
+    VS_CUDA(ctx, cudaFuncSetAttribute(q8_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGshBytes));
+    q8_kernel<3><<<vs::div_up(splat_end - splat_begin, Q8_SPLATS), Q8_SPLATS, kGshBytes, ctx->stream>>>(
+        u, splat_end, pa.t[me], pa.sh[me], pa.o[me], nullptr, nullptr, nullptr, to_q8(mom_t), to_q8(mom_sh),
+        to_q8(mom_o), a, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, pa);
+  } else {
+    q8_kernel<2><<<vs::div_up(splat_end - splat_begin, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
+        u, splat_end, pa.t[me], pa.sh[me], pa.o[me], nullptr, nullptr, nullptr, to_q8(mom_t), to_q8(mom_sh),
+        to_q8(mom_o), a, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, pa);
   }
-  q8_kernel<2><<<vs::div_up(splat_end - splat_begin, Q8_SPLATS), Q8_SPLATS, 0, ctx->stream>>>(
-      u, splat_end, pa.t[me], pa.sh[me], pa.o[me], nullptr, nullptr, nullptr, to_q8(mom_t), to_q8(mom_sh),
-      to_q8(mom_o), a, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, pa);
   ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "adam_q8_peer launch");
 }

@@ -123,7 +123,6 @@ VS_API void vs_ctx_destroy(vs_ctx* ctx) {
   vs_release(ctx, ctx->misc);
   vs_release(ctx, ctx->io_stage);
   vs_release(ctx, ctx->vjp_rows);
-  vs_release(ctx, ctx->peer_rows);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->d_err) cudaFree(ctx->d_err);
   if (ctx->h_pinned) cudaFreeHost(ctx->h_pinned);

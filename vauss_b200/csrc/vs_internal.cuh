@@ -27,7 +27,6 @@ struct vs_ctx {
   DevBuf sort_keys, sort_vals, sort_hist, scan_sums, misc;
   DevBuf io_stage;  // checkpoint I/O chunks (two halves)
   DevBuf vjp_rows;  // per-visible-splat VJP rows of the single-view Q8 step
-  DevBuf peer_rows;  // a shard's summed dense rows gathered from compact peer rows
 };
 
 struct vs_frame {
