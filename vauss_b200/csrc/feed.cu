@@ -340,7 +340,10 @@ vs_status start(vs_feed* f) {
   for (uint32_t s = 0; s < R; ++s) {
     VS_CUDA(ctx, cudaHostAlloc(reinterpret_cast<void**>(&f->host_stage[s]), raw, cudaHostAllocDefault));
     VS_CUDA(ctx, cudaMalloc(reinterpret_cast<void**>(&f->dev_stage[s]), raw));
-    VS_CUDA(ctx, cudaEventCreateWithFlags(&f->stage_done[s], cudaEventDisableTiming));
+    // the workers wait on these from the host: a blocking-sync event puts the
+    // waiting thread to sleep instead of spinning a core, which one process
+    // per GPU with several workers each would oversubscribe
+    VS_CUDA(ctx, cudaEventCreateWithFlags(&f->stage_done[s], cudaEventDisableTiming | cudaEventBlockingSync));
   }
   const uint32_t outs = R + f->cfg.hold;
   f->out_slots.assign(outs, nullptr);
