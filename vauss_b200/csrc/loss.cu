@@ -14,9 +14,10 @@
 //   -> horizontal blur of the three coefficient products    [42 x 32]
 //   -> vertical blur at the block: dL/dpred                 [32 x 32]
 //
-// Each blur runs as register sliding windows: a thread produces SEG
-// consecutive outputs along the blur direction from one (SEG + 10)-value
-// window.  Every output still sums in the reference's order (taps d = 1..5 as
+// Each blur runs as register sliding windows: a thread produces S
+// consecutive outputs along the blur direction from one (S + 10)-value
+// window (S = 7 over the 42-pixel footprint, 8 over the 32-pixel block, so the
+// windows tile both exactly).  Every output still sums in the reference's order (taps d = 1..5 as
 // (left + right) * w[5-d], then the centre), so the values equal the two-pass
 // computation bit for bit.  The loss partials stay per 16x16 tile, each
 // summed with the reference's shared-memory tree (lib.rs:108-123).
@@ -31,9 +32,14 @@ constexpr int HALO = 5;
 constexpr int R0 = LB + 4 * HALO;  // 52: pred/gt footprint
 constexpr int R1 = LB + 2 * HALO;  // 42: coefficient footprint
 constexpr int NT = 256;
-constexpr int SEG = 4;             // outputs per thread and window
-constexpr int WIN = SEG + 2 * HALO;
+// outputs per thread and window: SEG1 over the 42-pixel coefficient footprint
+// (42 = 6 x 7, no overrun), SEG2 over the 32-pixel block
+constexpr int SEG1 = 7;
+constexpr int SEG2 = 8;
+constexpr int WIN1 = SEG1 + 2 * HALO;
+constexpr int WIN2 = SEG2 + 2 * HALO;
 constexpr int SUB = 16;            // loss partials per 16x16 tile
+static_assert(R1 % SEG1 == 0 && LB % SEG2 == 0, "segments tile the footprints");
 
 __constant__ float c_taps[11];
 
@@ -43,10 +49,10 @@ struct LossSmem {
   float x[R0][R0];
   float y[R0][R0];
   union {
-    float h1[5][R0][R1 + 2];  // + 2 columns: the last segment overruns the footprint
-    float h2[3][R1 + 2][LB];
+    float h1[5][R0][R1];
+    float h2[3][R1][LB];
   } u;
-  float cm[3][R1 + 2][R1 + 2];
+  float cm[3][R1][R1];
   float red[4][SUB * SUB];
 };
 
@@ -54,10 +60,11 @@ __device__ __forceinline__ float gtap(int i) { return c_taps[i]; }
 
 // out[j] = sum over the 11-tap window centred at win[j + 5], in the
 // reference's order.
-template <int N>
-__device__ __forceinline__ void blur_seg(const float (&win)[N], float (&out)[SEG]) {
+template <int S, int N>
+__device__ __forceinline__ void blur_seg(const float (&win)[N], float (&out)[S]) {
+  static_assert(N == S + 2 * HALO, "window");
 #pragma unroll
-  for (int j = 0; j < SEG; ++j) {
+  for (int j = 0; j < S; ++j) {
     float acc = 0.0f;
 #pragma unroll
     for (int d = 1; d < 6; ++d) acc += (win[j + HALO - d] + win[j + HALO + d]) * gtap(5 - d);
@@ -99,38 +106,37 @@ __global__ void __launch_bounds__(NT) loss_kernel(uint32_t h, uint32_t w, const 
   __syncthreads();
 
   // 2. horizontal blur of the five moments: rows 0..51, columns block +- 5
-  constexpr int HSEGS = (R1 + SEG - 1) / SEG;  // 11
+  constexpr int HSEGS = R1 / SEG1;  // 6
   for (int it = tid; it < R0 * HSEGS; it += NT) {
-    const int ly = it / HSEGS, c0 = (it % HSEGS) * SEG;
-    float wx[WIN], wy[WIN];
+    const int ly = it / HSEGS, c0 = (it % HSEGS) * SEG1;
+    float wx[WIN1], wy[WIN1];
 #pragma unroll
-    for (int k = 0; k < WIN; ++k) {
-      const int col = min(c0 + k, R0 - 1);  // columns past the footprint only feed discarded outputs
-      wx[k] = s_x[ly][col];
-      wy[k] = s_y[ly][col];
+    for (int k = 0; k < WIN1; ++k) {
+      wx[k] = s_x[ly][c0 + k];
+      wy[k] = s_y[ly][c0 + k];
     }
-    float m[WIN], o[SEG];
+    float m[WIN1], o[SEG1];
     blur_seg(wx, o);
 #pragma unroll
-    for (int j = 0; j < SEG; ++j) s_h1[0][ly][c0 + j] = o[j];
+    for (int j = 0; j < SEG1; ++j) s_h1[0][ly][c0 + j] = o[j];
 #pragma unroll
-    for (int k = 0; k < WIN; ++k) m[k] = wx[k] * wx[k];
+    for (int k = 0; k < WIN1; ++k) m[k] = wx[k] * wx[k];
     blur_seg(m, o);
 #pragma unroll
-    for (int j = 0; j < SEG; ++j) s_h1[1][ly][c0 + j] = o[j];
+    for (int j = 0; j < SEG1; ++j) s_h1[1][ly][c0 + j] = o[j];
     blur_seg(wy, o);
 #pragma unroll
-    for (int j = 0; j < SEG; ++j) s_h1[2][ly][c0 + j] = o[j];
+    for (int j = 0; j < SEG1; ++j) s_h1[2][ly][c0 + j] = o[j];
 #pragma unroll
-    for (int k = 0; k < WIN; ++k) m[k] = wy[k] * wy[k];
+    for (int k = 0; k < WIN1; ++k) m[k] = wy[k] * wy[k];
     blur_seg(m, o);
 #pragma unroll
-    for (int j = 0; j < SEG; ++j) s_h1[3][ly][c0 + j] = o[j];
+    for (int j = 0; j < SEG1; ++j) s_h1[3][ly][c0 + j] = o[j];
 #pragma unroll
-    for (int k = 0; k < WIN; ++k) m[k] = wx[k] * wy[k];
+    for (int k = 0; k < WIN1; ++k) m[k] = wx[k] * wy[k];
     blur_seg(m, o);
 #pragma unroll
-    for (int j = 0; j < SEG; ++j) s_h1[4][ly][c0 + j] = o[j];
+    for (int j = 0; j < SEG1; ++j) s_h1[4][ly][c0 + j] = o[j];
   }
   __syncthreads();
 
@@ -138,19 +144,18 @@ __global__ void __launch_bounds__(NT) loss_kernel(uint32_t h, uint32_t w, const 
   //    block's own pixels also produce the loss value.
   const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
   for (int it = tid; it < R1 * HSEGS; it += NT) {
-    const int rx = it % R1, r0 = (it / R1) * SEG;
-    float o[5][SEG];
+    const int rx = it % R1, r0 = (it / R1) * SEG1;
+    float o[5][SEG1];
 #pragma unroll
     for (int k = 0; k < 5; ++k) {
-      float win[WIN];
+      float win[WIN1];
 #pragma unroll
-      for (int q = 0; q < WIN; ++q) win[q] = s_h1[k][min(r0 + q, R0 - 1)][rx];
+      for (int q = 0; q < WIN1; ++q) win[q] = s_h1[k][r0 + q][rx];
       blur_seg(win, o[k]);
     }
 #pragma unroll
-    for (int j = 0; j < SEG; ++j) {
+    for (int j = 0; j < SEG1; ++j) {
       const int ry = r0 + j;
-      if (ry >= R1) break;
       const int gy = y0 - HALO + ry, gx = x0 - HALO + rx;
       const bool in_img = gy >= 0 && gy < H && gx >= 0 && gx < W;
       const bool in_blk = ry >= HALO && ry < HALO + LB && rx >= HALO && rx < HALO + LB;
@@ -203,34 +208,34 @@ __global__ void __launch_bounds__(NT) loss_kernel(uint32_t h, uint32_t w, const 
   if (!dl_dpred) return;
 
   // 4. horizontal blur of the coefficient products: rows block +- 5, block columns
-  constexpr int BSEGS = LB / SEG;  // 8
+  constexpr int BSEGS = LB / SEG2;  // 4
   for (int it = tid; it < R1 * BSEGS; it += NT) {
-    const int ry = it / BSEGS, t0 = (it % BSEGS) * SEG;
+    const int ry = it / BSEGS, t0 = (it % BSEGS) * SEG2;
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
-      float win[WIN], o[SEG];
+      float win[WIN2], o[SEG2];
 #pragma unroll
-      for (int q = 0; q < WIN; ++q) win[q] = s_cm[k][ry][t0 + q];
+      for (int q = 0; q < WIN2; ++q) win[q] = s_cm[k][ry][t0 + q];
       blur_seg(win, o);
 #pragma unroll
-      for (int j = 0; j < SEG; ++j) s_h2[k][ry][t0 + j] = o[j];
+      for (int j = 0; j < SEG2; ++j) s_h2[k][ry][t0 + j] = o[j];
     }
   }
   __syncthreads();
 
   // 5. vertical blur at the block pixels -> dL/dpred
   for (int it = tid; it < LB * BSEGS; it += NT) {
-    const int tx = it % LB, t0 = (it / LB) * SEG;
-    float s[3][SEG];
+    const int tx = it % LB, t0 = (it / LB) * SEG2;
+    float s[3][SEG2];
 #pragma unroll
     for (int k = 0; k < 3; ++k) {
-      float win[WIN];
+      float win[WIN2];
 #pragma unroll
-      for (int q = 0; q < WIN; ++q) win[q] = s_h2[k][t0 + q][tx];
+      for (int q = 0; q < WIN2; ++q) win[q] = s_h2[k][t0 + q][tx];
       blur_seg(win, s[k]);
     }
 #pragma unroll
-    for (int j = 0; j < SEG; ++j) {
+    for (int j = 0; j < SEG2; ++j) {
       const int ty = t0 + j;
       const int gy = y0 + ty, gx = x0 + tx;
       if (gy < H && gx < W) {
