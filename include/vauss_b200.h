@@ -240,23 +240,25 @@ VS_API vs_status vs_vjp_dense(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg*
                               const float* min_scale, const float* v_combined, float* grads, float* refine,
                               const float* visible, float* vis_accum);
 
-/* The compact form of vs_vjp_dense for a rank that renders ONE view per step
- * (the view-parallel exchange, no reference counterpart): writes
+/* The compact form of vs_vjp_dense for the view-parallel exchange (no
+ * reference counterpart): view `slot` (0..31) of this rank's step writes
  * rows [N, VS_COMPACT_ROW] = (transforms gradient 10 | raw-opacity gradient |
- * rasterizer colour gradient 3 | 0 0) of the visible splats, adds visible to
- * vis_accum and the refine weight to refine, and stores the camera position
- * the VJP used into cam_out[0..2] (cam_out[3] = 0).  The SH gradient is the
- * colour gradient times the SH basis of the view direction from cam_out, which
- * the shard owner rebuilds (vs_adam_q8_peer with row_format 1) bit for bit as
- * the dense row holds it, so 64 bytes per splat cross NVLink instead of
- * 4(10 + 3(d+1)^2 + 1).  A splat whose vis_accum was already non-zero (a
- * second view in the step) sets a device error that vs_ctx_check reports as
- * VS_ERR_INVALID. */
+ * rasterizer colour gradient 3 | 0 0) of its visible splats, sets bit `slot`
+ * of view_mask[g] for them, adds visible to vis_accum and the refine weight to
+ * refine, and stores the camera position the VJP used into cam_out[0..2]
+ * (cam_out[3] = 0); rows and cam_out are that slot's own arrays.  The SH
+ * gradient is the colour gradient times the SH basis of the view direction
+ * from cam_out, which the shard owner rebuilds (vs_adam_q8_peer with
+ * row_format 1), so 64 bytes per splat and view are written and cross NVLink
+ * instead of a dense row.  A splat whose bit was already set (the slot used
+ * twice in a step) sets a device error that vs_ctx_check reports as
+ * VS_ERR_INVALID; view_mask is cleared by the caller once per step. */
 #define VS_COMPACT_ROW 16
 VS_API vs_status vs_vjp_compact(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
                                 const float* transforms, const void* sh_coeffs, const float* raw_opacities,
                                 const float* min_scale, const float* v_combined, float* rows, float* refine,
-                                const float* visible, float* vis_accum, float* cam_out);
+                                const float* visible, float* vis_accum, uint32_t* view_mask, uint32_t slot,
+                                float* cam_out);
 
 /* Adam (8-bit m+v) from dense gradients grads [N, width] (after the
  * cross-GPU all-reduce).  visible may be NULL (no noise); with opacities NULL
@@ -297,19 +299,26 @@ typedef struct vs_peer_set {
   float* transforms[VS_PEER_MAX];   /* the replicas, [N,10] */
   float* sh_coeffs[VS_PEER_MAX];    /* [N,(d+1)^2,3] f32 */
   float* raw_opacities[VS_PEER_MAX];
-  uint32_t row_format;              /* 0 dense rows, 1 compact rows (one view per rank and step) */
-  const float* cams[VS_PEER_MAX];   /* row_format 1: each rank's cam_out of vs_vjp_compact */
+  uint32_t row_format;              /* 0 dense rows, 1 compact rows (vs_vjp_compact) */
+  /* row_format 1: each rank renders `views` views per step; rank r's rows of
+   * slot v are grads[r] + v * N * VS_COMPACT_ROW, its camera cams[r] + 4 v,
+   * and view_masks[r][g] has bit v set when slot v saw splat g */
+  uint32_t views;
+  const float* cams[VS_PEER_MAX];
+  const uint32_t* view_masks[VS_PEER_MAX];
 } vs_peer_set;
 /* The 8-bit-moment Adam of vs_adam_q8_dense for splats [splat_begin,
  * splat_end) only (splat_begin a multiple of 256), with the gradient of each
  * splat summed in rank order over the ranks whose vis > 0 and the noise gated
  * on the summed vis; the moments (mom_*) hold that shard only, and the new
- * parameters go to every rank's replica.  With row_format 1 the ranks'
- * compact rows are summed in shared memory, the SH gradient rebuilt from each
- * rank's colour gradient and camera, with the same sums, bit for bit, as
- * row_format 0 over the dense rows of the same views.  All ranks' gradient rows must be
- * complete (vs_peer_barrier) before the call, and no rank may read its
- * replica until every rank's call has finished (a second barrier). */
+ * parameters go to every rank's replica.  With row_format 1 the compact
+ * rows of every (rank, view) that saw a splat are summed in that order, the SH
+ * gradient rebuilt from each view's colour gradient and camera: bit for bit
+ * the sums of one dense row accumulated by vs_vjp_dense over the same views in
+ * the same order (with one view per rank, the sums of row_format 0).  All
+ * ranks' gradient rows must be complete (vs_peer_barrier) before the call,
+ * and no rank may read its replica until every rank's call has finished (a
+ * second barrier). */
 VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_degree, uint32_t splat_begin,
                                  uint32_t splat_end, const vs_peer_set* peers, vs_q8_tensor mom_t,
                                  vs_q8_tensor mom_sh, vs_q8_tensor mom_o, const vs_q8_cfg* q8);

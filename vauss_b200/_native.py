@@ -62,7 +62,8 @@ class IpcHandle(ctypes.Structure):
 class PeerSet(ctypes.Structure):
     _fields_ = [("world", ctypes.c_uint32), ("rank", ctypes.c_uint32), ("grads", c_vp * PEER_MAX),
                 ("vis", c_vp * PEER_MAX), ("transforms", c_vp * PEER_MAX), ("sh_coeffs", c_vp * PEER_MAX),
-                ("raw_opacities", c_vp * PEER_MAX), ("row_format", ctypes.c_uint32), ("cams", c_vp * PEER_MAX)]
+                ("raw_opacities", c_vp * PEER_MAX), ("row_format", ctypes.c_uint32), ("views", ctypes.c_uint32),
+                ("cams", c_vp * PEER_MAX), ("view_masks", c_vp * PEER_MAX)]
 
 
 COMPACT_ROW = 16  # VS_COMPACT_ROW: floats per splat of vs_vjp_compact
@@ -127,7 +128,7 @@ _SIGS = {
     "vs_vjp_dense": ([c_vp, c_vp, ctypes.POINTER(RenderCfg), ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
                       c_vp, c_vp, c_vp], ctypes.c_int),
     "vs_vjp_compact": ([c_vp, c_vp, ctypes.POINTER(RenderCfg), ctypes.c_uint32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp,
-                        c_vp, c_vp, c_vp, c_vp], ctypes.c_int),
+                        c_vp, c_vp, c_vp, c_vp, ctypes.c_uint32, c_vp], ctypes.c_int),
     "vs_adam_q8_dense": ([c_vp, ctypes.c_uint32, ctypes.c_int32, c_vp, c_vp, c_vp, c_vp, Q8Tensor, Q8Tensor,
                           Q8Tensor, ctypes.POINTER(Q8Cfg), c_vp, c_vp], ctypes.c_int),
     "vs_peer_alloc": ([c_vp, ctypes.c_uint64, ctypes.POINTER(c_vp), ctypes.POINTER(IpcHandle)], ctypes.c_int),

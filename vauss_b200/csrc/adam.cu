@@ -248,12 +248,11 @@ __device__ __forceinline__ uint32_t compact_block(bool flag, uint32_t* list, uin
 // projection culled have no rasterizer row and no `visible` mark, so their
 // gradient rows, refine sums and view counts stay as they are.  The rows with
 // a non-zero rasterizer gradient are compacted per block first, so the VJP
-// runs on whole warps.  kCompact writes VS_COMPACT_ROW floats per splat
-// (transforms gradient, raw-opacity gradient, colour gradient): the view's SH
+// runs on whole warps.  kCompact writes VS_COMPACT_ROW floats per splat into
+// the rows of view slot `slot` (transforms gradient, raw-opacity gradient,
+// colour gradient) and marks the splat's bit in view_mask: the view's SH
 // gradient is that colour gradient times the SH basis of the view direction,
-// which the shard owner rebuilds from the camera position (cam_out); every row
-// must be fresh (one view per step), as the owner's sum takes one term per
-// rank.
+// which the shard owner rebuilds from the camera position (cam_out).
 template <bool kCompact>
 __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, const float* __restrict__ transforms,
                                                         const void* __restrict__ sh, const float* __restrict__ raw_opac,
@@ -263,6 +262,7 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
                                                         float* __restrict__ grads, float* __restrict__ refine,
                                                         const float* __restrict__ visible,
                                                         float* __restrict__ vis_accum, float* __restrict__ cam_out,
+                                                        uint32_t* __restrict__ view_mask, uint32_t slot,
                                                         uint32_t* __restrict__ err) {
   __shared__ uint32_t s_list[256];
   __shared__ uint32_t s_wcnt[8];
@@ -285,8 +285,13 @@ __global__ void __launch_bounds__(256) vjp_dense_kernel(Uniforms u, uint32_t v, 
     if (vis_accum) {
       const float seen = vis_accum[g];
       vis_accum[g] = seen + visible[g];
-      fresh = seen == 0.0f && visible[g] > 0.0f;
-      if (kCompact && seen != 0.0f && visible[g] > 0.0f) atomicOr(err, VS_DERR_STATE);
+      // a compact row is the slot's own: every visible splat's row is fresh
+      fresh = (kCompact || seen == 0.0f) && visible[g] > 0.0f;
+    }
+    if (kCompact && visible[g] > 0.0f) {
+      const uint32_t m = view_mask[g];
+      if (m & (1u << slot)) atomicOr(err, VS_DERR_STATE);  // the slot written twice in a step
+      view_mask[g] = m | (1u << slot);
     }
     const float* rg = v_combined + (size_t)c * 10;
 #pragma unroll
@@ -418,7 +423,12 @@ struct PeerArgs {
   const uint32_t* err;
   uint32_t cta_begin;  // first CTA (256 splats) of the shard
   uint32_t m_off;      // first splat covered by the moment arrays
-  const float* cams[VS_PEER_MAX];  // MODE 3 (compact rows): each rank's camera position
+  // MODE 3 (compact rows): `views` slots per rank, rows of slot v at
+  // grads[r] + v * n_all * VS_COMPACT_ROW, cameras cams[r] + 4 v, masks[r][g]
+  // bit v when slot v saw splat g
+  uint32_t views, n_all;
+  const float* cams[VS_PEER_MAX];
+  const uint32_t* masks[VS_PEER_MAX];
   const float* grads[VS_PEER_MAX];
   const float* vis[VS_PEER_MAX];
   float* t[VS_PEER_MAX];
@@ -736,11 +746,12 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
         }
         s_vmask[tid] = vm;
       } else if (MODE == 3) {
-        // compact rows: the transforms and opacity gradients summed in rank
-        // order, and the SH gradient rebuilt per rank from its colour gradient
-        // and the view direction and basis computed as splat_vjp computes
-        // them (same mean, same camera), each sum from 0 one term per rank:
-        // the sums of the dense exchange, bit for bit
+        // compact rows: over every (rank, view slot) that saw the splat, in
+        // that order, the transforms and opacity gradients summed and the SH
+        // gradient rebuilt from the slot's colour gradient and the view
+        // direction and basis computed as splat_vjp computes them (same
+        // mean, same camera), each sum from 0 one term per view: the sums of
+        // one dense row accumulated over the same views, bit for bit
         float* gs = s_gsh + tid * Q8_GSH_STRIDE;
         for (uint32_t j = 0; j < wsh; ++j) gs[j] = 0.0f;
         uint32_t vm = 0;
@@ -754,23 +765,30 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
                            transforms[(size_t)g * 10 + 2]};
           for (uint32_t r = 0; r < pa.world; ++r) {
             if (!((vm >> r) & 1u)) continue;
-            const float4* row = reinterpret_cast<const float4*>(pa.grads[r] + (size_t)g * VS_COMPACT_ROW);
-            const float4 x0 = row[0], x1 = row[1], x2 = row[2], x3 = row[3];
-            const float* cp = pa.cams[r];
-            const V3 cam = {cp[0], cp[1], cp[2]};
-            gr[0] += x0.x; gr[1] += x0.y; gr[2] += x0.z; gr[3] += x0.w;
-            gr[4] += x1.x; gr[5] += x1.y; gr[6] += x1.z; gr[7] += x1.w;
-            gr[8] += x2.x; gr[9] += x2.y; go += x2.z;
-            const float cv[3] = {x2.w, x3.x, x3.y};
-            const V3 uw = v3sub(mean, cam);
-            const float ulen = sqrtf(v3dot(uw, uw));
-            const V3 dv = v3scale(uw, 1.0f / ulen);
-            sh_basis_all(dv.x, dv.y, dv.z, b);
+            uint32_t slots = pa.masks[r][g];
+            if (pa.views < 32) slots &= (1u << pa.views) - 1u;
+            while (slots) {
+              const uint32_t v = (uint32_t)(__ffs(slots) - 1);
+              slots &= slots - 1u;
+              const float4* row = reinterpret_cast<const float4*>(
+                  pa.grads[r] + ((size_t)v * pa.n_all + g) * VS_COMPACT_ROW);
+              const float4 x0 = row[0], x1 = row[1], x2 = row[2], x3 = row[3];
+              const float* cp = pa.cams[r] + 4u * v;
+              const V3 cam = {cp[0], cp[1], cp[2]};
+              gr[0] += x0.x; gr[1] += x0.y; gr[2] += x0.z; gr[3] += x0.w;
+              gr[4] += x1.x; gr[5] += x1.y; gr[6] += x1.z; gr[7] += x1.w;
+              gr[8] += x2.x; gr[9] += x2.y; go += x2.z;
+              const float cv[3] = {x2.w, x3.x, x3.y};
+              const V3 uw = v3sub(mean, cam);
+              const float ulen = sqrtf(v3dot(uw, uw));
+              const V3 dv = v3scale(uw, 1.0f / ulen);
+              sh_basis_all(dv.x, dv.y, dv.z, b);
 #pragma unroll
-            for (int k = 0; k < 16; ++k) {
-              if (k < nc) {
+              for (int k = 0; k < 16; ++k) {
+                if (k < nc) {
 #pragma unroll
-                for (int q = 0; q < 3; ++q) gs[k * 3 + q] = gs[k * 3 + q] + cv[q] * b[k];
+                  for (int q = 0; q < 3; ++q) gs[k * 3 + q] = gs[k * 3 + q] + cv[q] * b[k];
+                }
               }
             }
           }
@@ -1020,21 +1038,23 @@ VS_API vs_status vs_vjp_dense(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg*
   if (frame->v == 0) return VS_OK;
   vjp_dense_kernel<false><<<vs::div_up(frame->v, 256), 256, 0, ctx->stream>>>(
       u, frame->v, transforms, sh_coeffs, raw_opacities, min_scale, (const uint32_t*)frame->global_from_compact.ptr,
-      v_combined, grads, refine, visible, vis_accum, nullptr, ctx->d_err); ++ctx->launches;
+      v_combined, grads, refine, visible, vis_accum, nullptr, nullptr, 0u, ctx->d_err); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "vjp_dense launch");
 }
 
 VS_API vs_status vs_vjp_compact(vs_ctx* ctx, vs_frame* frame, const vs_render_cfg* cfg, uint32_t num_splats,
                                 const float* transforms, const void* sh_coeffs, const float* raw_opacities,
                                 const float* min_scale, const float* v_combined, float* rows, float* refine,
-                                const float* visible, float* vis_accum, float* cam_out) {
+                                const float* visible, float* vis_accum, uint32_t* view_mask, uint32_t slot,
+                                float* cam_out) {
   if (!ctx) return VS_ERR_INVALID;
   if (!frame || !frame->rendered || !cfg) return vs_fail(ctx, VS_ERR_INVALID, "vjp_compact: missing frame/config");
   if (num_splats != frame->n)
     return vs_fail(ctx, VS_ERR_INVALID, "vjp_compact: %u splats, frame has %u", num_splats, frame->n);
   if (!transforms || !sh_coeffs || !raw_opacities || !rows || !refine || !visible || !vis_accum || !cam_out ||
-      (frame->v && !v_combined))
+      !view_mask || (frame->v && !v_combined))
     return vs_fail(ctx, VS_ERR_INVALID, "vjp_compact: null buffer");
+  if (slot >= 32) return vs_fail(ctx, VS_ERR_INVALID, "vjp_compact: view slot %u (0..31)", slot);
   if ((reinterpret_cast<uintptr_t>(rows) | reinterpret_cast<uintptr_t>(cam_out)) & 15u)
     return vs_fail(ctx, VS_ERR_INVALID, "vjp_compact: rows and cam_out must be 16-byte aligned");
   // with no visible splat no rank reads this rank's rows or camera
@@ -1043,7 +1063,7 @@ VS_API vs_status vs_vjp_compact(vs_ctx* ctx, vs_frame* frame, const vs_render_cf
   u.sh_half = cfg->sh_half;
   vjp_dense_kernel<true><<<vs::div_up(frame->v, 256), 256, 0, ctx->stream>>>(
       u, frame->v, transforms, sh_coeffs, raw_opacities, min_scale, (const uint32_t*)frame->global_from_compact.ptr,
-      v_combined, rows, refine, visible, vis_accum, cam_out, ctx->d_err); ++ctx->launches;
+      v_combined, rows, refine, visible, vis_accum, cam_out, view_mask, slot, ctx->d_err); ++ctx->launches;
   return vs_cuda(ctx, cudaGetLastError(), "vjp_compact launch");
 }
 
@@ -1083,19 +1103,24 @@ VS_API vs_status vs_adam_q8_peer(vs_ctx* ctx, uint32_t num_splats, int32_t sh_de
   if (count_sh >= 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "adam_q8_peer: %llu SH values exceed u32 indexing", (unsigned long long)count_sh);
   if (peers->row_format > 1) return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: row format %u", peers->row_format);
   const bool compact = peers->row_format == 1;
+  if (compact && (peers->views == 0 || peers->views > 32))
+    return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: %u views per rank (1..32)", peers->views);
   PeerArgs pa{};
   pa.world = peers->world;
   pa.rank = peers->rank;
   pa.err = ctx->d_err;
   pa.cta_begin = splat_begin / Q8_SPLATS;
   pa.m_off = splat_begin;
+  pa.views = peers->views;
+  pa.n_all = num_splats;
   for (uint32_t r = 0; r < peers->world; ++r) {
     if (!peers->grads[r] || !peers->vis[r] || !peers->transforms[r] || !peers->sh_coeffs[r] ||
         !peers->raw_opacities[r] || (compact && !peers->cams[r]))
       return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: null buffer of rank %u", r);
-    if (compact && (reinterpret_cast<uintptr_t>(peers->grads[r]) & 15u))
-      return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: compact rows must be 16-byte aligned");
+    if (compact && (!peers->view_masks[r] || (reinterpret_cast<uintptr_t>(peers->grads[r]) & 15u)))
+      return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: compact rows need view masks and 16-byte alignment");
     pa.cams[r] = compact ? peers->cams[r] : nullptr;
+    pa.masks[r] = compact ? peers->view_masks[r] : nullptr;
     if (!q8_aligned(peers->transforms[r], peers->sh_coeffs[r], peers->raw_opacities[r], mom_t, mom_sh, mom_o))
       return vs_fail(ctx, VS_ERR_INVALID, "adam_q8_peer: parameter and code arrays must be 16-byte aligned");
     pa.grads[r] = peers->grads[r];

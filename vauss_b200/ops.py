@@ -334,14 +334,15 @@ def vjp_dense(frame: Frame, cfg: N.RenderCfg, transforms, sh_coeffs, raw_opaciti
 
 
 def vjp_compact(frame: Frame, cfg: N.RenderCfg, transforms, sh_coeffs, raw_opacities, v_combined, rows, refine,
-                cam_out, min_scale=None, visible=None, vis_accum=None):
-    """One view's compact gradient rows [N, 16] (transforms | raw opacity | colour gradient) and the
-    camera position the VJP used (cam_out [4]), for a rank that renders one view per step; the shard
-    owner rebuilds the SH gradient (adam_q8_peer with PeerSet.row_format = 1)."""
+                cam_out, view_mask, slot: int = 0, min_scale=None, visible=None, vis_accum=None):
+    """View `slot`'s compact gradient rows [N, 16] (transforms | raw opacity | colour gradient), its bit
+    in view_mask [N] u32 and the camera position the VJP used (cam_out [4]); the shard owner rebuilds
+    the SH gradient (adam_q8_peer with PeerSet.row_format = 1)."""
     ctx = frame.ctx.bind()
     ctx.check(ctx.lib.vs_vjp_compact(ctx.h, frame.h, ctypes.byref(cfg), transforms.shape[0], _ptr(transforms),
                                      _ptr(sh_coeffs), _ptr(raw_opacities), _ptr(min_scale), _ptr(v_combined),
-                                     _ptr(rows), _ptr(refine), _ptr(visible), _ptr(vis_accum), _ptr(cam_out)))
+                                     _ptr(rows), _ptr(refine), _ptr(visible), _ptr(vis_accum), _ptr(view_mask),
+                                     int(slot), _ptr(cam_out)))
 
 
 def min_scale(transforms: torch.Tensor, view_cams: torch.Tensor, factor: float,

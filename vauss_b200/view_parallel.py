@@ -14,11 +14,12 @@ gradient rows, view counts and parameter replicas live in buffers every rank
 maps over NVLink: after a device barrier each rank runs the 8-bit-moment Adam
 on its shard of the splats only (vs_adam_q8_peer), summing the rows of the
 ranks that saw each splat straight from their memory and storing the new
-parameters into every replica, and a second barrier ends the step.  A rank
-that renders one view per step writes compact rows (vs_vjp_compact: 16
-floats, the SH gradient left as the colour gradient plus the camera position)
-and the owners rebuild the SH gradient, bit for bit as the dense rows hold it;
-with several views per rank the rows are dense.  Without
+parameters into every replica, and a second barrier ends the step.  Each
+view writes compact rows of its own (vs_vjp_compact: 16 floats, the SH
+gradient left as the colour gradient, plus the camera position and the view's
+bit in a per-splat mask) and the owners rebuild the SH gradient; the sums run
+over (rank, view) in order, bit for bit those of one dense row accumulated
+over the same views (`compact_rows=False` keeps dense rows per rank).  Without
 one, the dense gradient and the view counts go through one flat all-reduce
 (`exchange`, injectable so the host logic runs with gloo ranks on the CPU) and
 every rank runs the full replicated Adam.
@@ -36,6 +37,9 @@ from . import _native as N
 from . import ops
 from .peer import PeerGroup
 from .trainer import SceneBatch, Splats, SplatTrainer, TrainConfig, TrainStepStats
+
+
+MAX_VIEW_SLOTS = 32  # compact rows: view slots per rank and step (bits of the per-splat mask)
 
 
 def views_for_rank(num_views: int, rank: int, world: int, step: int, per_rank: int) -> list[int]:
@@ -74,7 +78,7 @@ class ViewParallelTrainer(SplatTrainer):
         super().__init__(config, device, **kw)
         self.exchange = exchange
         self.peer = peer
-        self.compact_rows = compact_rows  # with a peer group and one view per rank and step
+        self.compact_rows = compact_rows  # with a peer group: one compact row slot per view
         self.flat = None
         self.peer_set = None
 
@@ -96,9 +100,10 @@ class ViewParallelTrainer(SplatTrainer):
         width = 10 + nc * 3 + 1
         f32 = torch.float32
         addr_t, addr_sh, addr_o = g.alloc(n * 10, f32), g.alloc(n * nc * 3, f32), g.alloc(n, f32)
-        addr_g = g.alloc(n * width, f32, zero=True)  # dense rows, or compact rows of 16 floats
+        addr_g = g.alloc(n * width, f32, zero=True)  # dense rows, or compact rows of up to 3 views
         addr_v = g.alloc(n, f32, zero=True)
-        addr_c = g.alloc(4, f32, zero=True)  # camera position of the rank's view (compact rows)
+        addr_c = g.alloc(4 * MAX_VIEW_SLOTS, f32, zero=True)  # camera position of each view slot
+        addr_m = g.alloc(n, torch.int32, zero=True)  # view slots that saw each splat (compact rows)
         t = g.local(addr_t, n * 10, f32).view(n, 10)
         sh = g.local(addr_sh, n * nc * 3, f32).view(n, nc, 3)
         o = g.local(addr_o, n, f32)
@@ -107,11 +112,14 @@ class ViewParallelTrainer(SplatTrainer):
         o.copy_(splats.raw_opacities)
         self._grads = g.local(addr_g, n * width, f32).view(n, width)
         self._vis = g.local(addr_v, n, f32)
-        self._cam = g.local(addr_c, 4, f32)
+        self._cams = g.local(addr_c, 4 * MAX_VIEW_SLOTS, f32).view(MAX_VIEW_SLOTS, 4)
+        self._mask = g.local(addr_m, n, torch.int32)
+        self._addr_dense = addr_g
+        self._addr_compact, self._compact_slots = addr_g, (n * width) // (n * N.COMPACT_ROW) if n else 0
         ps = N.PeerSet()
         ps.world, ps.rank = g.world, g.rank
         for r in range(g.world):
-            ps.grads[r], ps.vis[r], ps.cams[r] = addr_g[r], addr_v[r], addr_c[r]
+            ps.grads[r], ps.vis[r], ps.cams[r], ps.view_masks[r] = addr_g[r], addr_v[r], addr_c[r], addr_m[r]
             ps.transforms[r], ps.sh_coeffs[r], ps.raw_opacities[r] = addr_t[r], addr_sh[r], addr_o[r]
         self.peer_set = ps
         self.shard = self.shard_of(n, g.world, g.rank)
@@ -121,6 +129,17 @@ class ViewParallelTrainer(SplatTrainer):
         self.record = None
         self._resident = t.data_ptr()
         return Splats(t, sh, o)
+
+    def _compact_rows(self, views: int, n: int) -> list[torch.Tensor]:
+        """Each view slot's [n, 16] compact rows; the dense-row buffer holds up
+        to 3 slots, more take a peer buffer of their own, allocated by all
+        ranks together the first time a step has that many views."""
+        if views > self._compact_slots:
+            addr = self.peer.alloc(views * n * N.COMPACT_ROW, torch.float32, zero=True)
+            self._addr_compact, self._compact_slots = addr, views
+            self._compact_local = self.peer.local(addr, views * n * N.COMPACT_ROW, torch.float32)
+        base = self._compact_local if self._addr_compact is not self._addr_dense else self._grads.view(-1)
+        return [base[v * n * N.COMPACT_ROW:(v + 1) * n * N.COMPACT_ROW] for v in range(views)]
 
     def step_views(self, batches: Sequence[SceneBatch], splats: Splats, hook=None) -> tuple[Splats, TrainStepStats]:
         """One optimizer step over this rank's views.  ``hook(name)``, when
@@ -140,12 +159,16 @@ class ViewParallelTrainer(SplatTrainer):
         n = splats.num_splats
         width = 10 + splats.sh_coeffs.shape[1] * 3 + 1
         # every rank renders the same number of views per step, so all ranks
-        # agree on the row format
-        compact = peer is not None and self.compact_rows and len(batches) == 1
+        # agree on the row format (and allocate compact slots together)
+        compact = peer is not None and self.compact_rows and 1 <= len(batches) <= MAX_VIEW_SLOTS
         if peer is not None:
-            # rows are overwritten where vis is 0, so only the counts are cleared
+            # rows are overwritten where vis is 0 (or the view's mask bit is
+            # clear), so only the counts and masks are cleared
             grads, vis = self._grads, self._vis
             vis.zero_()
+            if compact:
+                self._mask.zero_()
+                crows = self._compact_rows(len(batches), n)
         else:
             layout = ExchangeLayout(n, width)
             if self.flat is None or self.flat.numel() != layout.size:
@@ -177,7 +200,7 @@ class ViewParallelTrainer(SplatTrainer):
                 dst.copy_(b.img_packed, non_blocking=True)
             gts.append(dst)
             ready.append(self._copy_stream.record_event())
-        for b, gt, ev in zip(batches, gts, ready):
+        for slot, (b, gt, ev) in enumerate(zip(batches, gts, ready)):
             cam = b.camera
             cfg = ops.render_cfg(splats.sh_degree, mip=c.render_mode_mip, background=self.background(),
                                  has_min_scale=splats.min_scale is not None)
@@ -195,8 +218,9 @@ class ViewParallelTrainer(SplatTrainer):
                                    self._buf("v_combined", (max(n, 1), 10), torch.float32))
             mark("raster_bwd")
             if compact:
-                ops.vjp_compact(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, grads,
-                                refine, self._cam, min_scale=splats.min_scale, visible=out.visible, vis_accum=vis)
+                ops.vjp_compact(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc,
+                                crows[slot], refine, self._cams[slot], self._mask, slot, min_scale=splats.min_scale,
+                                visible=out.visible, vis_accum=vis)
             else:
                 ops.vjp_dense(out.frame, cfg, splats.transforms, splats.sh_coeffs, splats.raw_opacities, vc, grads,
                               refine, min_scale=splats.min_scale, visible=out.visible, vis_accum=vis)
@@ -215,7 +239,10 @@ class ViewParallelTrainer(SplatTrainer):
                         noise_scale=c.mean_noise_weight * self.lr_unit() * self.median_scale,
                         noise_limit=self.median_scale, noise_seed=int(self.rng.integers(0, 2 ** 32)))
         if peer is not None:
-            self.peer_set.row_format = 1 if compact else 0
+            ps = self.peer_set
+            ps.row_format, ps.views = (1, len(batches)) if compact else (0, 0)
+            for r in range(peer.world):
+                ps.grads[r] = (self._addr_compact if compact else self._addr_dense)[r]
             peer.barrier()  # every rank's rows and counts are complete
             mark("barrier_rows")
             ops.adam_q8_peer(splats.sh_degree, n, self.shard[0], self.shard[1], self.peer_set, o["t"], o["sh"],
