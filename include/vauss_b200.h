@@ -10,7 +10,9 @@
  *    reference layouts: transforms [N,10] f32 = mean(3), quaternion (w,x,y,z)(4),
  *    log-scale(3); sh_coeffs [N,(d+1)^2,3] f32 or f16; raw_opacities [N] f32;
  *    images [H,W,4] f32 RGBA; ground truth [H,W] u32 packed RGBA8 (r low byte).
- *  - A vs_ctx owns one device, one stream and a grow-only workspace.  A
+ *  - A vs_ctx owns one device, one stream and a grow-only workspace (from the
+ *    device's default stream-ordered memory pool, whose release threshold the
+ *    ctx raises so that this process keeps freed blocks for reuse).  A
  *    vs_frame owns the per-render intermediates (projected splats, the sorted
  *    intersection list, tile ranges) that the backward of that render reads.
  *  - Calls enqueue work on the ctx stream and return without waiting, except

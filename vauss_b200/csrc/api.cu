@@ -100,6 +100,20 @@ VS_API vs_status vs_ctx_create(int device, vs_ctx** out) {
   vs_ctx* ctx = new vs_ctx();
   ctx->device = device;
   vs_status st = set_device(ctx);
+  if (st == VS_OK) {
+    // Workspace grows through cudaMallocAsync from the device's default pool.
+    // With the pool's default release threshold (0) every synchronisation --
+    // one per render, the count readback -- hands freed blocks back to the
+    // driver, and a buffer that outgrows its headroom later maps new memory
+    // in the middle of a step; keeping freed blocks in this process's pool
+    // lets that regrowth reuse them.
+    cudaMemPool_t pool = nullptr;
+    st = vs_cuda(ctx, cudaDeviceGetDefaultMemPool(&pool, device), "cudaDeviceGetDefaultMemPool");
+    uint64_t keep = ~0ull;
+    if (st == VS_OK)
+      st = vs_cuda(ctx, cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep),
+                   "cudaMemPoolSetAttribute");
+  }
   if (st == VS_OK) st = vs_cuda(ctx, cudaMalloc(&ctx->d_err, 4), "cudaMalloc(err word)");
   if (st == VS_OK) st = vs_cuda(ctx, cudaMemset(ctx->d_err, 0, 4), "cudaMemset(err word)");
   if (st == VS_OK) st = vs_cuda(ctx, cudaMallocHost(&ctx->h_pinned, 64), "cudaMallocHost");
