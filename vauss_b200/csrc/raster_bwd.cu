@@ -35,6 +35,15 @@ __device__ __forceinline__ float sqrt_approx(float x) {
   return y;
 }
 
+// The hardware reciprocal (about 1 ulp): it only scales gradient terms, whose
+// sums already run in another order than the oracle's, never a coverage or
+// termination decision.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // Butterfly reduce-scatter of the NG = 10 gradient components over a warp in
 // 12 shuffles (groups of 5 | 3+2 | 2+1 | 1+1 | pair sum).  Afterwards the even
 // lane l holds the warp sum of component reduce10_comp(l) (or nothing, -1).
@@ -200,7 +209,7 @@ __global__ void __launch_bounds__(RB_THREADS) raster_bwd_kernel(
           if (bb.z >= 0.0f) g[5] = fmaf(vis, vr[k], g[5]);
           if (bb.w >= 0.0f) g[6] = fmaf(vis, vg[k], g[6]);
           if (cc.x >= 0.0f) g[7] = fmaf(vis, vb[k], g[7]);
-          const float ra = rcp_rn(1.0f - alpha);  // 1 - alpha in [1e-3, 1]
+          const float ra = rcp_approx(1.0f - alpha);  // 1 - alpha in [1e-3, 1]
           const float dot =
               fmaf(fmaf(st[k], cr, -sr[k]), vr[k], fmaf(fmaf(st[k], cg, -sg[k]), vg[k], fmaf(st[k], cb, -sb[k]) * vb[k])) * ra;
           const float v_alpha = fmaf(vt[k], ra, dot);
