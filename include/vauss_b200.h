@@ -296,7 +296,7 @@ VS_API vs_status vs_ctx_check(vs_ctx* ctx);
 typedef struct vs_peer_set {
   uint32_t world, rank;
   const float* grads[VS_PEER_MAX];  /* row_format 0: [N, width] dense gradient rows of each rank;
-                                       row_format 1: [N, VS_COMPACT_ROW] rows of vs_vjp_compact */
+                                       row_format 1: [views][N][VS_COMPACT_ROW] rows of vs_vjp_compact */
   const float* vis[VS_PEER_MAX];    /* [N] views of each rank that saw the splat (rows with 0 are not read) */
   float* transforms[VS_PEER_MAX];   /* the replicas, [N,10] */
   float* sh_coeffs[VS_PEER_MAX];    /* [N,(d+1)^2,3] f32 */
