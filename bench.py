@@ -49,6 +49,12 @@ intersect + radix sort + tile ranges.
 --optimizer reference (configs[2], one GPU) steps the reference's optimizer
 storage instead of the 8-bit m+v Adam.
 
+--emulate-peers W (one GPU) times the view-parallel update of configs[2]
+with W ranks emulated on one device (each rank's compact rows written from a
+render of its own view, every shard updated in turn with all ranks' buffers
+as peers): the sharded optimizer kernel's own cost, without NVLink, and a
+one-GPU command under which it can be profiled.
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--config 1|2|3|4]
 """
 from __future__ import annotations
@@ -88,6 +94,8 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-check", action="store_true", help="N > 1: skip the peer vs all-reduce exchange check")
     p.add_argument("--no-config3", action="store_true", help="skip the configs[3] companion leg")
+    p.add_argument("--emulate-peers", type=int, default=0, metavar="W",
+                   help="time the sharded compact-row update of configs[2] with W ranks emulated on one GPU")
     p.add_argument("--rows", default="compact", choices=["compact", "dense"],
                    help="N > 1: gradient rows of the peer exchange with one view per rank (compact 64-byte rows "
                         "with the SH gradient rebuilt by the owner, or dense rows)")
@@ -927,6 +935,92 @@ def run_reference(args):
     print(json.dumps(out), flush=True)
 
 
+def run_peer_emulation(args):
+    """``--emulate-peers W``: the view-parallel update of configs[2] with W
+    ranks emulated on one GPU, so that the sharded optimizer kernel can be
+    timed and profiled on one device.  Every emulated rank renders its own
+    view, runs the loss and the rasterizer backward and writes its compact
+    rows, view mask and camera into buffers of its own; then each rank's
+    shard is updated (vs_adam_q8_peer, row_format 1) with all ranks' buffers
+    as its peers, one launch after another, and the update of every shard is
+    timed with CUDA events over K steps.  No NVLink is crossed: the figure is
+    the kernel's own cost, the peer reads and replica stores landing in this
+    GPU's memory."""
+    import torch
+    from vauss_b200 import _native as N, ops, scenes
+    from vauss_b200.view_parallel import ViewParallelTrainer
+    dev = torch.device("cuda", 0)
+    world = args.emulate_peers
+    if not 1 <= world <= N.PEER_MAX:
+        raise SystemExit(f"--emulate-peers takes 1..{N.PEER_MAX} ranks")
+    sp, tgt, cams = make_workload(args.splats, 2)
+    n, deg, nc = sp.n, 3, 16
+    params = [torch.from_numpy(np.ascontiguousarray(x)).to(dev) for x in (sp.transforms, sp.sh, sp.raw_opac)]
+    tsp = [torch.from_numpy(np.ascontiguousarray(x)).to(dev) for x in (tgt.transforms, tgt.sh, tgt.raw_opac)]
+    cfg = ops.render_cfg(deg, mip=True)
+    rows = [torch.zeros(n * N.COMPACT_ROW, device=dev) for _ in range(world)]
+    vis = [torch.zeros(n, device=dev) for _ in range(world)]
+    refine = torch.zeros(n, device=dev)
+    camb = [torch.zeros(4, device=dev) for _ in range(world)]
+    masks = [torch.zeros(n, dtype=torch.int32, device=dev) for _ in range(world)]
+    visible, isect = 0, 0
+    for r in range(world):
+        cam = cams[(r * N_TARGETS) % N_VIEWS]
+        gt_img = ops.render(cam, cfg, *tsp).out_img[..., :3].clamp(0, 1).cpu().numpy()
+        gt = torch.from_numpy(scenes.pack_rgba8(gt_img).view(np.int32)).to(dev)
+        out = ops.render(cam, cfg, *params)
+        loss = ops.image_loss(out.out_img, gt, 0.8, 0.2)
+        vc = ops.rasterize_bwd(out.frame, out.out_img, loss.dl_dpred)
+        ops.vjp_compact(out.frame, cfg, *params, vc, rows[r], refine, camb[r], masks[r], 0, visible=out.visible,
+                        vis_accum=vis[r])
+        visible += out.num_visible
+        isect += out.num_intersections
+    del tsp
+    reps = [[x.clone() for x in params] for _ in range(world)]
+    ps = N.PeerSet()
+    ps.world, ps.row_format, ps.views = world, 1, 1
+    for r in range(world):
+        ps.grads[r], ps.vis[r], ps.cams[r], ps.view_masks[r] = (rows[r].data_ptr(), vis[r].data_ptr(),
+                                                                camb[r].data_ptr(), masks[r].data_ptr())
+        ps.transforms[r], ps.sh_coeffs[r], ps.raw_opacities[r] = (x.data_ptr() for x in reps[r])
+    shards = [ViewParallelTrainer.shard_of(n, world, r) for r in range(world)]
+    moms = [dict(t=ops.Q8Moments((e - b) * 10, dev), sh=ops.Q8Moments((e - b) * nc * 3, dev),
+                 o=ops.Q8Moments(e - b, dev)) for b, e in shards]
+    lr_t = np.float32([1.6e-4] * 3 + [1e-3] * 4 + [5e-3] * 3)
+    ctx = ops.context(dev)
+
+    def update_all(step, ev=None):
+        q8 = ops.q8_cfg(step + 1, lr_t, 2.5e-3, 1.25e-4, 2.5e-2)
+        for r, (b, e) in enumerate(shards):
+            ps.rank = r
+            if ev is not None:
+                ev[r][0].record()
+            ops.adam_q8_peer(deg, n, b, e, ps, moms[r]["t"], moms[r]["sh"], moms[r]["o"], q8, device=dev)
+            if ev is not None:
+                ev[r][1].record()
+
+    for k in range(args.warmup):
+        update_all(k)
+    ms = [0.0] * world
+    for k in range(args.steps):
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(world)]
+        update_all(args.warmup + k, ev)
+        torch.cuda.synchronize()
+        for r in range(world):
+            ms[r] += ev[r][0].elapsed_time(ev[r][1])
+    if ctx.lib.vs_ctx_check(ctx.h) != 0:
+        raise SystemExit(ctx.lib.vs_ctx_last_error(ctx.h).decode())
+    per = [m / args.steps for m in ms]
+    out = {"metric": "sharded 8-bit-moment update from compact rows, ranks emulated on one GPU",
+           "value": round(sum(per), 4), "unit": "ms per step (all shards)", "n_gpus": 1, "steps": args.steps,
+           "warmup": args.warmup, "higher_is_better": False, "emulated_ranks": world,
+           "ms_per_shard": [round(x, 4) for x in per], "splats": n, "visible_per_view": round(visible / world),
+           "intersections_per_view": round(isect / world), "data": "synthetic",
+           "config": {"workload": f"configs[2] step's update, {world} ranks emulated on one GPU (no NVLink)",
+                      "kernel": "q8_kernel<3> (vs_adam_q8_peer, row_format 1)"}}
+    print(json.dumps(out), flush=True)
+
+
 def run_microbench(args):
     """BASELINE.json configs[1], the single-view render forward + backward
     microbench: 1M SH-3 splats (means U[-3,3]^3, log-scales N(-4.5, 0.6),
@@ -1205,6 +1299,8 @@ def main():
         run_microbench(args)
     elif args.config == 4:
         run_sort_stress(args)
+    elif args.emulate_peers:
+        run_peer_emulation(args)
     else:
         run_ours(args)
 
