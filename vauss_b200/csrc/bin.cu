@@ -17,8 +17,9 @@ using namespace vs;
 
 constexpr uint32_t BIN_BLOCK = 256;
 
-// Keys are the depth bits less the smallest visible depth's bits (depth >=
-// 0.01, so the bits order like the depths): the same order in fewer key bits.
+// The depth-sort input when every visible depth is equal (no key bits, so no
+// radix pass writes the order): ids = 0..v-1, keys the depth bits less the
+// smallest.  Otherwise the sort's first pass reads the depths itself.
 __global__ void depth_keys_kernel(const float* __restrict__ depths, uint32_t v, uint32_t lo, uint32_t* __restrict__ keys,
                                   uint32_t* __restrict__ ids) {
   const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -196,18 +197,26 @@ vs_status launch_bin(vs_ctx* ctx, vs_frame* f) {
                    f->depth_hi, v);
   const uint32_t span = f->depth_hi - f->depth_lo;
   const uint32_t depth_bits = span ? 32u - (uint32_t)__builtin_clz(span) : 0u;
-  // the ids are sorted into the frame's depth_order: the keys start in the
-  // buffer pair from which the sort's last pass writes there
   uint32_t* order = (uint32_t*)f->depth_order.ptr;
-  const bool odd = radix_sort_passes(depth_bits) & 1u;
-  uint32_t* kin = odd ? k1 : k0;
-  uint32_t* vin = odd ? v1 : order;
-  depth_keys_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const float*)f->depths.ptr, v, f->depth_lo, kin, vin); ++ctx->launches;
+  const uint32_t* tile_counts = (const uint32_t*)f->tile_counts.ptr;
+  uint32_t* cum;  // the tile counts in depth order, then their inclusive scan: the emission offsets
+  if (depth_bits == 0) {
+    // every depth equal: the depth order is the compact order
+    depth_keys_kernel<<<blocks_v, BIN_BLOCK, 0, ctx->stream>>>((const float*)f->depths.ptr, v, f->depth_lo, k0, order); ++ctx->launches;
+    cum = k1;
+    VS_TRY(scan_gather_inclusive_u32(ctx, cum, tile_counts, order, v));
+  } else {
+    // The first pass reads the depth bits less the smallest (the same order in
+    // fewer key bits) with the compact ids as values; the last pass writes
+    // the ids into depth_order and, beside each, its tile count into v0.  The
+    // buffer pairs are chosen so that the last pass writes (k0, depth_order).
+    const bool odd = radix_sort_passes(depth_bits) & 1u;
+    VS_TRY(radix_sort_from(ctx, (const uint32_t*)f->depths.ptr, nullptr, f->depth_lo, odd ? k0 : k1,
+                           odd ? order : v1, odd ? k1 : k0, odd ? v1 : order, v, depth_bits, tile_counts, v0));
+    cum = v0;
+    VS_TRY(scan_inclusive_u32(ctx, cum, v, nullptr));
+  }
   bool alt = false;
-  VS_TRY(radix_sort_pairs(ctx, kin, vin, odd ? k0 : k1, odd ? order : v1, v, depth_bits, &alt));
-  // tile counts in depth order, inclusive scan -> emission offsets
-  uint32_t* cum = k1;  // the sorted keys are in k0
-  VS_TRY(scan_gather_inclusive_u32(ctx, cum, (const uint32_t*)f->tile_counts.ptr, order, v));
   VS_TRY(vs_ensure(ctx, f->isect_tile, (size_t)(I + 1) * 4));
   VS_TRY(vs_ensure(ctx, f->isect_compact, (size_t)(I + 1) * 4));
   if (I == 0) return VS_OK;

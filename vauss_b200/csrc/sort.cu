@@ -34,7 +34,7 @@ constexpr uint32_t MAX_DIGIT_BITS = 9;
 template <uint32_t RB>
 __global__ void __launch_bounds__(SORT_THREADS) hist_kernel(const uint32_t* __restrict__ keys, uint32_t count,
                                                             uint32_t shift, uint32_t mask, uint32_t tiles,
-                                                            uint32_t* __restrict__ hist) {
+                                                            uint32_t* __restrict__ hist, uint32_t sub = 0u) {
   constexpr uint32_t R = 1u << RB;
   __shared__ uint32_t s_hist[R];
   const uint32_t tid = threadIdx.x;
@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(SORT_THREADS) hist_kernel(const uint32_t* __re
     const bool valid = i < count;
     // plain shared-memory atomics: cheaper on sm_100 than grouping equal
     // digits with match_any first
-    if (valid) atomicAdd(&s_hist[(keys[i] >> shift) & mask], 1u);
+    if (valid) atomicAdd(&s_hist[((keys[i] - sub) >> shift) & mask], 1u);
   }
   __syncthreads();
   // the table holds the pass's mask + 1 digits only
@@ -58,7 +58,10 @@ template <uint32_t RB>
 __global__ void __launch_bounds__(SORT_THREADS) scatter_kernel(
     const uint32_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in, uint32_t* __restrict__ keys_out,
     uint32_t* __restrict__ vals_out, uint32_t count, uint32_t shift, uint32_t mask, uint32_t tiles,
-    const uint32_t* __restrict__ offsets /* exclusive-scanned hist, digit-major */) {
+    const uint32_t* __restrict__ offsets /* exclusive-scanned hist, digit-major */,
+    // optional: keys_in - sub are the keys; vals_in NULL gives the values
+    // 0..count-1; with gout, gout[out] = gsrc[value] beside every output
+    uint32_t sub = 0u, const uint32_t* __restrict__ gsrc = nullptr, uint32_t* __restrict__ gout = nullptr) {
   constexpr uint32_t R = 1u << RB;
   constexpr uint32_t DPT = R / SORT_THREADS;  // digits per thread, consecutive
   static_assert(DPT >= 1 && DPT * SORT_THREADS == R, "digit ownership");
@@ -84,8 +87,8 @@ __global__ void __launch_bounds__(SORT_THREADS) scatter_kernel(
   for (uint32_t r = 0; r < ITEMS; ++r) {
     const uint32_t i = base + r * 32 + lane;
     const bool valid = i < count;
-    k[r] = valid ? keys_in[i] : 0u;
-    v[r] = valid ? vals_in[i] : 0u;
+    k[r] = valid ? keys_in[i] - sub : 0u;
+    v[r] = valid ? (vals_in ? vals_in[i] : i) : 0u;
     d[r] = valid ? ((k[r] >> shift) & mask) : R;
   }
 #pragma unroll
@@ -169,7 +172,9 @@ __global__ void __launch_bounds__(SORT_THREADS) scatter_kernel(
     const uint32_t dd = (key >> shift) & mask;
     const uint32_t out = s_goff[dd] + (p - s_dstart[dd]);
     keys_out[out] = key;
-    vals_out[out] = s_vals[p];
+    const uint32_t val = s_vals[p];
+    vals_out[out] = val;
+    if (gout) gout[out] = gsrc[val];
   }
 }
 
@@ -409,10 +414,10 @@ vs_status scan_gather_inclusive_u32(vs_ctx* ctx, uint32_t* out, const uint32_t* 
 
 uint32_t radix_sort_passes(uint32_t key_bits) { return div_up(key_bits, MAX_DIGIT_BITS); }
 
-vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
-                           uint32_t count, uint32_t key_bits, bool* result_in_alt) {
-  *result_in_alt = false;
-  if (count <= 1 || key_bits == 0) return VS_OK;
+vs_status radix_sort_from(vs_ctx* ctx, const uint32_t* keys_in, const uint32_t* vals_in, uint32_t key_sub,
+                          uint32_t* a_keys, uint32_t* a_vals, uint32_t* b_keys, uint32_t* b_vals, uint32_t count,
+                          uint32_t key_bits, const uint32_t* gather_src, uint32_t* gather_out) {
+  if (count == 0 || key_bits == 0) return VS_OK;
   const uint32_t tiles = div_up(count, SORT_TILE);
   const uint32_t passes = radix_sort_passes(key_bits);
   const uint32_t wide = key_bits / passes + (key_bits % passes ? 1u : 0u);  // widest digit
@@ -420,29 +425,51 @@ vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t
   if (hist_n > 0xffffffffull) return vs_fail(ctx, VS_ERR_CAPACITY, "radix sort: %u keys exceed the histogram", count);
   VS_TRY(vs_ensure(ctx, ctx->sort_hist, hist_n * sizeof(uint32_t)));
   uint32_t* hist = (uint32_t*)ctx->sort_hist.ptr;
-  uint32_t *kin = keys, *vin = vals, *kout = keys_alt, *vout = vals_alt;
+  const uint32_t* kin = keys_in;
+  const uint32_t* vin = vals_in;
+  uint32_t *kout = a_keys, *vout = a_vals;
   uint32_t shift = 0;
   for (uint32_t p = 0; p < passes; ++p) {
     // the first key_bits % passes passes take one bit more than the rest
     const uint32_t bits = key_bits / passes + (p < key_bits % passes ? 1u : 0u);
     const uint32_t mask = (1u << bits) - 1u;
+    const uint32_t sub = p == 0 ? key_sub : 0u;
+    const bool last = p + 1 == passes;
+    const uint32_t* gs = last ? gather_src : nullptr;
+    uint32_t* go = last ? gather_out : nullptr;
     // the table is (mask + 1) x tiles words, within the hist_n allocated above
     if (bits > 8) {
-      hist_kernel<9><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
+      hist_kernel<9><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist, sub);
+      ++ctx->launches;
       VS_TRY(scan_impl(ctx, hist, (mask + 1u) * tiles, nullptr, false));
-      scatter_kernel<9><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist);
+      scatter_kernel<9><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles,
+                                                                 hist, sub, gs, go);
     } else {
-      hist_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist); ++ctx->launches;
+      hist_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, count, shift, mask, tiles, hist, sub);
+      ++ctx->launches;
       VS_TRY(scan_impl(ctx, hist, (mask + 1u) * tiles, nullptr, false));
-      scatter_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles, hist);
+      scatter_kernel<8><<<tiles, SORT_THREADS, 0, ctx->stream>>>(kin, vin, kout, vout, count, shift, mask, tiles,
+                                                                 hist, sub, gs, go);
     }
     ++ctx->launches;
     VS_CUDA(ctx, cudaGetLastError());
-    uint32_t* t = kin; kin = kout; kout = t;
-    t = vin; vin = vout; vout = t;
-    *result_in_alt = !*result_in_alt;
+    kin = kout;
+    vin = vout;
+    const bool to_b = kout == a_keys;
+    kout = to_b ? b_keys : a_keys;
+    vout = to_b ? b_vals : a_vals;
     shift += bits;
   }
+  return VS_OK;
+}
+
+vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
+                           uint32_t count, uint32_t key_bits, bool* result_in_alt) {
+  *result_in_alt = false;
+  if (count <= 1 || key_bits == 0) return VS_OK;
+  // pass 0 reads (keys, vals) and writes the alternates, pass 1 writes back, ...
+  VS_TRY(radix_sort_from(ctx, keys, vals, 0u, keys_alt, vals_alt, keys, vals, count, key_bits, nullptr, nullptr));
+  *result_in_alt = (radix_sort_passes(key_bits) & 1u) != 0;
   return VS_OK;
 }
 

@@ -68,6 +68,15 @@ vs_status launch_project(vs_ctx* ctx, vs_frame* f, const float* transforms, cons
 // passes of at most 9 bits; the result is in keys_alt/vals_alt after an odd
 // number of passes (*result_in_alt), else in keys/vals.
 uint32_t radix_sort_passes(uint32_t key_bits);
+// The same sort with the input read in place: pass 0 reads keys_in[i] -
+// key_sub and vals_in[i] (i when vals_in is NULL) and writes (a_keys,
+// a_vals), every later pass reads what the previous one wrote and writes the
+// other pair, so the result is in (a_*) after an odd number of passes, else
+// in (b_*); with gather_out the last pass also writes gather_out[i] =
+// gather_src[value i].  Nothing is written when key_bits or count is 0.
+vs_status radix_sort_from(vs_ctx* ctx, const uint32_t* keys_in, const uint32_t* vals_in, uint32_t key_sub,
+                          uint32_t* a_keys, uint32_t* a_vals, uint32_t* b_keys, uint32_t* b_vals, uint32_t count,
+                          uint32_t key_bits, const uint32_t* gather_src, uint32_t* gather_out);
 vs_status radix_sort_pairs(vs_ctx* ctx, uint32_t* keys, uint32_t* vals, uint32_t* keys_alt, uint32_t* vals_alt,
                            uint32_t count, uint32_t key_bits, bool* result_in_alt);
 vs_status scan_inclusive_u32(vs_ctx* ctx, uint32_t* data, uint32_t count, uint64_t* total_dev);
