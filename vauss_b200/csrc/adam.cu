@@ -875,8 +875,14 @@ __global__ void __launch_bounds__(Q8_SPLATS, 4) q8_kernel(
       q8_block<MODE, 1, 2>(lane, 0, splats_here, raw_opac, mo, (size_t)base, SALT_O, a, sm, grow, width, pa);
     }
   }
-  // Peer stores complete before the barrier that follows this kernel.
-  if (kPeer) __threadfence_system();
+  // Peer stores complete before the barrier that follows this kernel: the
+  // block barrier orders every thread's stores before thread 0's system-scope
+  // fence, which releases them all (one fence per CTA instead of one per warp
+  // waiting at its exit).
+  if (kPeer) {
+    __syncthreads();
+    if (tid == 0) __threadfence_system();
+  }
 }
 
 PeerArgs single_rank() {
